@@ -1,0 +1,76 @@
+// Shared device helpers and host-side status plumbing for the bee_b200 kernels.
+//
+// Conventions mirror the reference's int-returning kernel bridge
+// (Bee/CUDA/Ops/OpsBridge.hpp:22-43): every entry point returns a plain int,
+// 0 on success, otherwise a cudaError_t value.  Argument problems detected on
+// the host return cudaErrorInvalidValue (1) and leave a readable message in a
+// thread-local buffer (bee_b200_last_error()).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/bee_b200.h"
+
+namespace bee_b200 {
+
+// dtype codes: identical to bee::DType (Bee/Tensor/Core/DType.hpp:17-32).
+enum DT : int {
+    DT_BOOL = 0, DT_U8 = 1, DT_I32 = 2, DT_I64 = 3, DT_F32 = 4, DT_F64 = 5,
+    DT_I8 = 6, DT_F16 = 7, DT_BF16 = 8,
+};
+
+// op codes: identical to bee::cuda::BinaryOp / UnaryOp / ReduceOp
+// (Bee/CUDA/Api.hpp:77-100).
+enum BinOp : int { OP_ADD = 0, OP_SUB = 1, OP_MUL = 2, OP_DIV = 3 };
+enum UnOp : int { OP_NEG = 0, OP_ABS = 1, OP_SQRT = 2, OP_EXP = 3, OP_LOG = 4 };
+enum RedOp : int { RED_SUM = 0, RED_MIN = 1, RED_MAX = 2, RED_PROD = 3 };
+
+// Records a message for bee_b200_last_error() and returns `code`.
+int fail(int code, const char* fmt, ...);
+// Clears the thread-local message; returns 0.
+int ok();
+// Converts the pending launch error (if any) into a status.
+int launch_status(const char* what);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Number of SMs of the current device (cached per device ordinal).
+int sm_count();
+
+inline cudaStream_t as_stream(bee_b200_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ---------------------------------------------------------------- device side
+
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Streaming (evict-first) 128-bit global load / store: each input byte of the
+// memory-bound kernels is touched exactly once, so keep it out of L1 and mark
+// it first-to-evict in L2.
+__device__ __forceinline__ float4 ld_stream(const float4* p) { return __ldcs(p); }
+__device__ __forceinline__ void st_stream(float4* p, float4 v) { __stcs(p, v); }
+__device__ __forceinline__ uint4 ld_stream_u4(const uint4* p) { return __ldcs(p); }
+__device__ __forceinline__ void st_stream_u4(uint4* p, uint4 v) { __stcs(p, v); }
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+// Packs two floats into a bf16x2 word with round-to-nearest-even (cvt.rn.bf16x2.f32).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+}  // namespace bee_b200

@@ -1,0 +1,303 @@
+// Global and per-axis reductions (HBM-bound).
+//
+// Replaces K7/K8 of the reference (Bee/CUDA/Ops/Reduce.cu:129-183).  The
+// reference's axis reduce gives one thread a whole row, so for a row reduce
+// neighbouring threads read addresses a row apart; here a row is owned by a
+// CTA (long rows) or a warp (short rows) that streams it with coalesced
+// 16-byte loads and combines with warp shuffles.  The global reduce is one
+// launch: every CTA reduces a grid-stride slice into a partial, and the last
+// CTA to finish (atomic ticket) folds the partials in index order, so float
+// results do not depend on scheduling.
+//
+// Accumulation semantics follow the reference's OpReduce* functors
+// (Bee/Tensor/Cpu/ReduceCpu.hpp:177-290): accumulate in the element type
+// (integer sums and products wrap), min/max by comparison, identities
+// 0 / 1 / numeric max / numeric lowest.
+#include <cfloat>
+#include <climits>
+
+#include "common.cuh"
+
+namespace bee_b200 {
+
+template <typename T> struct Lim;
+template <> struct Lim<uint8_t> { static __device__ uint8_t lo() { return 0; } static __device__ uint8_t hi() { return 255; } };
+template <> struct Lim<int32_t> { static __device__ int32_t lo() { return INT_MIN; } static __device__ int32_t hi() { return INT_MAX; } };
+template <> struct Lim<int64_t> { static __device__ int64_t lo() { return LLONG_MIN; } static __device__ int64_t hi() { return LLONG_MAX; } };
+template <> struct Lim<float> { static __device__ float lo() { return -FLT_MAX; } static __device__ float hi() { return FLT_MAX; } };
+template <> struct Lim<double> { static __device__ double lo() { return -DBL_MAX; } static __device__ double hi() { return DBL_MAX; } };
+
+// Integer sum/prod go through the unsigned type so that wrap-around is
+// defined behaviour (two's complement, identical bits to the reference).
+template <typename T> struct Wrap { using U = T; };
+template <> struct Wrap<int32_t> { using U = uint32_t; };
+template <> struct Wrap<int64_t> { using U = uint64_t; };
+
+template <int OP, typename T> struct Red {
+    static __device__ __forceinline__ T identity() {
+        if constexpr (OP == RED_SUM) return T(0);
+        else if constexpr (OP == RED_PROD) return T(1);
+        else if constexpr (OP == RED_MIN) return Lim<T>::hi();
+        else return Lim<T>::lo();
+    }
+    static __device__ __forceinline__ T apply(T a, T b) {
+        using U = typename Wrap<T>::U;
+        if constexpr (OP == RED_SUM) return static_cast<T>(static_cast<U>(a) + static_cast<U>(b));
+        else if constexpr (OP == RED_PROD) return static_cast<T>(static_cast<U>(a) * static_cast<U>(b));
+        else if constexpr (OP == RED_MIN) return b < a ? b : a;
+        else return b > a ? b : a;
+    }
+};
+
+template <int OP, typename T> __device__ __forceinline__ T warp_reduce(T v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = Red<OP, T>::apply(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide reduce; the result is valid in every thread.  `smem` holds
+// blockDim.x / 32 entries.
+template <int OP, typename T> __device__ __forceinline__ T block_reduce(T v, T* smem) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    v = warp_reduce<OP>(v);
+    __syncthreads();
+    if (lane == 0) smem[warp] = v;
+    __syncthreads();
+    T r = Red<OP, T>::identity();
+    for (int w = 0; w < nwarps; ++w) r = Red<OP, T>::apply(r, smem[w]);
+    return r;
+}
+
+template <typename T> union V16 {
+    uint4 v;
+    T s[16 / sizeof(T)];
+};
+
+// Folds a 16-byte vector into `acc` lane by lane (fixed order).
+template <int OP, typename T> __device__ __forceinline__ T fold(T acc, uint4 raw) {
+    V16<T> x;
+    x.v = raw;
+#pragma unroll
+    for (int k = 0; k < int(16 / sizeof(T)); ++k) acc = Red<OP, T>::apply(acc, x.s[k]);
+    return acc;
+}
+
+// Reduces src[lo, hi) cooperatively by `nthr` threads (index `tid`); the
+// 16-byte vector path is used when src+lo is 16-byte aligned.
+template <int OP, typename T>
+__device__ __forceinline__ T strided_reduce(const T* __restrict__ src, size_t lo, size_t hi, size_t tid, size_t nthr) {
+    constexpr size_t E = 16 / sizeof(T);
+    T acc = Red<OP, T>::identity();
+    const T* base = src + lo;
+    const size_t len = hi - lo;
+    size_t head = 0;
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
+        const size_t nvec = len / E;
+        const uint4* v = reinterpret_cast<const uint4*>(base);
+        size_t i = tid;
+        constexpr int U = 4;
+        for (; i + (U - 1) * nthr < nvec; i += U * nthr) {
+            uint4 r[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) r[u] = ld_stream_u4(v + i + u * nthr);
+#pragma unroll
+            for (int u = 0; u < U; ++u) acc = fold<OP>(acc, r[u]);
+        }
+        for (; i < nvec; i += nthr) acc = fold<OP>(acc, ld_stream_u4(v + i));
+        head = nvec * E;
+    }
+    for (size_t j = head + tid; j < len; j += nthr) acc = Red<OP, T>::apply(acc, base[j]);
+    return acc;
+}
+
+// ---------------------------------------------------------------- global
+
+struct GlobalScratch {
+    unsigned int ticket;  // number of CTAs that have published their partial
+    unsigned int pad[63];
+    // followed by gridDim.x partials of sizeof(T), 256-byte aligned
+};
+
+template <int OP, typename T>
+__global__ void __launch_bounds__(512) reduce_global_kernel(const T* __restrict__ src, T* __restrict__ dst, size_t n,
+                                                            GlobalScratch* scratch) {
+    __shared__ T smem[32];
+    __shared__ bool last;
+    T* partials = reinterpret_cast<T*>(scratch + 1);
+    const size_t nthr = static_cast<size_t>(gridDim.x) * blockDim.x;
+    // CTA b owns the contiguous chunk [b*chunk, (b+1)*chunk) so that the
+    // partials are in element order; chunks are multiples of 16 elements.
+    const size_t chunk = ((n + gridDim.x - 1) / gridDim.x + 15) & ~size_t(15);
+    const size_t lo = min(n, static_cast<size_t>(blockIdx.x) * chunk);
+    const size_t hi = min(n, lo + chunk);
+    (void)nthr;
+    T v = strided_reduce<OP>(src, lo, hi, threadIdx.x, blockDim.x);
+    v = block_reduce<OP>(v, smem);
+    if (threadIdx.x == 0) {
+        partials[blockIdx.x] = v;
+        __threadfence();
+        unsigned int t = atomicAdd(&scratch->ticket, 1u);
+        last = (t == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // Last CTA: fold the partials in index order (thread-strided, then the
+    // block reduce), then re-arm the ticket for the next call.
+    T r = Red<OP, T>::identity();
+    for (unsigned i = threadIdx.x; i < gridDim.x; i += blockDim.x)
+        r = Red<OP, T>::apply(r, *reinterpret_cast<volatile T*>(partials + i));
+    r = block_reduce<OP>(r, smem);
+    if (threadIdx.x == 0) {
+        *dst = r;
+        scratch->ticket = 0;
+    }
+}
+
+// ---------------------------------------------------------------- axis
+
+// One CTA per row of length `axis` (inner == 1).
+template <int OP, typename T>
+__global__ void __launch_bounds__(512) reduce_rows_cta_kernel(const T* __restrict__ src, T* __restrict__ dst,
+                                                              size_t rows, size_t axis) {
+    __shared__ T smem[32];
+    for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        T v = strided_reduce<OP>(src + r * axis, 0, axis, threadIdx.x, blockDim.x);
+        v = block_reduce<OP>(v, smem);
+        if (threadIdx.x == 0) dst[r] = v;
+    }
+}
+
+// One warp per row (short rows, inner == 1).
+template <int OP, typename T>
+__global__ void __launch_bounds__(256) reduce_rows_warp_kernel(const T* __restrict__ src, T* __restrict__ dst,
+                                                               size_t rows, size_t axis) {
+    const size_t warps = static_cast<size_t>(gridDim.x) * (blockDim.x >> 5);
+    const int lane = threadIdx.x & 31;
+    for (size_t r = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+        T v = strided_reduce<OP>(src + r * axis, 0, axis, lane, 32);
+        v = warp_reduce<OP>(v);
+        if (lane == 0) dst[r] = v;
+    }
+}
+
+// [outer, axis, inner] with inner > 1: one thread per output, neighbouring
+// threads read neighbouring inner elements (coalesced), walking the axis.
+template <int OP, typename T>
+__global__ void __launch_bounds__(256) reduce_inner_kernel(const T* __restrict__ src, T* __restrict__ dst,
+                                                           size_t outer, size_t axis, size_t inner) {
+    const size_t total = outer * inner;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+        const size_t o = idx / inner, i = idx - o * inner;
+        const T* p = src + o * axis * inner + i;
+        T acc = Red<OP, T>::identity();
+        for (size_t k = 0; k < axis; ++k) acc = Red<OP, T>::apply(acc, p[k * inner]);
+        dst[idx] = acc;
+    }
+}
+
+template <int OP, typename T>
+static int run_global(const void* src, void* dst, size_t n, cudaStream_t st) {
+    unsigned grid = static_cast<unsigned>(sm_count()) * 2;
+    const size_t per_cta = 512 * (16 / sizeof(T)) * 4;  // one unrolled sweep of a 512-thread CTA
+    size_t need = (n + per_cta - 1) / per_cta;
+    if (need < grid) grid = static_cast<unsigned>(need < 1 ? 1 : need);
+    const size_t bytes = sizeof(GlobalScratch) + static_cast<size_t>(grid) * sizeof(T);
+    void* scratch = nullptr;
+    cudaError_t e = cudaMallocAsync(&scratch, bytes, st);
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "reduce_global: scratch allocation: %s", cudaGetErrorString(e));
+    e = cudaMemsetAsync(scratch, 0, sizeof(GlobalScratch), st);
+    if (e == cudaSuccess) {
+        reduce_global_kernel<OP, T><<<grid, 512, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst), n,
+                                                          static_cast<GlobalScratch*>(scratch));
+        e = cudaGetLastError();
+    }
+    cudaError_t e2 = cudaFreeAsync(scratch, st);
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "reduce_global: %s", cudaGetErrorString(e));
+    if (e2 != cudaSuccess) return fail(static_cast<int>(e2), "reduce_global: scratch release: %s", cudaGetErrorString(e2));
+    return ok();
+}
+
+template <int OP, typename T>
+static int run_axis(const void* src, void* dst, size_t outer, size_t axis, size_t inner, cudaStream_t st) {
+    const T* s = static_cast<const T*>(src);
+    T* d = static_cast<T*>(dst);
+    const size_t cap = static_cast<size_t>(sm_count()) * 16;
+    if (inner == 1) {
+        if (axis >= 2048) {
+            const size_t grid = outer < cap ? outer : cap;
+            reduce_rows_cta_kernel<OP, T><<<static_cast<unsigned>(grid), 512, 0, st>>>(s, d, outer, axis);
+        } else {
+            size_t grid = (outer + 7) / 8;
+            if (grid > cap) grid = cap;
+            reduce_rows_warp_kernel<OP, T><<<static_cast<unsigned>(grid), 256, 0, st>>>(s, d, outer, axis);
+        }
+    } else {
+        size_t grid = (outer * inner + 255) / 256;
+        if (grid > cap) grid = cap;
+        reduce_inner_kernel<OP, T><<<static_cast<unsigned>(grid), 256, 0, st>>>(s, d, outer, axis, inner);
+    }
+    return launch_status("reduce_axis");
+}
+
+template <typename T>
+static int dispatch_global(int op, const void* src, void* dst, size_t n, cudaStream_t st) {
+    switch (op) {
+    case RED_SUM: if constexpr (!std::is_same_v<T, uint8_t>) return run_global<RED_SUM, T>(src, dst, n, st); break;
+    case RED_PROD: if constexpr (!std::is_same_v<T, uint8_t>) return run_global<RED_PROD, T>(src, dst, n, st); break;
+    case RED_MIN: return run_global<RED_MIN, T>(src, dst, n, st);
+    case RED_MAX: return run_global<RED_MAX, T>(src, dst, n, st);
+    default: return fail(cudaErrorInvalidValue, "reduce_global: unknown op code %d", op);
+    }
+    return fail(cudaErrorInvalidValue, "reduce_global: op %d does not support U8", op);
+}
+
+template <typename T>
+static int dispatch_axis(int op, const void* src, void* dst, size_t outer, size_t axis, size_t inner, cudaStream_t st) {
+    switch (op) {
+    case RED_SUM: if constexpr (!std::is_same_v<T, uint8_t>) return run_axis<RED_SUM, T>(src, dst, outer, axis, inner, st); break;
+    case RED_PROD: if constexpr (!std::is_same_v<T, uint8_t>) return run_axis<RED_PROD, T>(src, dst, outer, axis, inner, st); break;
+    case RED_MIN: return run_axis<RED_MIN, T>(src, dst, outer, axis, inner, st);
+    case RED_MAX: return run_axis<RED_MAX, T>(src, dst, outer, axis, inner, st);
+    default: return fail(cudaErrorInvalidValue, "reduce_axis: unknown op code %d", op);
+    }
+    return fail(cudaErrorInvalidValue, "reduce_axis: op %d does not support U8", op);
+}
+
+}  // namespace bee_b200
+
+using namespace bee_b200;
+
+extern "C" {
+
+int bee_b200_reduce_global(int op, int dt, const void* src, void* dst, size_t n, bee_b200_stream_t stream) {
+    if (n == 0) return fail(cudaErrorInvalidValue, "reduce_global: empty input");
+    if (!src || !dst) return fail(cudaErrorInvalidValue, "reduce_global: null pointer");
+    cudaStream_t st = as_stream(stream);
+    switch (dt) {
+    case DT_U8: return dispatch_global<uint8_t>(op, src, dst, n, st);
+    case DT_I32: return dispatch_global<int32_t>(op, src, dst, n, st);
+    case DT_I64: return dispatch_global<int64_t>(op, src, dst, n, st);
+    case DT_F32: return dispatch_global<float>(op, src, dst, n, st);
+    case DT_F64: return dispatch_global<double>(op, src, dst, n, st);
+    default: return fail(cudaErrorInvalidValue, "reduce_global: unsupported dtype %d", dt);
+    }
+}
+
+int bee_b200_reduce_axis(int op, int dt, const void* src, void* dst, size_t outer, size_t axis, size_t inner,
+                         bee_b200_stream_t stream) {
+    if (outer == 0 || axis == 0 || inner == 0) return fail(cudaErrorInvalidValue, "reduce_axis: empty extent");
+    if (!src || !dst) return fail(cudaErrorInvalidValue, "reduce_axis: null pointer");
+    cudaStream_t st = as_stream(stream);
+    switch (dt) {
+    case DT_U8: return dispatch_axis<uint8_t>(op, src, dst, outer, axis, inner, st);
+    case DT_I32: return dispatch_axis<int32_t>(op, src, dst, outer, axis, inner, st);
+    case DT_I64: return dispatch_axis<int64_t>(op, src, dst, outer, axis, inner, st);
+    case DT_F32: return dispatch_axis<float>(op, src, dst, outer, axis, inner, st);
+    case DT_F64: return dispatch_axis<double>(op, src, dst, outer, axis, inner, st);
+    default: return fail(cudaErrorInvalidValue, "reduce_axis: unsupported dtype %d", dt);
+    }
+}
+
+}  // extern "C"

@@ -1,0 +1,373 @@
+// Row-wise operators: softmax, RMSNorm, RoPE and the fused RMSNorm+RoPE.
+//
+// None of these exist in the reference (its CPU oracle composes them from
+// public ops: max/sub/exp/sum/div for softmax, mul/mean/add/sqrt/div/mul for
+// RMSNorm, slice views with mul/sub/add for RoPE).  B200 design: one CTA owns
+// one row at a time and keeps it in registers, so every byte is read from HBM
+// once and written once (the single-pass minimum); loads are 16 bytes (fp32)
+// or 8/16 bytes (bf16) and streaming; the reductions are warp shuffles plus
+// one shared-memory exchange; the grid is a multiple of the SM count and
+// strides over rows.
+#include <cmath>
+
+#include "common.cuh"
+
+namespace bee_b200 {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ---------------------------------------------------------------- element IO
+
+// A "quad" is 4 consecutive elements: fp32 -> one 16-byte load, bf16 -> 8 bytes.
+template <typename T> struct Quad;
+template <> struct Quad<float> {
+    static __device__ __forceinline__ void load(const float* p, float v[4]) {
+        float4 q = __ldcs(reinterpret_cast<const float4*>(p));
+        v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+    }
+    static __device__ __forceinline__ void store(float* p, const float v[4]) {
+        __stcs(reinterpret_cast<float4*>(p), make_float4(v[0], v[1], v[2], v[3]));
+    }
+    static __device__ __forceinline__ float get(const float* p, size_t i) { return p[i]; }
+    static __device__ __forceinline__ void put(float* p, size_t i, float v) { p[i] = v; }
+};
+template <> struct Quad<uint16_t> {  // bf16 bits
+    static __device__ __forceinline__ void load(const uint16_t* p, float v[4]) {
+        uint2 q = __ldcs(reinterpret_cast<const uint2*>(p));
+        v[0] = bf16_lo(q.x); v[1] = bf16_hi(q.x); v[2] = bf16_lo(q.y); v[3] = bf16_hi(q.y);
+    }
+    static __device__ __forceinline__ void store(uint16_t* p, const float v[4]) {
+        __stcs(reinterpret_cast<uint2*>(p), make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3])));
+    }
+    static __device__ __forceinline__ float get(const uint16_t* p, size_t i) {
+        return __uint_as_float(static_cast<uint32_t>(p[i]) << 16);
+    }
+    static __device__ __forceinline__ void put(uint16_t* p, size_t i, float v) {
+        __nv_bfloat16 h = __float2bfloat16_rn(v);
+        p[i] = *reinterpret_cast<uint16_t*>(&h);
+    }
+};
+
+// Loads the row slots owned by this thread: slot s covers elements
+// [(s*THREADS + tid)*4, +4).  `vec` selects quad loads (row start aligned and
+// cols % 4 == 0) versus element loads; missing elements get `fill`.
+template <typename T, int THREADS, int NQ>
+__device__ __forceinline__ void load_row(const T* row, size_t cols, bool vec, float fill, float v[NQ][4]) {
+#pragma unroll
+    for (int s = 0; s < NQ; ++s) {
+        const size_t e = (static_cast<size_t>(s) * THREADS + threadIdx.x) * 4;
+        if (vec && e + 4 <= cols) {
+            Quad<T>::load(row + e, v[s]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[s][k] = (e + k < cols) ? Quad<T>::get(row, e + k) : fill;
+        }
+    }
+}
+
+template <typename T, int THREADS, int NQ>
+__device__ __forceinline__ void store_row(T* row, size_t cols, bool vec, const float v[NQ][4]) {
+#pragma unroll
+    for (int s = 0; s < NQ; ++s) {
+        const size_t e = (static_cast<size_t>(s) * THREADS + threadIdx.x) * 4;
+        if (vec && e + 4 <= cols) {
+            Quad<T>::store(row + e, v[s]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (e + k < cols) Quad<T>::put(row, e + k, v[s][k]);
+        }
+    }
+}
+
+template <int THREADS> __device__ __forceinline__ float block_max(float v, float* red) {
+    v = warp_max(v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = red[0];
+#pragma unroll
+    for (int w = 1; w < THREADS / 32; ++w) r = fmaxf(r, red[w]);
+    return r;
+}
+
+template <int THREADS> __device__ __forceinline__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = 0.f;
+#pragma unroll
+    for (int w = 0; w < THREADS / 32; ++w) r += red[w];
+    return r;
+}
+
+// ---------------------------------------------------------------- softmax
+
+template <typename Ti, typename To, int THREADS, int NQ>
+__global__ void __launch_bounds__(THREADS) softmax_rows_kernel(const Ti* __restrict__ src, To* __restrict__ dst,
+                                                               size_t rows, size_t cols, int vec) {
+    __shared__ float red[THREADS / 32];
+    for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        float v[NQ][4];
+        load_row<Ti, THREADS, NQ>(src + r * cols, cols, vec, -INFINITY, v);
+        float m = -INFINITY;
+#pragma unroll
+        for (int s = 0; s < NQ; ++s)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) m = fmaxf(m, v[s][k]);
+        m = block_max<THREADS>(m, red);
+        const float ms = m * kLog2e;
+        float sum = 0.f;
+#pragma unroll
+        for (int s = 0; s < NQ; ++s)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                // exp(x - m) = 2^(x*log2e - m*log2e); padding (-inf) gives 0.
+                v[s][k] = exp2f(fmaf(v[s][k], kLog2e, -ms));
+                sum += v[s][k];
+            }
+        sum = block_sum<THREADS>(sum, red);
+        const float inv = 1.0f / sum;
+#pragma unroll
+        for (int s = 0; s < NQ; ++s)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[s][k] *= inv;
+        store_row<To, THREADS, NQ>(dst + r * cols, cols, vec, v);
+    }
+}
+
+// Rows longer than the register-resident limit: online max/sum in one read,
+// normalise in a second read (3 passes of traffic instead of 2).
+template <typename Ti, typename To>
+__global__ void __launch_bounds__(1024) softmax_rows_long_kernel(const Ti* __restrict__ src, To* __restrict__ dst,
+                                                                 size_t rows, size_t cols) {
+    __shared__ float red_m[32], red_s[32];
+    for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const Ti* row = src + r * cols;
+        float m = -INFINITY, s = 0.f;
+        for (size_t j = threadIdx.x; j < cols; j += blockDim.x) {
+            const float x = Quad<Ti>::get(row, j);
+            const float nm = fmaxf(m, x);
+            s = s * exp2f((m - nm) * kLog2e) + exp2f((x - nm) * kLog2e);
+            m = nm;
+        }
+        // combine (m, s) pairs across the warp, then across warps
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
+            const float nm = fmaxf(m, om);
+            s = (nm == -INFINITY) ? 0.f : s * exp2f((m - nm) * kLog2e) + os * exp2f((om - nm) * kLog2e);
+            m = nm;
+        }
+        __syncthreads();
+        if ((threadIdx.x & 31) == 0) {
+            red_m[threadIdx.x >> 5] = m;
+            red_s[threadIdx.x >> 5] = s;
+        }
+        __syncthreads();
+        float M = -INFINITY;
+        for (int w = 0; w < int(blockDim.x >> 5); ++w) M = fmaxf(M, red_m[w]);
+        float S = 0.f;
+        for (int w = 0; w < int(blockDim.x >> 5); ++w)
+            S += (red_m[w] == -INFINITY) ? 0.f : red_s[w] * exp2f((red_m[w] - M) * kLog2e);
+        const float inv = 1.0f / S;
+        for (size_t j = threadIdx.x; j < cols; j += blockDim.x)
+            Quad<To>::put(dst + r * cols, j, exp2f((Quad<Ti>::get(row, j) - M) * kLog2e) * inv);
+    }
+}
+
+// ---------------------------------------------------------------- RMSNorm (+RoPE)
+
+struct RopeArgs {
+    int enabled;
+    size_t seq;
+    size_t head_dim;
+    size_t pos_offset;
+    double log_theta;
+};
+
+// One CTA per row.  NORM: scale by 1/sqrt(mean(x^2)+eps) * w.  ROPE: rotate
+// each head's halves; the partner element of a head lives in another thread,
+// so the row passes through shared memory (fp32) between the two steps.
+template <typename T, int THREADS, int NQ, bool NORM, bool ROPE>
+__global__ void __launch_bounds__(THREADS) norm_rope_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                            T* __restrict__ y, size_t rows, size_t cols, float eps,
+                                                            RopeArgs rope, int vec) {
+    extern __shared__ float smem[];  // ROPE: cols floats of row + head_dim/2 float2 of (cos, sin)
+    __shared__ float red[THREADS / 32];
+    __shared__ double inv_freq[128];
+    const size_t half = rope.head_dim / 2;
+    if (ROPE) {
+        for (size_t i = threadIdx.x; i < half; i += THREADS)
+            inv_freq[i] = exp(-(2.0 * static_cast<double>(i) / static_cast<double>(rope.head_dim)) * rope.log_theta);
+    }
+    float wv[NQ][4];
+    if (NORM) load_row<T, THREADS, NQ>(w, cols, vec, 0.f, wv);
+    float* rowbuf = smem;
+    float2* cs = reinterpret_cast<float2*>(smem + cols);
+    for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        float v[NQ][4];
+        load_row<T, THREADS, NQ>(x + r * cols, cols, vec, 0.f, v);
+        if (NORM) {
+            float ss = 0.f;
+#pragma unroll
+            for (int s = 0; s < NQ; ++s)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) ss = fmaf(v[s][k], v[s][k], ss);
+            ss = block_sum<THREADS>(ss, red);
+            const float inv = 1.0f / sqrtf(ss / static_cast<float>(cols) + eps);
+#pragma unroll
+            for (int s = 0; s < NQ; ++s)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[s][k] = v[s][k] * inv * wv[s][k];
+        }
+        if (ROPE) {
+            const double p = static_cast<double>(r % rope.seq + rope.pos_offset);
+            __syncthreads();  // previous row's readers of rowbuf / cs are done
+            for (size_t i = threadIdx.x; i < half; i += THREADS) {
+                double sn, c;
+                sincos(p * inv_freq[i], &sn, &c);
+                cs[i] = make_float2(static_cast<float>(c), static_cast<float>(sn));
+            }
+#pragma unroll
+            for (int s = 0; s < NQ; ++s) {
+                const size_t e = (static_cast<size_t>(s) * THREADS + threadIdx.x) * 4;
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (e + k < cols) rowbuf[e + k] = v[s][k];
+            }
+            __syncthreads();
+#pragma unroll
+            for (int s = 0; s < NQ; ++s) {
+                const size_t e = (static_cast<size_t>(s) * THREADS + threadIdx.x) * 4;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const size_t idx = e + k;
+                    if (idx >= cols) continue;
+                    const size_t d = idx % rope.head_dim;
+                    if (d < half) {
+                        const float2 t = cs[d];
+                        v[s][k] = v[s][k] * t.x - rowbuf[idx + half] * t.y;
+                    } else {
+                        const float2 t = cs[d - half];
+                        v[s][k] = v[s][k] * t.x + rowbuf[idx - half] * t.y;
+                    }
+                }
+            }
+        }
+        store_row<T, THREADS, NQ>(y + r * cols, cols, vec, v);
+    }
+}
+
+// ---------------------------------------------------------------- launchers
+
+static unsigned row_grid(size_t rows, int ctas_per_sm) {
+    size_t cap = static_cast<size_t>(sm_count()) * ctas_per_sm;
+    return static_cast<unsigned>(rows < cap ? rows : cap);
+}
+
+template <typename Ti, typename To>
+static int launch_softmax(const void* src, void* dst, size_t rows, size_t cols, cudaStream_t st) {
+    const Ti* s = static_cast<const Ti*>(src);
+    To* d = static_cast<To*>(dst);
+    const int vec = (cols % 4 == 0) && aligned16(src) && aligned16(dst) ? 1 : 0;
+    // Register-resident variants: up to 32 fp32 values per thread.
+    if (cols <= 256 * 4) softmax_rows_kernel<Ti, To, 256, 1><<<row_grid(rows, 8), 256, 0, st>>>(s, d, rows, cols, vec);
+    else if (cols <= 256 * 4 * 4) softmax_rows_kernel<Ti, To, 256, 4><<<row_grid(rows, 8), 256, 0, st>>>(s, d, rows, cols, vec);
+    else if (cols <= 256 * 4 * 8) softmax_rows_kernel<Ti, To, 256, 8><<<row_grid(rows, 8), 256, 0, st>>>(s, d, rows, cols, vec);
+    else if (cols <= 1024 * 4 * 8) softmax_rows_kernel<Ti, To, 1024, 8><<<row_grid(rows, 2), 1024, 0, st>>>(s, d, rows, cols, vec);
+    else softmax_rows_long_kernel<Ti, To><<<row_grid(rows, 2), 1024, 0, st>>>(s, d, rows, cols);
+    return launch_status("softmax_rows");
+}
+
+template <typename T, bool NORM, bool ROPE>
+static int launch_norm_rope(const void* x, const void* w, void* y, size_t rows, size_t cols, float eps, RopeArgs rope,
+                            cudaStream_t st) {
+    const T* px = static_cast<const T*>(x);
+    const T* pw = static_cast<const T*>(w);
+    T* py = static_cast<T*>(y);
+    const int vec = (cols % 4 == 0) && aligned16(x) && aligned16(y) && (!NORM || aligned16(w)) ? 1 : 0;
+    const size_t smem = ROPE ? cols * sizeof(float) + (rope.head_dim / 2) * sizeof(float2) : 0;
+    if (smem > 200 * 1024) return fail(cudaErrorInvalidValue, "rope: row of %zu elements exceeds shared memory", cols);
+#define BEE_NR_LAUNCH(THREADS, NQ, CTAS)                                                                              \
+    do {                                                                                                              \
+        auto k = norm_rope_kernel<T, THREADS, NQ, NORM, ROPE>;                                                       \
+        if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));         \
+        k<<<row_grid(rows, CTAS), THREADS, smem, st>>>(px, pw, py, rows, cols, eps, rope, vec);                       \
+    } while (0)
+    if (cols <= 128 * 4 * 2) BEE_NR_LAUNCH(128, 2, 12);
+    else if (cols <= 256 * 4 * 4) BEE_NR_LAUNCH(256, 4, 8);
+    else if (cols <= 512 * 4 * 4) BEE_NR_LAUNCH(512, 4, 4);
+    else if (cols <= 1024 * 4 * 8) BEE_NR_LAUNCH(1024, 8, 2);
+    else return fail(cudaErrorInvalidValue, "rms_norm/rope: row of %zu elements exceeds 32768", cols);
+#undef BEE_NR_LAUNCH
+    return launch_status(NORM ? (ROPE ? "rms_norm_rope" : "rms_norm_rows") : "rope");
+}
+
+static int check_rope(size_t rows, size_t seq, size_t heads, size_t head_dim, double theta, const char* what) {
+    if (seq == 0 || heads == 0 || head_dim == 0) return fail(cudaErrorInvalidValue, "%s: empty extent", what);
+    if (head_dim % 2 != 0 || head_dim > 256)
+        return fail(cudaErrorInvalidValue, "%s: head_dim %zu must be even and <= 256", what, head_dim);
+    if (rows % seq != 0) return fail(cudaErrorInvalidValue, "%s: rows %zu not a multiple of seq %zu", what, rows, seq);
+    if (!(theta > 0.0)) return fail(cudaErrorInvalidValue, "%s: theta must be positive", what);
+    return 0;
+}
+
+}  // namespace bee_b200
+
+using namespace bee_b200;
+
+extern "C" {
+
+int bee_b200_softmax_rows(int dt, const void* src, void* dst, size_t rows, size_t cols, bee_b200_stream_t stream) {
+    if (rows == 0) return ok();
+    if (cols == 0) return fail(cudaErrorInvalidValue, "softmax_rows: zero columns");
+    if (!src || !dst) return fail(cudaErrorInvalidValue, "softmax_rows: null pointer");
+    cudaStream_t st = as_stream(stream);
+    if (dt == DT_F32) return launch_softmax<float, float>(src, dst, rows, cols, st);
+    if (dt == DT_BF16) return launch_softmax<uint16_t, uint16_t>(src, dst, rows, cols, st);
+    return fail(cudaErrorInvalidValue, "softmax_rows: unsupported dtype %d", dt);
+}
+
+int bee_b200_rms_norm_rows(int dt, const void* x, const void* w, void* y, size_t rows, size_t cols, float eps,
+                           bee_b200_stream_t stream) {
+    if (rows == 0) return ok();
+    if (cols == 0) return fail(cudaErrorInvalidValue, "rms_norm_rows: zero columns");
+    if (!x || !w || !y) return fail(cudaErrorInvalidValue, "rms_norm_rows: null pointer");
+    if (!(eps >= 0.f)) return fail(cudaErrorInvalidValue, "rms_norm_rows: eps must be >= 0");
+    cudaStream_t st = as_stream(stream);
+    RopeArgs none{0, 1, 2, 0, 0.0};
+    if (dt == DT_F32) return launch_norm_rope<float, true, false>(x, w, y, rows, cols, eps, none, st);
+    if (dt == DT_BF16) return launch_norm_rope<uint16_t, true, false>(x, w, y, rows, cols, eps, none, st);
+    return fail(cudaErrorInvalidValue, "rms_norm_rows: unsupported dtype %d", dt);
+}
+
+int bee_b200_rope(int dt, const void* x, void* y, size_t rows, size_t seq, size_t heads, size_t head_dim, double theta,
+                  size_t pos_offset, bee_b200_stream_t stream) {
+    if (rows == 0) return ok();
+    if (int rc = check_rope(rows, seq, heads, head_dim, theta, "rope")) return rc;
+    if (!x || !y) return fail(cudaErrorInvalidValue, "rope: null pointer");
+    cudaStream_t st = as_stream(stream);
+    RopeArgs ra{1, seq, head_dim, pos_offset, log(theta)};
+    const size_t cols = heads * head_dim;
+    if (dt == DT_F32) return launch_norm_rope<float, false, true>(x, x, y, rows, cols, 0.f, ra, st);
+    if (dt == DT_BF16) return launch_norm_rope<uint16_t, false, true>(x, x, y, rows, cols, 0.f, ra, st);
+    return fail(cudaErrorInvalidValue, "rope: unsupported dtype %d", dt);
+}
+
+int bee_b200_rms_norm_rope(int dt, const void* x, const void* w, void* y, size_t rows, size_t seq, size_t heads,
+                           size_t head_dim, float eps, double theta, size_t pos_offset, bee_b200_stream_t stream) {
+    if (rows == 0) return ok();
+    if (int rc = check_rope(rows, seq, heads, head_dim, theta, "rms_norm_rope")) return rc;
+    if (!x || !w || !y) return fail(cudaErrorInvalidValue, "rms_norm_rope: null pointer");
+    if (!(eps >= 0.f)) return fail(cudaErrorInvalidValue, "rms_norm_rope: eps must be >= 0");
+    cudaStream_t st = as_stream(stream);
+    RopeArgs ra{1, seq, head_dim, pos_offset, log(theta)};
+    const size_t cols = heads * head_dim;
+    if (dt == DT_F32) return launch_norm_rope<float, true, true>(x, w, y, rows, cols, eps, ra, st);
+    if (dt == DT_BF16) return launch_norm_rope<uint16_t, true, true>(x, w, y, rows, cols, eps, ra, st);
+    return fail(cudaErrorInvalidValue, "rms_norm_rope: unsupported dtype %d", dt);
+}
+
+}  // extern "C"

@@ -1,0 +1,115 @@
+// Status reporting, device memory and stream entry points of the C ABI.
+//
+// Mirrors bee::cuda's runtime wrappers (Bee/CUDA/Api.cpp:117-192): allocation
+// is stream-ordered from the current device's default pool, copies are
+// cudaMemcpyAsync on the caller's stream.  Unlike the reference nothing here
+// synchronises implicitly; bee_b200_stream_synchronize is the explicit fence.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace bee_b200 {
+
+namespace {
+thread_local char g_msg[512] = "";
+}
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int ok() {
+    g_msg[0] = '\0';
+    return 0;
+}
+
+int launch_status(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "%s: launch failed: %s", what, cudaGetErrorString(e));
+    return ok();
+}
+
+int sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cached[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+}  // namespace bee_b200
+
+using namespace bee_b200;
+
+extern "C" {
+
+const char* bee_b200_last_error(void) { return g_msg; }
+
+const char* bee_b200_status_string(int status) { return cudaGetErrorString(static_cast<cudaError_t>(status)); }
+
+int bee_b200_version(void) { return 100; }
+
+int bee_b200_allocate(void** out_ptr, size_t nbytes, size_t alignment, bee_b200_stream_t stream) {
+    if (!out_ptr) return fail(cudaErrorInvalidValue, "allocate: out_ptr is null");
+    *out_ptr = nullptr;
+    if (alignment > 256 || (alignment & (alignment - 1)) != 0)
+        return fail(cudaErrorInvalidValue, "allocate: alignment %zu unsupported (power of two <= 256)", alignment);
+    if (nbytes == 0) return ok();
+    cudaError_t e = cudaMallocAsync(out_ptr, nbytes, as_stream(stream));
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "allocate(%zu): %s", nbytes, cudaGetErrorString(e));
+    return ok();
+}
+
+int bee_b200_deallocate(void* ptr, bee_b200_stream_t stream) {
+    if (!ptr) return ok();
+    cudaError_t e = cudaFreeAsync(ptr, as_stream(stream));
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "deallocate: %s", cudaGetErrorString(e));
+    return ok();
+}
+
+static int copy(void* dst, const void* src, size_t nbytes, cudaMemcpyKind kind, bee_b200_stream_t stream,
+                const char* what) {
+    if (nbytes == 0) return ok();
+    if (!dst || !src) return fail(cudaErrorInvalidValue, "%s: null pointer", what);
+    cudaError_t e = cudaMemcpyAsync(dst, src, nbytes, kind, as_stream(stream));
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "%s(%zu): %s", what, nbytes, cudaGetErrorString(e));
+    return ok();
+}
+
+int bee_b200_memcpy_h2d(void* dst, const void* src, size_t nbytes, bee_b200_stream_t stream) {
+    return copy(dst, src, nbytes, cudaMemcpyHostToDevice, stream, "memcpy_h2d");
+}
+
+int bee_b200_memcpy_d2h(void* dst, const void* src, size_t nbytes, bee_b200_stream_t stream) {
+    return copy(dst, src, nbytes, cudaMemcpyDeviceToHost, stream, "memcpy_d2h");
+}
+
+int bee_b200_memcpy_d2d(void* dst, const void* src, size_t nbytes, bee_b200_stream_t stream) {
+    return copy(dst, src, nbytes, cudaMemcpyDeviceToDevice, stream, "memcpy_d2d");
+}
+
+int bee_b200_memset(void* ptr, int value, size_t nbytes, bee_b200_stream_t stream) {
+    if (nbytes == 0) return ok();
+    if (!ptr) return fail(cudaErrorInvalidValue, "memset: null pointer");
+    cudaError_t e = cudaMemsetAsync(ptr, value & 0xff, nbytes, as_stream(stream));
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "memset(%zu): %s", nbytes, cudaGetErrorString(e));
+    return ok();
+}
+
+int bee_b200_stream_synchronize(bee_b200_stream_t stream) {
+    cudaError_t e = cudaStreamSynchronize(as_stream(stream));
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "stream_synchronize: %s", cudaGetErrorString(e));
+    return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,467 @@
+"""Benchmark of the Bee::Tensor hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload sweep]
+
+Workload "sweep" (the headline): the memory-bound op sweep on row-major
+[8192, 8192] tensors — fp32 add and mul of two N(0,1) tensors, fp32->bf16 cast,
+row sum, row max, row softmax, and the bit-exact int32 full sum of a uniform
+[-1000, 1000] tensor.  A step runs every op once over the GPU's shard; rows are
+sharded over GPUs with 8192 rows per GPU (weak scaling: the global tensor is
+[8192*N, 8192]); the only exchange is the NCCL all-reduce of the int32 partial
+sums.  Each tensor is 256 MiB, larger than the 126 MB L2, so no L2 flush is
+needed between ops or steps.  ``value`` is the algorithmic bytes moved by all
+ranks per second (GB/s, 1e9).
+
+``--impl reference`` times the reference's own CPU implementation of the same
+ops (the Bee::Tensor CPU path compiled from the reference sources into
+oracle/_ref, else the oracle port) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+ROWS, COLS = 8192, 8192
+N_EL = ROWS * COLS
+F32_BYTES = N_EL * 4
+# algorithmic bytes per op over one 8192 x 8192 shard
+OP_BYTES = {
+    "add_f32": 3 * F32_BYTES,
+    "mul_f32": 3 * F32_BYTES,
+    "cast_f32_bf16": F32_BYTES + N_EL * 2,
+    "row_sum_f32": F32_BYTES + ROWS * 4,
+    "row_max_f32": F32_BYTES + ROWS * 4,
+    "softmax_f32": 2 * F32_BYTES,
+    "sum_i32": F32_BYTES + 4,
+}
+STEP_BYTES = sum(OP_BYTES.values())
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: str):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def smi_id(dev) -> str:
+    """nvidia-smi identifier (PCI bus id) of a torch device, robust to CUDA_VISIBLE_DEVICES."""
+    import torch
+    p = torch.cuda.get_device_properties(dev)
+    try:
+        return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+    except AttributeError:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        idx = dev.index or 0
+        return vis.split(",")[idx] if vis else str(idx)
+
+
+# ---------------------------------------------------------------- distributed plumbing
+
+class Dist:
+    def __init__(self, gpus: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if gpus != self.world:
+            raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={self.world}; launch N>1 with torch.distributed.run")
+
+    def init(self):
+        import torch
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist.group.WORLD
+
+    def barrier(self):
+        if self.pg is not None:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, x: float) -> float:
+        if self.pg is None:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg is not None:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- our arm
+
+def make_inputs(rank: int):
+    """Seeded host inputs for one shard (rank r owns rows [8192 r, 8192 (r+1)))."""
+    rng = np.random.default_rng(1_000 + rank)
+    x = rng.standard_normal((ROWS, COLS), dtype=np.float32)
+    y = rng.standard_normal((ROWS, COLS), dtype=np.float32)
+    xi = rng.integers(-1000, 1001, (ROWS, COLS), dtype=np.int32)
+    return x, y, xi
+
+
+def run_ours(args, d: Dist):
+    import torch
+    from bee_b200 import _capi
+    from bee_b200._capi import call
+
+    d.init()
+    lib = _capi.lib()  # fails loudly if the CUDA library is missing
+    dev = torch.device("cuda", d.local)
+    stream = torch.cuda.Stream(device=dev)
+    st = stream.cuda_stream
+    peaks = load_peaks()
+
+    x, y, xi = make_inputs(d.rank)
+    hx = torch.from_numpy(x).pin_memory()
+    hy = torch.from_numpy(y).pin_memory()
+    hxi = torch.from_numpy(xi).pin_memory()
+    with torch.cuda.stream(stream):
+        dx = hx.to(dev, non_blocking=True)
+        dy = hy.to(dev, non_blocking=True)
+        dxi = hxi.to(dev, non_blocking=True)
+        o_add = torch.empty_like(dx)
+        o_mul = torch.empty_like(dx)
+        o_bf = torch.empty((ROWS, COLS), dtype=torch.bfloat16, device=dev)
+        o_rsum = torch.empty(ROWS, dtype=torch.float32, device=dev)
+        o_rmax = torch.empty(ROWS, dtype=torch.float32, device=dev)
+        o_sm = torch.empty_like(dx)
+        o_isum = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream.synchronize()
+
+    F32, BF16, I32 = _capi.F32, _capi.BF16, _capi.I32
+    ops = [
+        ("add_f32", lambda: call("bee_b200_ew_binary", 0, F32, dx.data_ptr(), dy.data_ptr(), o_add.data_ptr(), N_EL, st)),
+        ("mul_f32", lambda: call("bee_b200_ew_binary", 2, F32, dx.data_ptr(), dy.data_ptr(), o_mul.data_ptr(), N_EL, st)),
+        ("cast_f32_bf16", lambda: call("bee_b200_ew_cast", F32, dx.data_ptr(), BF16, o_bf.data_ptr(), N_EL, st)),
+        ("row_sum_f32", lambda: call("bee_b200_reduce_axis", 0, F32, dx.data_ptr(), o_rsum.data_ptr(), ROWS, COLS, 1, st)),
+        ("row_max_f32", lambda: call("bee_b200_reduce_axis", 2, F32, dx.data_ptr(), o_rmax.data_ptr(), ROWS, COLS, 1, st)),
+        ("softmax_f32", lambda: call("bee_b200_softmax_rows", F32, dx.data_ptr(), o_sm.data_ptr(), ROWS, COLS, st)),
+        ("sum_i32", lambda: call("bee_b200_reduce_global", 0, I32, dxi.data_ptr(), o_isum.data_ptr(), N_EL, st)),
+    ]
+    launches_per_step = len(ops)
+
+    def allreduce_isum():
+        if d.pg is not None:
+            import torch.distributed as dist
+            with torch.cuda.stream(stream):
+                dist.all_reduce(o_isum, op=dist.ReduceOp.SUM)
+
+    def step(evs=None):
+        for i, (_, fn) in enumerate(ops):
+            if evs is not None:
+                evs[i].record(stream)
+            fn()
+        if evs is not None:
+            evs[len(ops)].record(stream)
+        allreduce_isum()
+
+    # warm-up (also checks the int32 sum against the host, bit-exact)
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+    want = int(xi.astype(np.int64).sum())
+    if d.pg is not None:
+        import torch.distributed as dist
+        t = torch.tensor([want], dtype=torch.int64, device=dev)
+        dist.all_reduce(t)
+        want = int(t.item())
+    want32 = ((want + 2**31) % 2**32) - 2**31
+    got = int(o_isum.item())
+    if got != want32:
+        raise SystemExit(f"int32 sum mismatch: {got} != {want32}")
+
+    # timed region
+    per_step_events = [[torch.cuda.Event(enable_timing=True) for _ in range(len(ops) + 1)] for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(smi_id(dev)) as clk:
+        t0.record(stream)
+        for k in range(args.steps):
+            step(per_step_events[k])
+        t1.record(stream)
+        stream.synchronize()
+    d.barrier()
+    torch.cuda.synchronize()
+    ms_local = t0.elapsed_time(t1)
+    ms = d.max(ms_local)
+    per_op_ms = {name: sum(ev[i].elapsed_time(ev[i + 1]) for ev in per_step_events) / args.steps
+                 for i, (name, _) in enumerate(ops)}
+    if d.world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([per_op_ms[n] for n, _ in ops], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        per_op_ms = {n: float(v) for (n, _), v in zip(ops, t.tolist())}
+
+    ms_per_step = ms / args.steps
+    value = d.world * STEP_BYTES * args.steps / (ms / 1e3) / 1e9
+    dominant = max(per_op_ms, key=per_op_ms.get)
+    dom_gbs = OP_BYTES[dominant] / (per_op_ms[dominant] / 1e3) / 1e9
+
+    # end to end through the C ABI with host buffers: H2D inputs, ops, D2H outputs
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, d, lib, dev, stream, hx, hy, hxi, ops, allreduce_isum,
+                      [o_add, o_mul, o_bf, o_rsum, o_rmax, o_sm, o_isum], [dx, dy, dxi])
+
+    clocks = clk.summary()
+    out = None
+    if d.rank == 0:
+        ops_json = {n: {"ms": round(per_op_ms[n], 4), "GB/s": round(OP_BYTES[n] / (per_op_ms[n] / 1e3) / 1e9, 1),
+                        "frac_of_hbm": round(OP_BYTES[n] / (per_op_ms[n] / 1e3) / 1e9 / peaks["hbm_gbs"], 3)}
+                    for n, _ in ops}
+        out = {
+            "metric": "memory-bound op sweep HBM GB/s (add, mul, fp32->bf16 cast, row sum, row max, row softmax, "
+                      "int32 full sum) on [8192, 8192] row shards",
+            "value": round(value, 1), "unit": "GB/s", "n_gpus": d.world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded N(0,1) fp32, uniform int32 in [-1000, 1000])",
+            "config": {"workload": "memory-bound op sweep, [8192, 8192] fp32 + int32 per GPU, rows sharded "
+                                   "(8192 rows per GPU, global [8192*N, 8192])",
+                       "ops": [n for n, _ in ops], "bytes_per_step_per_gpu": STEP_BYTES,
+                       "l2": "inputs larger than L2 (each tensor 256 MiB > 126 MB), no flush",
+                       "parallelism": f"rows sharded over {d.world} GPU(s); NCCL all-reduce of the int32 partial sum"},
+            "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(dom_gbs, 1), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(dom_gbs / peaks["hbm_gbs"], 3),
+                         "peak_source": peaks["source"], "traffic": None},
+            "ops": ops_json,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+            "e2e": e2e,
+        }
+    return out
+
+
+def run_e2e(args, d, lib, dev, stream, hx, hy, hxi, ops, allreduce_isum, outs, dins):
+    """Same sweep through the C ABI with host buffers: every step copies the
+    inputs host->device (pinned), runs the ops and copies every output back."""
+    import torch
+    from bee_b200._capi import call
+    st = stream.cuda_stream
+    h_outs = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+    h_ins = [hx, hy, hxi]
+    h2d = sum(t.numel() * t.element_size() for t in h_ins)
+    d2h = sum(t.numel() * t.element_size() for t in h_outs)
+
+    def e2e_step():
+        for h, dd in zip(h_ins, dins):
+            call("bee_b200_memcpy_h2d", dd.data_ptr(), h.data_ptr(), h.numel() * h.element_size(), st)
+        for _, fn in ops:
+            fn()
+        allreduce_isum()
+        for h, o in zip(h_outs, outs):
+            call("bee_b200_memcpy_d2h", h.data_ptr(), o.data_ptr(), o.numel() * o.element_size(), st)
+        call("bee_b200_stream_synchronize", st)
+
+    steps = max(1, min(args.steps, 5))
+    e2e_step()
+    d.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        e2e_step()
+    t1.record(stream)
+    stream.synchronize()
+    ms = d.max(t0.elapsed_time(t1))
+    return {"value": round(d.world * STEP_BYTES * steps / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
+            "ms_per_step": round(ms / steps, 3)}
+
+
+# ---------------------------------------------------------------- CPU baseline / reference arm
+
+def cpu_sweep(sample_rows: int, reps: int = 1):
+    """Times the reference CPU ops (oracle/_ref, else the oracle port) on a
+    [sample_rows, 8192] sample of the shard; returns (GB/s, info)."""
+    from oracle.oracle import Oracle, Reference, reference_available
+    x, y, xi = make_inputs(0)
+    xs, ys, xis = x[:sample_rows], y[:sample_rows], xi[:sample_rows]
+    n = sample_rows * COLS
+    scale = sample_rows / ROWS
+    times = {}
+    if reference_available():
+        ref = Reference()
+        kind, cores = "reference", ref.threads()
+        times["add_f32"] = ref.binary_f32(0, xs, ys, reps)[1]
+        times["mul_f32"] = ref.binary_f32(2, xs, ys, reps)[1]
+        times["row_sum_f32"] = ref.reduce_rows_f32(0, xs, reps)[1]
+        times["row_max_f32"] = ref.reduce_rows_f32(2, xs, reps)[1]
+        times["softmax_f32"] = ref.softmax_f32(xs, reps)[1]
+        times["sum_i32"] = ref.reduce_global_i32(0, xis, reps)[1]
+        # the reference's CPU cast to BF16 writes nothing (CastCpu.hpp:348): time the restatement
+        orc = Oracle()
+        t = time.perf_counter()
+        orc.cast_f32_bf16(xs)
+        times["cast_f32_bf16"] = time.perf_counter() - t
+    else:
+        orc = Oracle()
+        kind, cores = "port", 1
+
+        def tm(fn):
+            t = time.perf_counter()
+            fn()
+            return time.perf_counter() - t
+        times["add_f32"] = tm(lambda: orc.binary(0, xs, ys))
+        times["mul_f32"] = tm(lambda: orc.binary(2, xs, ys))
+        times["cast_f32_bf16"] = tm(lambda: orc.cast_f32_bf16(xs))
+        times["row_sum_f32"] = tm(lambda: orc.reduce_rows_f32(0, xs))
+        times["row_max_f32"] = tm(lambda: orc.reduce_rows_f32(2, xs))
+        times["softmax_f32"] = tm(lambda: orc.softmax_f32(xs))
+        times["sum_i32"] = tm(lambda: orc.reduce_global_i32(0, xis))
+    total_t = sum(times.values())
+    gbs = STEP_BYTES * scale / total_t / 1e9
+    info = {"kind": kind, "cores": cores,
+            "sample": f"[{sample_rows}, {COLS}] rows of the [8192, 8192] shard per op ({n} elements), "
+                      f"all 7 ops; bf16 cast timed on the oracle restatement (the reference's CPU cast to BF16 "
+                      f"is a no-op)" if kind == "reference" else f"[{sample_rows}, {COLS}] sample, oracle port",
+            "per_op_s": {k: round(v, 4) for k, v in times.items()}}
+    return gbs, info
+
+
+def run_reference(args, d: Dist):
+    if d.rank != 0:
+        return None
+    sample_rows = args.ref_rows
+    for _ in range(args.warmup):
+        cpu_sweep(sample_rows)
+    vals, info = [], None
+    t_all = time.perf_counter()
+    for _ in range(args.steps):
+        v, info = cpu_sweep(sample_rows)
+        vals.append(v)
+    wall = time.perf_counter() - t_all
+    value = statistics.median(vals)
+    cb = dict(info)
+    cb.update({"value": round(value, 3), "unit": "GB/s"})
+    return {
+        "metric": "memory-bound op sweep HBM GB/s (add, mul, fp32->bf16 cast, row sum, row max, row softmax, "
+                  "int32 full sum) on [8192, 8192] row shards",
+        "impl": "reference", "value": round(value, 3), "unit": "GB/s", "n_gpus": d.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(wall / max(args.steps, 1) * 1e3, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) fp32, uniform int32 in [-1000, 1000])",
+        "config": {"workload": "memory-bound op sweep, [8192, 8192] fp32 + int32 per GPU, rows sharded "
+                               "(8192 rows per GPU, global [8192*N, 8192])",
+                   "sample_rows_per_step": sample_rows},
+        "cpu_baseline": cb,
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["sweep"], default="sweep")
+    ap.add_argument("--ref-rows", type=int, default=2048, help="rows per CPU-baseline sample")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    d = Dist(args.gpus)
+    if args.impl == "reference":
+        out = run_reference(args, d)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
+    try:
+        out = run_ours(args, d)
+        if out is not None and not args.no_cpu_baseline and d.world == 1:
+            gbs, info = cpu_sweep(args.ref_rows)
+            cb = dict(info)
+            cb.update({"value": round(gbs, 3), "unit": "GB/s"})
+            out["cpu_baseline"] = cb
+        if out is not None:
+            print(json.dumps(out), flush=True)
+    finally:
+        d.close()
+
+
+if __name__ == "__main__":
+    main()

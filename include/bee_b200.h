@@ -1,0 +1,147 @@
+/*
+ * bee_b200 — C ABI of the B200 (sm_100a) backend for the Bee::Tensor compute path.
+ *
+ * Every function takes plain device pointers, element counts and a CUDA stream
+ * (passed as an opaque pointer; NULL means the legacy default stream) and
+ * returns an int status: 0 on success, otherwise a cudaError_t value.  Bad
+ * arguments (unknown dtype/op code, sizes that do not fit, misaligned
+ * pointers where a kernel needs 16-byte alignment) return 1
+ * (cudaErrorInvalidValue) and store a message readable through
+ * bee_b200_last_error() on the calling thread.  All compute calls are
+ * asynchronous on the given stream; a caller that wants the reference's
+ * synchronous semantics synchronises the stream afterwards (the C++ bridge in
+ * bee_b200/host does exactly that).
+ *
+ * Integer codes are the reference's:
+ *   dtype   = bee::DType            (Bee/Tensor/Core/DType.hpp:17-32)
+ *             Bool 0, U8 1, I32 2, I64 3, F32 4, F64 5, I8 6, F16 7, BF16 8
+ *   binary  = bee::cuda::BinaryOp   (Bee/CUDA/Api.hpp:77-83)   Add 0, Sub 1, Mul 2, Div 3
+ *   unary   = bee::cuda::UnaryOp    (Bee/CUDA/Api.hpp:85-92)   Neg 0, Abs 1, Sqrt 2, Exp 3, Log 4
+ *   reduce  = bee::cuda::ReduceOp   (Bee/CUDA/Api.hpp:94-100)  Sum 0, Min 1, Max 2, Prod 3
+ *
+ * Each declaration names the reference interface it replaces (file:line).
+ */
+#ifndef BEE_B200_H
+#define BEE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define BEE_B200_API __attribute__((visibility("default")))
+#else
+#define BEE_B200_API
+#endif
+
+typedef void* bee_b200_stream_t; /* a cudaStream_t */
+
+/* ----------------------------------------------------------------- status */
+
+/* Message describing the last failure on this thread ("" after a success). */
+BEE_B200_API const char* bee_b200_last_error(void);
+/* cudaGetErrorString() for a status returned by this library. */
+BEE_B200_API const char* bee_b200_status_string(int status);
+/* Library ABI version: major*10000 + minor*100 + patch. */
+BEE_B200_API int bee_b200_version(void);
+
+/* ------------------------------------------------------ memory and streams
+ * Replace bee::tensor::cuda::allocate / deallocate / memcpy_h2d / memcpy_d2h /
+ * memcpy_d2d / memset / synchronize (Bee/Tensor/Cuda/Backend.hpp:20-46,84),
+ * which forward to Bee/CUDA/Api.cpp:117-192.  Allocation is stream-ordered
+ * from the device's default memory pool, like the reference's
+ * cudaMallocFromPoolAsync (Bee/CUDA/Mem/MemoryPool.hpp:55-70); `alignment`
+ * above 256 is rejected (pool allocations are 256-byte aligned). */
+BEE_B200_API int bee_b200_allocate(void** out_ptr, size_t nbytes, size_t alignment, bee_b200_stream_t stream);
+BEE_B200_API int bee_b200_deallocate(void* ptr, bee_b200_stream_t stream);
+BEE_B200_API int bee_b200_memcpy_h2d(void* dst, const void* src, size_t nbytes, bee_b200_stream_t stream);
+BEE_B200_API int bee_b200_memcpy_d2h(void* dst, const void* src, size_t nbytes, bee_b200_stream_t stream);
+BEE_B200_API int bee_b200_memcpy_d2d(void* dst, const void* src, size_t nbytes, bee_b200_stream_t stream);
+BEE_B200_API int bee_b200_memset(void* ptr, int value, size_t nbytes, bee_b200_stream_t stream);
+BEE_B200_API int bee_b200_stream_synchronize(bee_b200_stream_t stream);
+
+/* ------------------------------------------------------------- elementwise */
+
+/* out[i] = a[i] (op) b[i] over n contiguous elements of dtype dt.
+ * dt in {U8, I32, I64, F32, F64, BF16}; BF16 computes in fp32 and rounds to
+ * nearest even.  Replaces ops_binary (Bee/CUDA/Ops/OpsBridge.hpp:27) behind
+ * tensor::cuda::ew_binary (Bee/Tensor/Cuda/Backend.hpp:51). */
+BEE_B200_API int bee_b200_ew_binary(int op, int dt, const void* a, const void* b, void* out, size_t n,
+                       bee_b200_stream_t stream);
+
+/* dst[i] = op(src[i]).  Neg/Abs: I32, I64, F32, F64, BF16; Sqrt/Exp/Log: F32,
+ * F64, BF16.  Replaces ops_unary (Bee/CUDA/Ops/OpsBridge.hpp:28) behind
+ * tensor::cuda::ew_unary (Bee/Tensor/Cuda/Backend.hpp:54). */
+BEE_B200_API int bee_b200_ew_unary(int op, int dt, const void* src, void* dst, size_t n, bee_b200_stream_t stream);
+
+/* dst[i] = cast(src[i]) between Bool, U8, I32, I64, F32, F64 and BF16.
+ * F32->BF16 rounds to nearest even (NaN stays NaN); ->Bool is (x != 0);
+ * float->int truncates toward zero like static_cast.  Replaces ops_cast
+ * (Bee/CUDA/Ops/OpsBridge.hpp:29) behind tensor::cuda::ew_cast
+ * (Bee/Tensor/Cuda/Backend.hpp:57), which has no BF16 case
+ * (Bee/CUDA/Ops/Cast.cu:96-104). */
+BEE_B200_API int bee_b200_ew_cast(int src_dt, const void* src, int dst_dt, void* dst, size_t n,
+                     bee_b200_stream_t stream);
+
+/* buf[i] *= factor for dt in {F32, F64} (mean = sum then scale).  Replaces
+ * ops_scale_fp (Bee/CUDA/Ops/OpsBridge.hpp:35). */
+BEE_B200_API int bee_b200_scale_fp(int dt, void* buf, double factor, size_t n, bee_b200_stream_t stream);
+
+/* ------------------------------------------------------------------ reduce */
+
+/* *dst = reduce(src[0..n)).  Sum/Prod: I32, I64, F32, F64; Min/Max also U8.
+ * Integer sums wrap like the reference's T-typed accumulation
+ * (Bee/Tensor/Cpu/ReduceCpu.hpp:190-193) and are bit-exact under any order.
+ * Float results are deterministic (fixed reduction tree).  n == 0 is an
+ * error, as in Bee/CUDA/Api.cpp:237-238.  Scratch for the per-block partials
+ * is taken from the stream-ordered pool for the duration of the call, as the
+ * reference does (Bee/CUDA/Ops/Reduce.cu:196-224).  Replaces
+ * ops_reduce_global (Bee/CUDA/Ops/OpsBridge.hpp:31) behind
+ * tensor::cuda::reduce_global (Bee/Tensor/Cuda/Backend.hpp:60). */
+BEE_B200_API int bee_b200_reduce_global(int op, int dt, const void* src, void* dst, size_t n,
+                           bee_b200_stream_t stream);
+
+/* [outer, axis, inner] -> [outer, inner] (same dtype set as reduce_global;
+ * F32 sums accumulate in fp32).  Replaces ops_reduce_axis
+ * (Bee/CUDA/Ops/OpsBridge.hpp:32) behind tensor::cuda::reduce_axis
+ * (Bee/Tensor/Cuda/Backend.hpp:63); inner == 1 is the row reduce. */
+BEE_B200_API int bee_b200_reduce_axis(int op, int dt, const void* src, void* dst, size_t outer, size_t axis,
+                         size_t inner, bee_b200_stream_t stream);
+
+/* ----------------------------------------------------- row-wise operators
+ * New operators (the reference has none; its CPU oracle composes them from
+ * public ops: max/sub/exp/sum/div for softmax, mul/mean/add/sqrt/div/mul for
+ * RMSNorm, slice views with mul/sub/add for RoPE). */
+
+/* Numerically stable softmax over each row of a [rows, cols] matrix:
+ * y = exp(x - max(x)) / sum(exp(x - max(x))).  dt in {F32, BF16}; math in
+ * fp32.  dst may alias src. */
+BEE_B200_API int bee_b200_softmax_rows(int dt, const void* src, void* dst, size_t rows, size_t cols,
+                          bee_b200_stream_t stream);
+
+/* y = x / sqrt(mean(x^2) + eps) * w over each row of [rows, cols]; w has
+ * cols elements.  dt in {F32, BF16}; math in fp32. */
+BEE_B200_API int bee_b200_rms_norm_rows(int dt, const void* x, const void* w, void* y, size_t rows, size_t cols,
+                           float eps, bee_b200_stream_t stream);
+
+/* Rotate-half RoPE on x viewed as [rows, heads, head_dim], rows = batch*seq,
+ * position of row r = r % seq + pos_offset, inv_freq_i = theta^(-2i/head_dim):
+ *   y[i]      = x[i] cos(p f_i) - x[i+h/2] sin(p f_i)
+ *   y[i+h/2]  = x[i+h/2] cos(p f_i) + x[i] sin(p f_i),  i < head_dim/2.
+ * dt in {F32, BF16}; head_dim even and at most 256; rows a multiple of seq. */
+BEE_B200_API int bee_b200_rope(int dt, const void* x, void* y, size_t rows, size_t seq, size_t heads,
+                  size_t head_dim, double theta, size_t pos_offset, bee_b200_stream_t stream);
+
+/* RMSNorm followed by RoPE in one pass (row = one token of heads*head_dim). */
+BEE_B200_API int bee_b200_rms_norm_rope(int dt, const void* x, const void* w, void* y, size_t rows, size_t seq,
+                           size_t heads, size_t head_dim, float eps, double theta, size_t pos_offset,
+                           bee_b200_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BEE_B200_H */

@@ -1,0 +1,66 @@
+"""Tolerance rules of the parity tests (stated once, used everywhere).
+
+* Integer, byte and index results: bit-exact.
+* IEEE-exact fp32 operations (add, sub, mul, div, min, max, the fp32->bf16
+  cast): bit-exact.
+* fp32 results of multi-step math: relative tolerance 1e-4.
+* bf16 results against the fp32 oracle: relative tolerance 1e-2.
+
+"Relative" is measured against max(|ref|, floor * rms(ref)) element-wise, so
+that entries whose exact value is near zero (cancellation in a sum, a dot
+product or a rotation) are judged on the scale of the tensor rather than on
+their own vanishing magnitude.  Sums are judged against the sum of absolute
+values of their terms, the natural condition number of summation.
+"""
+import numpy as np
+
+
+def rel_err(got, ref, floor=1e-3):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    scale = np.maximum(np.abs(ref), floor * np.sqrt(np.mean(ref * ref)) if ref.size else 0.0)
+    scale = np.where(scale == 0, 1.0, scale)
+    return float(np.max(np.abs(got - ref) / scale)) if ref.size else 0.0
+
+
+def assert_rel(got, ref, rtol, floor=1e-3, what=""):
+    e = rel_err(got, ref, floor)
+    assert e <= rtol, f"{what}: max relative error {e:.3e} > {rtol:.1e}"
+
+
+def assert_sum_close(got, ref, abs_terms, rtol, what=""):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    lim = rtol * np.maximum(np.asarray(abs_terms, np.float64), 1e-30)
+    bad = np.abs(got - ref) > lim
+    assert not bad.any(), f"{what}: {int(bad.sum())} sums outside {rtol:.1e} x sum|x|"
+
+
+def assert_dot_close(got, ref, a, b, rtol, what=""):
+    """Matrix products: |got - ref| <= rtol * (|A| @ |B|) element-wise (the
+    condition of each dot product), with a, b the fp32 operands (batched or not)."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    scale = np.abs(np.asarray(a, np.float64)) @ np.abs(np.asarray(b, np.float64))
+    scale = np.maximum(scale, 1e-30)
+    e = float(np.max(np.abs(got - ref) / scale)) if ref.size else 0.0
+    assert e <= rtol, f"{what}: max error {e:.3e} x (|A||B|) > {rtol:.1e}"
+
+
+def attention_scale(q, k, v, scale):
+    """Per-element condition of O = softmax(Q K^T * scale) V: P @ |V| (P >= 0),
+    in float64, for use with assert_scaled."""
+    q, k, v = (np.asarray(t, np.float64) for t in (q, k, v))
+    s = np.einsum("hid,hjd->hij", q, k) * scale
+    s -= s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(-1, keepdims=True)
+    return p @ np.abs(v)
+
+
+def assert_scaled(got, ref, scale, rtol, what=""):
+    """|got - ref| <= rtol * scale element-wise (scale from a condition formula)."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    e = float(np.max(np.abs(got - ref) / np.maximum(scale, 1e-30))) if ref.size else 0.0
+    assert e <= rtol, f"{what}: max scaled error {e:.3e} > {rtol:.1e}"
