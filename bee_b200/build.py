@@ -33,7 +33,10 @@ NVCC_FLAGS = [
     "-I", str(ROOT / "include"),
     "-DBEE_B200_BUILD",
 ]
-HOST_FLAGS = ["-O2", "-std=c++20", "-fPIC", "-fvisibility=hidden", "-I", str(ROOT / "include"), "-I", str(HOST)]
+CUDA_INC = str(Path(NVCC).resolve().parent.parent / "include")
+HOST_FLAGS = ["-O2", "-std=c++23", "-fPIC", "-I", str(ROOT / "include"), "-I", str(HOST), "-I", CUDA_INC]
+HOST_TEST_SRC = ROOT / "tests" / "cpp" / "test_host_bridge.cpp"
+HOST_TEST_BIN = LIB_DIR / "test_host_bridge"
 
 
 def _sources():
@@ -78,6 +81,10 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         objs.append(obj)
     if force or _stale(LIB, objs):
         _run([NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lrt", "-ldl", "-lpthread"])
+    # C++ program exercising the host bridge (run by tests/test_gpu_host_bridge.py)
+    if HOST_TEST_SRC.exists() and (force or _stale(HOST_TEST_BIN, [HOST_TEST_SRC, LIB] + headers)):
+        _run(["g++", *HOST_FLAGS, str(HOST_TEST_SRC), "-o", str(HOST_TEST_BIN), "-L", str(LIB_DIR), "-lbee_b200",
+              "-Wl,-rpath,$ORIGIN"])
     return LIB
 
 

@@ -1,0 +1,532 @@
+// Dense GEMM: C = alpha * A . op(B), batched.
+//
+// Replaces the reference's matmul kernels K1-K3 (Bee/CUDA/Ops/Matmul.cu:29-122,
+// Bee/CUDA/Ops/MatmulCutlass.cu:49-105, Bee/CUDA/Ops/MatmulTmaWmma.cu:77-211),
+// none of which has an sm_100 path.
+//
+// bf16 path (the hot one): a persistent, warp-specialised tcgen05 kernel.
+//   * warp 0 — TMA producer: 128x64 A tiles and 64xBN B tiles, 128-byte
+//     swizzle, into a STAGES-deep shared-memory ring guarded by mbarriers
+//     (no cluster multicast anywhere: the code is safe on any number of GPUs);
+//   * warp 1 — MMA issuer: tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN,
+//     K=16), fp32 accumulators in TMEM, double-buffered (2 x BN columns) so the
+//     epilogue of tile i overlaps the main loop of tile i+1; tcgen05.commit
+//     releases ring slots and hands finished accumulators over;
+//   * warps 2-5 — epilogue: tcgen05.ld 32 columns at a time, scale by alpha,
+//     convert (bf16 RNE or fp32) and store.
+//   Tiles are visited in a grouped raster (16 M-blocks per group) so the ~148
+//   tiles in flight share A and B panels in L2.  Every mbarrier wait is
+//   bounded: a wait that gives up records a code in the device status word,
+//   raises a CTA-wide abort flag, and the CTA drains and frees TMEM.
+//
+// Other dtypes (F32 for the parity config, F64, I32, I64) and bf16 shapes the
+// TMA path cannot express (row strides not a multiple of 16 bytes) use a
+// shared-memory tiled SIMT kernel with boundary checks.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace bee_b200 {
+
+using namespace sm100;
+
+// Device status word: code of the first bounded wait that gave up (0 = none).
+__device__ int g_gemm_status = 0;
+
+struct GemmParams {
+    int M, N, K;
+    int m_tiles, n_tiles, tiles_per_batch, total_tiles;
+    int num_kb;
+    long long ldc;             // elements
+    long long batch_stride_c;  // elements
+    float alpha;
+    void* C;
+};
+
+template <int BN> struct TileCfg {
+    static constexpr int BM = 128;
+    static constexpr int BK = 64;
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (BN == 256) ? 4 : 6;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+    static constexpr uint32_t TMEM_COLS = 2 * BN;
+    static constexpr int THREADS = 192;
+};
+
+constexpr int kGroupM = 16;
+
+__device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& b, int& mb, int& nb) {
+    b = tile / p.tiles_per_batch;
+    const int t = tile - b * p.tiles_per_batch;
+    const int per_group = kGroupM * p.n_tiles;
+    const int group = t / per_group;
+    const int first_m = group * kGroupM;
+    const int gsize = min(p.m_tiles - first_m, kGroupM);
+    const int r = t - group * per_group;
+    mb = first_m + r % gsize;
+    nb = r / gsize;
+}
+
+template <int BN, bool B_KMAJOR, bool OUT_F32>
+__global__ void __launch_bounds__(192, 1) gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                   const __grid_constant__ CUtensorMap tmB,
+                                                                   const GemmParams p) {
+    using Cfg = TileCfg<BN>;
+    constexpr int STAGES = Cfg::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[STAGES];
+    __shared__ __align__(8) uint64_t empty_bar[STAGES];
+    __shared__ __align__(8) uint64_t tfull_bar[2];
+    __shared__ __align__(8) uint64_t tempty_bar[2];
+    __shared__ __align__(8) uint64_t done_bar;
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int abort_sh;
+
+    // 128-byte swizzled tiles need 1024-byte alignment
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    volatile int* abort_flag = &abort_sh;
+    int* status = &g_gemm_status;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull_bar[a], 1);
+            mbar_init(&tempty_bar[a], 128);
+        }
+        mbar_init(&done_bar, 1);
+        abort_sh = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch(&tmA);
+        tma_prefetch(&tmB);
+    }
+    if (warp == 1) tmem_alloc<Cfg::TMEM_COLS>(&tmem_base_sh);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_base_sh;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        int stage = 0;
+        uint32_t phase = 0;
+        long long issued = 0;
+        for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
+            if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+            int b, mb, nb;
+            tile_coords(tile, p, b, mb, nb);
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, status, 1);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                if (lane == 0) {
+                    uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+                    uint8_t* sb = sa + Cfg::A_BYTES;
+                    mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+                    tma_load_3d(sa, &tmA, &full_bar[stage], kb * Cfg::BK, mb * Cfg::BM, b);
+                    if constexpr (B_KMAJOR) {
+                        tma_load_3d(sb, &tmB, &full_bar[stage], kb * Cfg::BK, nb * BN, b);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < BN / 64; ++j)
+                            tma_load_3d(sb + j * (64 * Cfg::BK * 2), &tmB, &full_bar[stage], nb * BN + j * 64,
+                                        kb * Cfg::BK, b);
+                    }
+                }
+                __syncwarp();
+                ++issued;
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        // Drain: the last (up to) STAGES loads must have landed before the CTA
+        // may exit (normally the MMA warp has already consumed them).
+        if (lane == 0) {
+            const long long first = issued > STAGES ? issued - STAGES : 0;
+            for (long long it = first; it < issued; ++it)
+                mbar_wait(&full_bar[it % STAGES], static_cast<uint32_t>((it / STAGES) & 1), abort_flag, status, 2,
+                          200000000ull);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        constexpr uint32_t idesc = idesc_bf16_f32(128, BN, !B_KMAJOR);
+        int stage = 0;
+        uint32_t phase = 0;
+        int local = 0;
+        bool issued_any = false;
+        for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++local) {
+            if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+            const int acc = local & 1;
+            const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, status, 3);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                if (lane == 0) ok = mbar_wait(&full_bar[stage], phase, abort_flag, status, 4);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t a_base = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+                    const uint32_t b_base = a_base + Cfg::A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < Cfg::BK / 16; ++k) {
+                        const uint64_t adesc = sdesc_sw128(a_base + k * 32, 16, 1024);
+                        const uint64_t bdesc = B_KMAJOR ? sdesc_sw128(b_base + k * 32, 16, 1024)
+                                                        : sdesc_sw128(b_base + k * 16 * 128, 64 * Cfg::BK * 2, 1024);
+                        mma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+                    }
+                    mma_commit(&empty_bar[stage]);
+                    issued_any = true;
+                }
+                __syncwarp();
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+            if (lane == 0) mma_commit(&tfull_bar[acc]);
+            __syncwarp();
+        }
+        // every MMA this thread issued must be complete before TMEM is freed
+        if (lane == 0 && issued_any) {
+            mma_commit(&done_bar);
+            mbar_wait(&done_bar, 0, abort_flag, status, 5, 200000000ull);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ epilogue (warps 2-5)
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        int local = 0;
+        for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++local) {
+            if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+            int b, mb, nb;
+            tile_coords(tile, p, b, mb, nb);
+            const int acc = local & 1;
+            const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+            bool ok = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, status, 6);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            const int row = mb * Cfg::BM + q * 32 + lane;
+            const bool row_ok = row < p.M;
+            const long long row_off = static_cast<long long>(b) * p.batch_stride_c + static_cast<long long>(row) * p.ldc;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(acc * BN + c * 32) +
+                                       (static_cast<uint32_t>(q * 32) << 16),
+                                   r);
+                tmem_ld_wait();
+                const int col0 = nb * BN + c * 32;
+                if (!row_ok || col0 >= p.N) continue;
+                if constexpr (OUT_F32) {
+                    float* dst = static_cast<float*>(p.C) + row_off + col0;
+                    if (col0 + 32 <= p.N && (p.ldc & 3) == 0) {
+#pragma unroll
+                        for (int v = 0; v < 8; ++v)
+                            reinterpret_cast<float4*>(dst)[v] =
+                                make_float4(__uint_as_float(r[4 * v]) * p.alpha, __uint_as_float(r[4 * v + 1]) * p.alpha,
+                                            __uint_as_float(r[4 * v + 2]) * p.alpha,
+                                            __uint_as_float(r[4 * v + 3]) * p.alpha);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.N) dst[j] = __uint_as_float(r[j]) * p.alpha;
+                    }
+                } else {
+                    uint16_t* dst = static_cast<uint16_t*>(p.C) + row_off + col0;
+                    if (col0 + 32 <= p.N && (p.ldc & 7) == 0) {
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            uint4 o;
+                            o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * p.alpha, __uint_as_float(r[8 * v + 1]) * p.alpha);
+                            o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * p.alpha, __uint_as_float(r[8 * v + 3]) * p.alpha);
+                            o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * p.alpha, __uint_as_float(r[8 * v + 5]) * p.alpha);
+                            o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * p.alpha, __uint_as_float(r[8 * v + 7]) * p.alpha);
+                            reinterpret_cast<uint4*>(dst)[v] = o;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.N) {
+                                __nv_bfloat16 h = __float2bfloat16_rn(__uint_as_float(r[j]) * p.alpha);
+                                dst[j] = *reinterpret_cast<uint16_t*>(&h);
+                            }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[acc]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc<Cfg::TMEM_COLS>(tmem_base);
+}
+
+// ---------------------------------------------------------------- SIMT GEMM
+
+template <typename T> struct Acc { using type = T; };
+template <> struct Acc<uint16_t> { using type = float; };  // bf16 bits
+
+template <typename T> __device__ __forceinline__ typename Acc<T>::type ld_as_acc(const T* p) { return *p; }
+template <> __device__ __forceinline__ float ld_as_acc<uint16_t>(const uint16_t* p) {
+    return __uint_as_float(static_cast<uint32_t>(*p) << 16);
+}
+
+template <typename T, typename TO> __device__ __forceinline__ void st_from_acc(TO* p, typename Acc<T>::type v, float alpha) {
+    if constexpr (std::is_same_v<TO, uint16_t>) {
+        __nv_bfloat16 h = __float2bfloat16_rn(static_cast<float>(v) * alpha);
+        *p = *reinterpret_cast<uint16_t*>(&h);
+    } else if constexpr (std::is_floating_point_v<TO>) {
+        *p = static_cast<TO>(v * static_cast<typename Acc<T>::type>(alpha));
+    } else {
+        *p = static_cast<TO>(v);
+    }
+}
+
+template <typename T> __device__ __forceinline__ typename Acc<T>::type fma_acc(typename Acc<T>::type a, typename Acc<T>::type b,
+                                                                              typename Acc<T>::type c) {
+    using A = typename Acc<T>::type;
+    if constexpr (std::is_same_v<A, int32_t>)
+        return static_cast<int32_t>(static_cast<uint32_t>(c) + static_cast<uint32_t>(a) * static_cast<uint32_t>(b));
+    else if constexpr (std::is_same_v<A, int64_t>)
+        return static_cast<int64_t>(static_cast<uint64_t>(c) + static_cast<uint64_t>(a) * static_cast<uint64_t>(b));
+    else
+        return fma(a, b, c);
+}
+
+// 64x64 output tile per 256-thread CTA, 4x4 outputs per thread (strided by 16
+// so shared-memory reads are broadcasts / conflict-free), BK = 16.
+template <typename T, typename TO>
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A, const T* __restrict__ B,
+                                                        TO* __restrict__ C, int M, int N, int K, long long sA,
+                                                        long long sB, long long sC, int b_trans, float alpha) {
+    using AT = typename Acc<T>::type;
+    constexpr int BM = 64, BN = 64, BK = 16;
+    __shared__ AT As[BK][BM + 1];
+    __shared__ AT Bs[BK][BN + 1];
+    const int bz = blockIdx.z;
+    A += bz * sA;
+    B += bz * sB;
+    C += bz * sC;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    AT acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = AT(0);
+    for (int k0 = 0; k0 < K; k0 += BK) {
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const int idx = threadIdx.x + l * 256;
+            const int r = idx / BK, k = idx % BK;  // A: row r, col k
+            const int gm = m0 + r, gk = k0 + k;
+            As[k][r] = (gm < M && gk < K) ? ld_as_acc(A + static_cast<long long>(gm) * K + gk) : AT(0);
+            if (!b_trans) {
+                const int kk = idx / BN, n = idx % BN;  // B [K, N]
+                const int gk2 = k0 + kk, gn = n0 + n;
+                Bs[kk][n] = (gk2 < K && gn < N) ? ld_as_acc(B + static_cast<long long>(gk2) * N + gn) : AT(0);
+            } else {
+                const int n = idx / BK, kk = idx % BK;  // B stored [N, K]
+                const int gk2 = k0 + kk, gn = n0 + n;
+                Bs[kk][n] = (gk2 < K && gn < N) ? ld_as_acc(B + static_cast<long long>(gn) * K + gk2) : AT(0);
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < BK; ++k) {
+            AT a[4], bv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = As[k][ty + 16 * i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) bv[j] = Bs[k][tx + 16 * j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fma_acc<T>(a[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int gm = m0 + ty + 16 * i, gn = n0 + tx + 16 * j;
+            if (gm < M && gn < N) st_from_acc<T, TO>(C + static_cast<long long>(gm) * N + gn, acc[i][j], alpha);
+        }
+}
+
+// ---------------------------------------------------------------- host side
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 3-D bf16 tensor map {inner, outer, batch} with 128-byte swizzle.
+static int make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t batch,
+                    uint64_t row_stride, uint64_t batch_stride, uint32_t box_inner, uint32_t box_outer) {
+    auto enc = encode_fn();
+    if (!enc) return fail(cudaErrorNotSupported, "bmm: cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[3] = {inner, outer, batch};
+    cuuint64_t strides[2] = {row_stride * 2, batch_stride * 2};
+    cuuint32_t box[3] = {box_inner, box_outer, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(cudaErrorInvalidValue, "bmm: tensor map encoding failed (CUresult %d)", int(r));
+    return 0;
+}
+
+template <int BN, bool B_KMAJOR, bool OUT_F32>
+static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
+    using Cfg = TileCfg<BN>;
+    auto kern = gemm_bf16_tcgen05_kernel<BN, B_KMAJOR, OUT_F32>;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+        if (e != cudaSuccess) return fail(static_cast<int>(e), "bmm: shared memory attribute: %s", cudaGetErrorString(e));
+        attr_set[dev] = true;
+    }
+    const int grid = p.total_tiles < sm_count() ? p.total_tiles : sm_count();
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(ta, tb, p);
+    return launch_status("bmm(tcgen05)");
+}
+
+template <bool B_KMAJOR, bool OUT_F32>
+static int dispatch_tc_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
+    return bn == 256 ? launch_tc<256, B_KMAJOR, OUT_F32>(ta, tb, p, st) : launch_tc<128, B_KMAJOR, OUT_F32>(ta, tb, p, st);
+}
+
+// bf16 x bf16 -> (bf16 | fp32) on the tensor cores.  Returns 0, an error, or
+// -1 when the shape cannot be expressed with TMA (caller falls back).
+static int bmm_bf16_tc(int dt_out, const void* A, const void* B, void* C, size_t batch, size_t M, size_t K, size_t N,
+                       int b_trans, float alpha, cudaStream_t st) {
+    if (K % 8 != 0 || (!b_trans && N % 8 != 0) || !aligned16(A) || !aligned16(B)) return -1;
+    if (M > (1u << 31) || N > (1u << 31) || K > (1u << 31) || batch > 65535) return -1;
+    const int bn = N > 128 ? 256 : 128;
+    CUtensorMap ta, tb;
+    if (int rc = make_map(&ta, A, K, M, batch, K, M * K, 64, 128)) return rc;
+    if (b_trans) {
+        if (int rc = make_map(&tb, B, K, N, batch, K, N * K, 64, static_cast<uint32_t>(bn))) return rc;
+    } else {
+        if (int rc = make_map(&tb, B, N, K, batch, N, K * N, 64, 64)) return rc;
+    }
+    GemmParams p;
+    p.M = static_cast<int>(M);
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.m_tiles = static_cast<int>((M + 127) / 128);
+    p.n_tiles = static_cast<int>((N + bn - 1) / bn);
+    p.tiles_per_batch = p.m_tiles * p.n_tiles;
+    const long long total = static_cast<long long>(p.tiles_per_batch) * static_cast<long long>(batch);
+    if (total > (1ll << 31) - 1) return -1;
+    p.total_tiles = static_cast<int>(total);
+    p.num_kb = static_cast<int>((K + 63) / 64);
+    p.ldc = static_cast<long long>(N);
+    p.batch_stride_c = static_cast<long long>(M) * static_cast<long long>(N);
+    p.alpha = alpha;
+    p.C = C;
+    const bool f32 = dt_out == DT_F32;
+    if (b_trans) return f32 ? dispatch_tc_bn<true, true>(bn, ta, tb, p, st) : dispatch_tc_bn<true, false>(bn, ta, tb, p, st);
+    return f32 ? dispatch_tc_bn<false, true>(bn, ta, tb, p, st) : dispatch_tc_bn<false, false>(bn, ta, tb, p, st);
+}
+
+template <typename T, typename TO>
+static int launch_simt(const void* A, const void* B, void* C, size_t batch, size_t M, size_t K, size_t N, int b_trans,
+                       float alpha, cudaStream_t st) {
+    if (M > (1u << 30) || N > (1u << 30) || K > (1u << 30) || batch > 65535)
+        return fail(cudaErrorInvalidValue, "matmul: extent too large for the SIMT path");
+    dim3 grid(static_cast<unsigned>((N + 63) / 64), static_cast<unsigned>((M + 63) / 64), static_cast<unsigned>(batch));
+    if (grid.y > 65535) return fail(cudaErrorInvalidValue, "matmul: M too large for the SIMT path");
+    gemm_simt_kernel<T, TO><<<grid, 256, 0, st>>>(static_cast<const T*>(A), static_cast<const T*>(B), static_cast<TO*>(C),
+                                                  static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                                                  static_cast<long long>(M * K), static_cast<long long>(K * N),
+                                                  static_cast<long long>(M * N), b_trans, alpha);
+    return launch_status("matmul(simt)");
+}
+
+}  // namespace bee_b200
+
+using namespace bee_b200;
+
+extern "C" {
+
+int bee_b200_bmm(int dt_in, int dt_out, const void* A, const void* B, void* C, size_t batch, size_t M, size_t K,
+                 size_t N, int b_trans, float alpha, bee_b200_stream_t stream) {
+    if (batch == 0 || M == 0 || N == 0) return ok();
+    if (!A || !B || !C) return fail(cudaErrorInvalidValue, "bmm: null pointer");
+    cudaStream_t st = as_stream(stream);
+    if (dt_in == DT_BF16) {
+        if (dt_out != DT_BF16 && dt_out != DT_F32)
+            return fail(cudaErrorInvalidValue, "bmm: bf16 input needs a BF16 or F32 output, got %d", dt_out);
+        if (K == 0) {
+            cudaError_t e = cudaMemsetAsync(C, 0, batch * M * N * (dt_out == DT_F32 ? 4 : 2), st);
+            return e == cudaSuccess ? ok() : fail(static_cast<int>(e), "bmm: %s", cudaGetErrorString(e));
+        }
+        int rc = bmm_bf16_tc(dt_out, A, B, C, batch, M, K, N, b_trans, alpha, st);
+        if (rc != -1) return rc;
+        return dt_out == DT_F32 ? launch_simt<uint16_t, float>(A, B, C, batch, M, K, N, b_trans, alpha, st)
+                                : launch_simt<uint16_t, uint16_t>(A, B, C, batch, M, K, N, b_trans, alpha, st);
+    }
+    if (dt_out != dt_in) return fail(cudaErrorInvalidValue, "bmm: output dtype must equal input dtype for %d", dt_in);
+    switch (dt_in) {
+    case DT_F32: return launch_simt<float, float>(A, B, C, batch, M, K, N, b_trans, alpha, st);
+    case DT_F64: return launch_simt<double, double>(A, B, C, batch, M, K, N, b_trans, alpha, st);
+    case DT_I32: return launch_simt<int32_t, int32_t>(A, B, C, batch, M, K, N, b_trans, alpha, st);
+    case DT_I64: return launch_simt<int64_t, int64_t>(A, B, C, batch, M, K, N, b_trans, alpha, st);
+    default: return fail(cudaErrorInvalidValue, "bmm: unsupported dtype %d", dt_in);
+    }
+}
+
+int bee_b200_matmul(int dt, const void* A, const void* B, void* C, size_t M, size_t K, size_t N,
+                    bee_b200_stream_t stream) {
+    return bee_b200_bmm(dt, dt, A, B, C, 1, M, K, N, 0, 1.0f, stream);
+}
+
+int bee_b200_device_status(int* out_code) {
+    if (!out_code) return fail(cudaErrorInvalidValue, "device_status: null pointer");
+    int zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(out_code, g_gemm_status, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_gemm_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "device_status: %s", cudaGetErrorString(e));
+    return ok();
+}
+
+}  // extern "C"

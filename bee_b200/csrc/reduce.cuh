@@ -1,0 +1,147 @@
+// Device-side building blocks of the reductions: accumulation functors with
+// the reference's semantics, warp/block reduce, vectorised strided reduce and
+// the one-launch global reduce kernel (per-CTA partials folded by the last CTA).
+#pragma once
+
+#include <cfloat>
+#include <climits>
+
+#include "common.cuh"
+
+namespace bee_b200 {
+
+template <typename T> struct Lim;
+template <> struct Lim<uint8_t> { static __device__ uint8_t lo() { return 0; } static __device__ uint8_t hi() { return 255; } };
+template <> struct Lim<int32_t> { static __device__ int32_t lo() { return INT_MIN; } static __device__ int32_t hi() { return INT_MAX; } };
+template <> struct Lim<int64_t> { static __device__ int64_t lo() { return LLONG_MIN; } static __device__ int64_t hi() { return LLONG_MAX; } };
+template <> struct Lim<float> { static __device__ float lo() { return -FLT_MAX; } static __device__ float hi() { return FLT_MAX; } };
+template <> struct Lim<double> { static __device__ double lo() { return -DBL_MAX; } static __device__ double hi() { return DBL_MAX; } };
+
+// Integer sum/prod go through the unsigned type so that wrap-around is
+// defined behaviour (two's complement, identical bits to the reference).
+template <typename T> struct Wrap { using U = T; };
+template <> struct Wrap<int32_t> { using U = uint32_t; };
+template <> struct Wrap<int64_t> { using U = uint64_t; };
+
+template <int OP, typename T> struct Red {
+    static __device__ __forceinline__ T identity() {
+        if constexpr (OP == RED_SUM) return T(0);
+        else if constexpr (OP == RED_PROD) return T(1);
+        else if constexpr (OP == RED_MIN) return Lim<T>::hi();
+        else return Lim<T>::lo();
+    }
+    static __device__ __forceinline__ T apply(T a, T b) {
+        using U = typename Wrap<T>::U;
+        if constexpr (OP == RED_SUM) return static_cast<T>(static_cast<U>(a) + static_cast<U>(b));
+        else if constexpr (OP == RED_PROD) return static_cast<T>(static_cast<U>(a) * static_cast<U>(b));
+        else if constexpr (OP == RED_MIN) return b < a ? b : a;
+        else return b > a ? b : a;
+    }
+};
+
+template <int OP, typename T> __device__ __forceinline__ T warp_reduce(T v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = Red<OP, T>::apply(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide reduce; the result is valid in every thread.  `smem` holds
+// blockDim.x / 32 entries.
+template <int OP, typename T> __device__ __forceinline__ T block_reduce(T v, T* smem) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    v = warp_reduce<OP>(v);
+    __syncthreads();
+    if (lane == 0) smem[warp] = v;
+    __syncthreads();
+    T r = Red<OP, T>::identity();
+    for (int w = 0; w < nwarps; ++w) r = Red<OP, T>::apply(r, smem[w]);
+    return r;
+}
+
+template <typename T> union V16 {
+    uint4 v;
+    T s[16 / sizeof(T)];
+};
+
+// Folds a 16-byte vector into `acc` lane by lane (fixed order).
+template <int OP, typename T> __device__ __forceinline__ T fold(T acc, uint4 raw) {
+    V16<T> x;
+    x.v = raw;
+#pragma unroll
+    for (int k = 0; k < int(16 / sizeof(T)); ++k) acc = Red<OP, T>::apply(acc, x.s[k]);
+    return acc;
+}
+
+// Reduces src[lo, hi) cooperatively by `nthr` threads (index `tid`); the
+// 16-byte vector path is used when src+lo is 16-byte aligned.
+template <int OP, typename T>
+__device__ __forceinline__ T strided_reduce(const T* __restrict__ src, size_t lo, size_t hi, size_t tid, size_t nthr) {
+    constexpr size_t E = 16 / sizeof(T);
+    T acc = Red<OP, T>::identity();
+    const T* base = src + lo;
+    const size_t len = hi - lo;
+    size_t head = 0;
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
+        const size_t nvec = len / E;
+        const uint4* v = reinterpret_cast<const uint4*>(base);
+        size_t i = tid;
+        constexpr int U = 4;
+        for (; i + (U - 1) * nthr < nvec; i += U * nthr) {
+            uint4 r[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) r[u] = ld_stream_u4(v + i + u * nthr);
+#pragma unroll
+            for (int u = 0; u < U; ++u) acc = fold<OP>(acc, r[u]);
+        }
+        for (; i < nvec; i += nthr) acc = fold<OP>(acc, ld_stream_u4(v + i));
+        head = nvec * E;
+    }
+    for (size_t j = head + tid; j < len; j += nthr) acc = Red<OP, T>::apply(acc, base[j]);
+    return acc;
+}
+
+// ---------------------------------------------------------------- global
+
+struct GlobalScratch {
+    unsigned int ticket;  // number of CTAs that have published their partial
+    unsigned int pad[63];
+    // followed by gridDim.x partials of sizeof(T), 256-byte aligned
+};
+
+template <int OP, typename T>
+__global__ void __launch_bounds__(512) reduce_global_kernel(const T* __restrict__ src, T* __restrict__ dst, size_t n,
+                                                            GlobalScratch* scratch) {
+    __shared__ T smem[32];
+    __shared__ bool last;
+    T* partials = reinterpret_cast<T*>(scratch + 1);
+    const size_t nthr = static_cast<size_t>(gridDim.x) * blockDim.x;
+    // CTA b owns the contiguous chunk [b*chunk, (b+1)*chunk) so that the
+    // partials are in element order; chunks are multiples of 16 elements.
+    const size_t chunk = ((n + gridDim.x - 1) / gridDim.x + 15) & ~size_t(15);
+    const size_t lo = min(n, static_cast<size_t>(blockIdx.x) * chunk);
+    const size_t hi = min(n, lo + chunk);
+    (void)nthr;
+    T v = strided_reduce<OP>(src, lo, hi, threadIdx.x, blockDim.x);
+    v = block_reduce<OP>(v, smem);
+    if (threadIdx.x == 0) {
+        partials[blockIdx.x] = v;
+        __threadfence();
+        unsigned int t = atomicAdd(&scratch->ticket, 1u);
+        last = (t == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // Last CTA: fold the partials in index order (thread-strided, then the
+    // block reduce), then re-arm the ticket for the next call.
+    T r = Red<OP, T>::identity();
+    for (unsigned i = threadIdx.x; i < gridDim.x; i += blockDim.x)
+        r = Red<OP, T>::apply(r, *reinterpret_cast<volatile T*>(partials + i));
+    r = block_reduce<OP>(r, smem);
+    if (threadIdx.x == 0) {
+        *dst = r;
+        scratch->ticket = 0;
+    }
+}
+
+}  // namespace bee_b200

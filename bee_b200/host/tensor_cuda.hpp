@@ -1,0 +1,68 @@
+// C++ host bridge over the bee_b200 C ABI: the functions of the reference's
+// bee::tensor::cuda boundary (Bee/Tensor/Cuda/Backend.hpp:20-84) with the same
+// names, argument meaning and error behaviour, plus the operators the
+// reference lacks (softmax, RMSNorm, RoPE, batched matmul).
+//
+// Semantics mirrored from the reference (Bee/CUDA/Api.cpp):
+//   * every call is synchronous: work is issued on the per-thread default
+//     stream and the stream is synchronised before returning (:45-48, :121);
+//   * size-0 elementwise / cast / scale / matmul calls succeed without work,
+//     size-0 reduces fail (:213-214, :237-238, :245-246);
+//   * a CUDA failure becomes Error{Recoverable, errc = cudaError_t} with the
+//     message "<op> 失败: <error name> (<error string>)" (:59-64).
+// Result<T> is std::expected<T, Error>, the reference's own alias
+// (Bee/Base/Diagnostics/Error.hpp:79); Error carries the fields the Tensor
+// layer reads (message, errc, severity).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <expected>
+#include <string>
+
+namespace bee_b200::tensor_cuda {
+
+enum class Severity : std::uint8_t { Recoverable, Transient, Fatal, Bug };
+
+struct Error {
+    std::string message;
+    int errc = 0;
+    Severity severity = Severity::Recoverable;
+    std::string detail;  // bee_b200_last_error() at the time of failure
+};
+
+template <typename T> using Result = std::expected<T, Error>;
+
+// ---- memory (Backend.hpp:20-46, 84)
+[[nodiscard]] auto allocate(std::size_t nbytes, std::size_t alignment) -> Result<void*>;
+auto deallocate(void* p, std::size_t nbytes, std::size_t alignment) -> void;
+[[nodiscard]] auto memcpy_h2d(void* dst, const void* src, std::size_t nbytes) -> Result<void>;
+[[nodiscard]] auto memcpy_d2h(void* dst, const void* src, std::size_t nbytes) -> Result<void>;
+[[nodiscard]] auto memcpy_d2d(void* dst, const void* src, std::size_t nbytes) -> Result<void>;
+[[nodiscard]] auto memset(void* ptr, int value, std::size_t nbytes) -> Result<void>;
+[[nodiscard]] auto synchronize() -> Result<void>;
+
+// ---- operators on the path (Backend.hpp:51-70)
+[[nodiscard]] auto ew_binary(int op, int dt, const void* a, const void* b, void* out, std::size_t n) -> Result<void>;
+[[nodiscard]] auto ew_unary(int op, int dt, const void* src, void* dst, std::size_t n) -> Result<void>;
+[[nodiscard]] auto ew_cast(int src_dt, const void* src, int dst_dt, void* dst, std::size_t n) -> Result<void>;
+[[nodiscard]] auto reduce_global(int op, int dt, const void* src, void* dst, std::size_t n) -> Result<void>;
+[[nodiscard]] auto reduce_axis(int op, int dt, const void* src, void* dst, std::size_t outer, std::size_t axis,
+                               std::size_t inner) -> Result<void>;
+[[nodiscard]] auto scale_fp(int dt, void* buf, double factor, std::size_t n) -> Result<void>;
+[[nodiscard]] auto matmul(int dt, const void* A, const void* B, void* C, std::size_t M, std::size_t K, std::size_t N)
+    -> Result<void>;
+
+// ---- new operators
+[[nodiscard]] auto bmm(int dt_in, int dt_out, const void* A, const void* B, void* C, std::size_t batch, std::size_t M,
+                       std::size_t K, std::size_t N, bool b_transposed, float alpha) -> Result<void>;
+[[nodiscard]] auto softmax_rows(int dt, const void* src, void* dst, std::size_t rows, std::size_t cols) -> Result<void>;
+[[nodiscard]] auto rms_norm_rows(int dt, const void* x, const void* w, void* y, std::size_t rows, std::size_t cols,
+                                 float eps) -> Result<void>;
+[[nodiscard]] auto rope(int dt, const void* x, void* y, std::size_t rows, std::size_t seq, std::size_t heads,
+                        std::size_t head_dim, double theta, std::size_t pos_offset) -> Result<void>;
+[[nodiscard]] auto rms_norm_rope(int dt, const void* x, const void* w, void* y, std::size_t rows, std::size_t seq,
+                                 std::size_t heads, std::size_t head_dim, float eps, double theta,
+                                 std::size_t pos_offset) -> Result<void>;
+
+}  // namespace bee_b200::tensor_cuda

@@ -61,72 +61,73 @@ def load_peaks():
 # ---------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """Samples nvidia-smi clocks / throttle reasons while the timed region runs."""
+    """Samples SM clock and throttle reasons through NVML every few ms while the
+    timed region runs (nvidia-smi's 200 ms period is longer than the region)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-
-    def __init__(self, index: str):
-        self.index = index
-        self.proc = None
-        self.lines = []
-        self.thread = None
+    def __init__(self, bus_id: str, period_s: float = 0.002):
+        self.bus_id = bus_id
+        self.period = period_s
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+        self.error = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml as nv
+            nv.nvmlInit()
+            self._nvml = nv
+            self._h = nv.nvmlDeviceGetHandleByPciBusId(self.bus_id)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self._h, nv.NVML_CLOCK_SM)
+            self._sample()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        except Exception as e:  # NVML missing: report no samples rather than fail the bench
+            self.error = f"{type(e).__name__}: {e}"
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _sample(self):
+        nv = self._nvml
+        mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+        reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        self.samples.append((mhz, reasons))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                break
+            time.sleep(self.period)
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.thread.join(timeout=2)
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+        try:
+            if self._nvml is not None:
+                self._sample()
+                self._nvml.nvmlShutdown()
+        except Exception:
+            pass
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        bits = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
+        reasons = sorted({name for _, r in self.samples for name, b in bits.items() if r & b})
+        out = {"sm_mhz": statistics.median([m for m, _ in self.samples]) if self.samples else None,
+               "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples), "source": "nvml"}
+        if self.error:
+            out["error"] = self.error
+        return out
 
 
 def smi_id(dev) -> str:
-    """nvidia-smi identifier (PCI bus id) of a torch device, robust to CUDA_VISIBLE_DEVICES."""
+    """PCI bus id of a torch device (NVML handle key), robust to CUDA_VISIBLE_DEVICES."""
     import torch
     p = torch.cuda.get_device_properties(dev)
-    try:
-        return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
-    except AttributeError:
-        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-        idx = dev.index or 0
-        return vis.split(",")[idx] if vis else str(idx)
+    return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
 
 
 # ---------------------------------------------------------------- distributed plumbing
@@ -434,7 +435,7 @@ def run_reference(args, d: Dist):
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["sweep"], default="sweep")

@@ -140,6 +140,32 @@ BEE_B200_API int bee_b200_rms_norm_rope(int dt, const void* x, const void* w, vo
                            size_t heads, size_t head_dim, float eps, double theta, size_t pos_offset,
                            bee_b200_stream_t stream);
 
+/* ------------------------------------------------------------------ matmul */
+
+/* C[M,N] = A[M,K] . B[K,N], row-major contiguous, same dtype.
+ * BF16: tcgen05 tensor cores with fp32 accumulation and a bf16 (RNE) result;
+ * F32 / F64 / I32 / I64: tiled SIMT kernel accumulating in the element type
+ * (I32/I64 wrap).  Replaces ops_matmul (Bee/CUDA/Ops/OpsBridge.hpp:38) behind
+ * tensor::cuda::matmul (Bee/Tensor/Cuda/Backend.hpp:70). */
+BEE_B200_API int bee_b200_matmul(int dt, const void* A, const void* B, void* C, size_t M, size_t K, size_t N,
+                                 bee_b200_stream_t stream);
+
+/* Batched C[b] = alpha * A[b] . op(B[b]) over `batch` contiguous matrices:
+ * A [batch, M, K]; B [batch, K, N], or [batch, N, K] when b_trans != 0 (so
+ * Q.K^T reads K as stored); C [batch, M, N].  dt_in BF16 with dt_out BF16 or
+ * F32 runs on the tensor cores (TMA needs K % 8 == 0, N % 8 == 0 unless
+ * b_trans, 16-byte aligned A and B; other shapes use the SIMT kernel); other
+ * dtypes need dt_out == dt_in.  New: the reference matmul is 2-D only
+ * (Bee/Tensor/Ops/Matmul.cpp:63-64). */
+BEE_B200_API int bee_b200_bmm(int dt_in, int dt_out, const void* A, const void* B, void* C, size_t batch, size_t M,
+                              size_t K, size_t N, int b_trans, float alpha, bee_b200_stream_t stream);
+
+/* Reads and clears the device status word of the tensor-core kernels on the
+ * current device: 0, or the code of the first bounded pipeline wait that gave
+ * up (the kernel then abandons its remaining tiles instead of hanging).
+ * Synchronous. */
+BEE_B200_API int bee_b200_device_status(int* out_code);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,6 +15,7 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 /* bf16 bits -> fp32 (exact). */
@@ -48,12 +49,17 @@ void oracle_cast_bf16_f32(const uint16_t* x, float* y, int64_t n) {
 /* C = A.B, row-major, fp32 accumulation in k order: the scalar reference GEMM
  * of Tests/Tensor/GemmTests.cpp:31-40 (i-j-k with a T accumulator). */
 void oracle_matmul_f32(const float* A, const float* B, float* C, int64_t M, int64_t K, int64_t N) {
-    for (int64_t i = 0; i < M; ++i)
-        for (int64_t j = 0; j < N; ++j) {
-            float acc = 0.0f;
-            for (int64_t k = 0; k < K; ++k) acc += A[i * K + k] * B[k * N + j];
-            C[i * N + j] = acc;
+    /* i-k-j traversal with a row accumulator: each C[i][j] still sums its
+     * products in k order, exactly as the i-j-k loop, but B is read by rows. */
+    for (int64_t i = 0; i < M; ++i) {
+        float* c = C + i * N;
+        for (int64_t j = 0; j < N; ++j) c[j] = 0.0f;
+        for (int64_t k = 0; k < K; ++k) {
+            const float a = A[i * K + k];
+            const float* b = B + k * N;
+            for (int64_t j = 0; j < N; ++j) c[j] = c[j] + a * b[j];
         }
+    }
 }
 
 /* Batched bf16 GEMM with fp32 math: C[b] = alpha * A[b] . op(B[b]), where
@@ -64,20 +70,27 @@ void oracle_matmul_f32(const float* A, const float* B, float* C, int64_t M, int6
  * bf16-rounded inputs.) */
 void oracle_bmm_bf16(const uint16_t* A, const uint16_t* B, float* C, int64_t batch, int64_t M, int64_t K, int64_t N,
                      int b_trans, float alpha) {
+    double* row = (double*)malloc((size_t)N * sizeof(double));
+    float* bf = (float*)malloc((size_t)K * (size_t)N * sizeof(float));
     for (int64_t b = 0; b < batch; ++b) {
         const uint16_t* a = A + b * M * K;
         const uint16_t* bb = B + b * K * N;
         float* c = C + b * M * N;
-        for (int64_t i = 0; i < M; ++i)
-            for (int64_t j = 0; j < N; ++j) {
-                double acc = 0.0;
-                for (int64_t k = 0; k < K; ++k) {
-                    const float bv = b_trans ? bf16_to_f32(bb[j * K + k]) : bf16_to_f32(bb[k * N + j]);
-                    acc += (double)(bf16_to_f32(a[i * K + k]) * bv);
-                }
-                c[i * N + j] = (float)(acc * (double)alpha);
+        /* B as fp32 in [K, N] order (transposing when stored [N, K]) */
+        for (int64_t k = 0; k < K; ++k)
+            for (int64_t j = 0; j < N; ++j) bf[k * N + j] = bf16_to_f32(b_trans ? bb[j * K + k] : bb[k * N + j]);
+        for (int64_t i = 0; i < M; ++i) {
+            for (int64_t j = 0; j < N; ++j) row[j] = 0.0;
+            for (int64_t k = 0; k < K; ++k) {
+                const float av = bf16_to_f32(a[i * K + k]);
+                const float* br = bf + k * N;
+                for (int64_t j = 0; j < N; ++j) row[j] += (double)(av * br[j]);
             }
+            for (int64_t j = 0; j < N; ++j) c[i * N + j] = (float)(row[j] * (double)alpha);
+        }
     }
+    free(bf);
+    free(row);
 }
 
 /* Row reduce of [rows, cols] fp32 (op 0 sum, 1 min, 2 max), sequential fp32
