@@ -49,6 +49,7 @@ SIGNATURES = {
     "bee_b200_ew_cast": [_i, _vp, _i, _vp, _sz, _vp],
     "bee_b200_scale_fp": [_i, _vp, _d, _sz, _vp],
     "bee_b200_reduce_global": [_i, _i, _vp, _vp, _sz, _vp],
+    "bee_b200_reduce_global_noalloc": [_i, _i, _vp, _vp, _sz, _vp],
     "bee_b200_reduce_axis": [_i, _i, _vp, _vp, _sz, _sz, _sz, _vp],
     "bee_b200_softmax_rows": [_i, _vp, _vp, _sz, _sz, _vp],
     "bee_b200_rms_norm_rows": [_i, _vp, _vp, _vp, _sz, _sz, _f, _vp],

@@ -104,6 +104,23 @@ BEE_B200_API int bee_b200_scale_fp(int dt, void* buf, double factor, size_t n, b
 BEE_B200_API int bee_b200_reduce_global(int op, int dt, const void* src, void* dst, size_t n,
                            bee_b200_stream_t stream);
 
+/* bee_b200_reduce_global without any allocation — no counterpart in the
+ * reference (its global reduce always allocates, Bee/CUDA/Ops/Reduce.cu:208).
+ * For callers that must not allocate device memory during the call: error
+ * handling or diagnostics after an out-of-memory failure, a host runtime that
+ * owns all device memory through its own allocator, or a latency-critical loop
+ * that cannot let the stream-ordered pool grow.  Per-block scratch lives in a
+ * fixed 64 KiB array compiled into the library, which every GPU that loads the
+ * library holds until the process exits; a call whose partials would not fit
+ * (more than 8160 blocks of 8-byte partials) is rejected with
+ * cudaErrorInvalidValue and a message.  The first call on each device looks up
+ * the array's device address (one-time set-up per device): make it before any
+ * stream capture.  All calls share the array: calls whose kernels overlap on
+ * the GPU (different streams at once) race, so keep them on one stream.
+ * Same arguments, dtypes, ops and results as bee_b200_reduce_global. */
+BEE_B200_API int bee_b200_reduce_global_noalloc(int op, int dt, const void* src, void* dst, size_t n,
+                                                bee_b200_stream_t stream);
+
 /* [outer, axis, inner] -> [outer, inner] (same dtype set as reduce_global;
  * F32 sums accumulate in fp32).  Replaces ops_reduce_axis
  * (Bee/CUDA/Ops/OpsBridge.hpp:32) behind tensor::cuda::reduce_axis
