@@ -40,6 +40,12 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Number of SMs of the current device (cached per device ordinal).
 int sm_count();
 
+// Stream-ordered allocation from the current device's default memory pool,
+// whose release threshold is raised to the maximum on first use (as the
+// reference's MemoryPool::get_default does, Bee/CUDA/Mem/MemoryPool.hpp:33-49)
+// so freed blocks stay reserved and later allocations are sub-allocations.
+cudaError_t pool_malloc(void** ptr, size_t bytes, cudaStream_t st);
+
 inline cudaStream_t as_stream(bee_b200_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // ---------------------------------------------------------------- device side

@@ -68,7 +68,7 @@ static int run_global(const void* src, void* dst, size_t n, cudaStream_t st) {
     if (need < grid) grid = static_cast<unsigned>(need < 1 ? 1 : need);
     const size_t bytes = sizeof(GlobalScratch) + static_cast<size_t>(grid) * sizeof(T);
     void* scratch = nullptr;
-    cudaError_t e = cudaMallocAsync(&scratch, bytes, st);
+    cudaError_t e = pool_malloc(&scratch, bytes, st);
     if (e != cudaSuccess) return fail(static_cast<int>(e), "reduce_global: scratch allocation: %s", cudaGetErrorString(e));
     e = cudaMemsetAsync(scratch, 0, sizeof(GlobalScratch), st);
     if (e == cudaSuccess) {

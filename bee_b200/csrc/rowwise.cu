@@ -320,14 +320,21 @@ using namespace bee_b200;
 
 extern "C" {
 
-int bee_b200_softmax_rows(int dt, const void* src, void* dst, size_t rows, size_t cols, bee_b200_stream_t stream) {
+int bee_b200_softmax_rows_to(int src_dt, const void* src, int dst_dt, void* dst, size_t rows, size_t cols,
+                             bee_b200_stream_t stream) {
     if (rows == 0) return ok();
     if (cols == 0) return fail(cudaErrorInvalidValue, "softmax_rows: zero columns");
     if (!src || !dst) return fail(cudaErrorInvalidValue, "softmax_rows: null pointer");
     cudaStream_t st = as_stream(stream);
-    if (dt == DT_F32) return launch_softmax<float, float>(src, dst, rows, cols, st);
-    if (dt == DT_BF16) return launch_softmax<uint16_t, uint16_t>(src, dst, rows, cols, st);
-    return fail(cudaErrorInvalidValue, "softmax_rows: unsupported dtype %d", dt);
+    if (src_dt == DT_F32 && dst_dt == DT_F32) return launch_softmax<float, float>(src, dst, rows, cols, st);
+    if (src_dt == DT_BF16 && dst_dt == DT_BF16) return launch_softmax<uint16_t, uint16_t>(src, dst, rows, cols, st);
+    if (src_dt == DT_F32 && dst_dt == DT_BF16) return launch_softmax<float, uint16_t>(src, dst, rows, cols, st);
+    if (src_dt == DT_BF16 && dst_dt == DT_F32) return launch_softmax<uint16_t, float>(src, dst, rows, cols, st);
+    return fail(cudaErrorInvalidValue, "softmax_rows: unsupported dtypes %d -> %d", src_dt, dst_dt);
+}
+
+int bee_b200_softmax_rows(int dt, const void* src, void* dst, size_t rows, size_t cols, bee_b200_stream_t stream) {
+    return bee_b200_softmax_rows_to(dt, src, dt, dst, rows, cols, stream);
 }
 
 int bee_b200_rms_norm_rows(int dt, const void* x, const void* w, void* y, size_t rows, size_t cols, float eps,

@@ -47,6 +47,30 @@ int sm_count() {
     return cached[dev];
 }
 
+cudaError_t pool_malloc(void** ptr, size_t bytes, cudaStream_t st) {
+    static std::mutex mu;
+    static cudaMemPool_t pools[64] = {nullptr};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    cudaMemPool_t pool;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!pools[dev]) {
+            cudaMemPool_t p = nullptr;
+            e = cudaDeviceGetDefaultMemPool(&p, dev);
+            if (e != cudaSuccess) return e;
+            uint64_t keep = ~uint64_t{0};
+            e = cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep);
+            if (e != cudaSuccess) return e;
+            pools[dev] = p;
+        }
+        pool = pools[dev];
+    }
+    return cudaMallocFromPoolAsync(ptr, bytes, pool, st);
+}
+
 }  // namespace bee_b200
 
 using namespace bee_b200;
@@ -65,7 +89,7 @@ int bee_b200_allocate(void** out_ptr, size_t nbytes, size_t alignment, bee_b200_
     if (alignment > 256 || (alignment & (alignment - 1)) != 0)
         return fail(cudaErrorInvalidValue, "allocate: alignment %zu unsupported (power of two <= 256)", alignment);
     if (nbytes == 0) return ok();
-    cudaError_t e = cudaMallocAsync(out_ptr, nbytes, as_stream(stream));
+    cudaError_t e = pool_malloc(out_ptr, nbytes, as_stream(stream));
     if (e != cudaSuccess) return fail(static_cast<int>(e), "allocate(%zu): %s", nbytes, cudaGetErrorString(e));
     return ok();
 }

@@ -64,7 +64,8 @@ class ClockSampler:
     """Samples SM clock and throttle reasons through NVML every few ms while the
     timed region runs (nvidia-smi's 200 ms period is longer than the region)."""
 
-    def __init__(self, bus_id: str, period_s: float = 0.002):
+    def __init__(self, bus_id: str, period_s: float = 0.002, enabled: bool = True):
+        self.enabled = enabled
         self.bus_id = bus_id
         self.period = period_s
         self.samples = []
@@ -75,6 +76,9 @@ class ClockSampler:
         self.error = None
 
     def __enter__(self):
+        if not self.enabled:
+            self.error = "disabled (--no-clocks)"
+            return self
         try:
             import pynvml as nv
             nv.nvmlInit()
@@ -258,7 +262,7 @@ def run_ours(args, d: Dist):
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     d.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(smi_id(dev)) as clk:
+    with ClockSampler(smi_id(dev), enabled=not args.no_clocks) as clk:
         t0.record(stream)
         for k in range(args.steps):
             step(per_step_events[k])
@@ -288,6 +292,7 @@ def run_ours(args, d: Dist):
                       [o_add, o_mul, o_bf, o_rsum, o_rmax, o_sm, o_isum], [dx, dy, dxi])
 
     clocks = clk.summary()
+    extra = None if args.no_extras else run_extras(args, d, dev, stream, peaks)
     out = None
     if d.rank == 0:
         ops_json = {n: {"ms": round(per_op_ms[n], 4), "GB/s": round(OP_BYTES[n] / (per_op_ms[n] / 1e3) / 1e9, 1),
@@ -311,7 +316,138 @@ def run_ours(args, d: Dist):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "e2e": e2e,
+            "extra": extra,
         }
+    return out
+
+
+def run_extras(args, d, dev, stream, peaks):
+    """The other configs of the path, each timed on its own (CUDA events on the
+    launching stream, max over ranks) after the headline sweep:
+
+    * gemm_bf16_8192: C = A.B, M = N = K = 8192, bf16 in, fp32 accumulate, bf16 out;
+      B sharded by output columns (each GPU owns an [8192, 8192] column block of a
+      [8192, 8192*N] B, weak scaling, no collective);
+    * gemm_bf16_8192_splitk: the same single 8192^3 product with K sharded over the
+      GPUs (strong scaling), fp32 partials summed by an NCCL all-reduce, then cast
+      to bf16;
+    * rms_norm_rope_bf16: RMSNorm (eps 1e-6) + RoPE (theta 1e4, rotate-half) of X
+      [16 x 2048, 4096] bf16 viewed [16, 2048, 32, 128], fused, per GPU (weak);
+    * attention_bf16: S = Q.K^T/sqrt(128) (fp32), P = softmax(S) (bf16),
+      O = P.V for 32 heads x [2048, 128] per GPU (heads sharded, weak);
+    * gemm_f32_1024: the fp32 parity config, 1024^3.
+    """
+    import torch
+    from bee_b200 import _capi
+    from bee_b200._capi import call
+    from bee_b200.shard import shard_range
+    st = stream.cuda_stream
+    steps = max(3, min(args.steps, 20))
+    warm = 3
+    g = torch.Generator(device=dev).manual_seed(4321 + d.rank)
+    out = {}
+
+    def timed(fn):
+        for _ in range(warm):
+            fn()
+        d.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        stream.synchronize()
+        return d.max(e0.elapsed_time(e1)) / steps
+
+    def status_ok():
+        import ctypes
+        c = ctypes.c_int(-1)
+        call("bee_b200_device_status", ctypes.byref(c))
+        return c.value == 0
+
+    with torch.cuda.stream(stream):
+        n = 8192
+        std = (1.0 / np.sqrt(n)) ** 0.5  # N(0, variance 1/sqrt(8192))
+        a = (torch.randn(n, n, device=dev, generator=g) * std).to(torch.bfloat16)
+        b = (torch.randn(n, n, device=dev, generator=g) * std).to(torch.bfloat16)
+        c = torch.empty(n, n, device=dev, dtype=torch.bfloat16)
+        flop = 2.0 * n ** 3
+        ms = timed(lambda: call("bee_b200_bmm", _capi.BF16, _capi.BF16, a.data_ptr(), b.data_ptr(), c.data_ptr(),
+                                1, n, n, n, 0, 1.0, st))
+        tf = d.world * flop / (ms / 1e3) / 1e12
+        out["gemm_bf16_8192"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
+                                 "frac_of_measured_bf16_burst": round(tf / d.world / peaks["bf16_tflops"], 3),
+                                 "frac_of_measured_bf16_sustained": round(tf / d.world / peaks["bf16_tflops_sustained"], 3),
+                                 "frac_of_spec_2250": round(tf / d.world / 2250.0, 3),
+                                 "scaling": "weak (column shards)", "status_ok": status_ok()}
+
+        # split-K: rank r multiplies A[:, K_r] by B[K_r, :]
+        klo, khi = shard_range(n, d.world, d.rank)
+        kr = khi - klo
+        ak = a[:, klo:khi].contiguous()
+        bk = b[klo:khi].contiguous()
+        part = torch.empty(n, n, device=dev, dtype=torch.float32)
+
+        def splitk():
+            call("bee_b200_bmm", _capi.BF16, _capi.F32, ak.data_ptr(), bk.data_ptr(), part.data_ptr(), 1, n, kr, n,
+                 0, 1.0, st)
+            if d.pg is not None:
+                import torch.distributed as dist
+                dist.all_reduce(part, op=dist.ReduceOp.SUM)
+            call("bee_b200_ew_cast", _capi.F32, part.data_ptr(), _capi.BF16, c.data_ptr(), n * n, st)
+        ms = timed(splitk)
+        tf = flop / (ms / 1e3) / 1e12
+        out["gemm_bf16_8192_splitk"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
+                                        "scaling": "strong (K sharded, NCCL all-reduce of fp32 partials)",
+                                        "allreduce_bytes_per_gpu": n * n * 4 if d.world > 1 else 0}
+        del a, b, c, ak, bk, part
+
+        rows, cols, seq, heads, hd = 16 * 2048, 4096, 2048, 32, 128
+        x = torch.randn(rows, cols, device=dev, generator=g).to(torch.bfloat16)
+        w = (1 + 0.02 * torch.randn(cols, device=dev, generator=g)).to(torch.bfloat16)
+        y = torch.empty_like(x)
+        ms = timed(lambda: call("bee_b200_rms_norm_rope", _capi.BF16, x.data_ptr(), w.data_ptr(), y.data_ptr(), rows,
+                                seq, heads, hd, 1e-6, 10000.0, 0, st))
+        nbytes = 2 * rows * cols * 2 + cols * 2
+        gbs = d.world * nbytes / (ms / 1e3) / 1e9
+        out["rms_norm_rope_bf16"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                     "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                     "bytes_per_gpu": nbytes, "scaling": "weak (rows sharded)"}
+        del x, w, y
+
+        h, s_, dh = 32, 2048, 128
+        q = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
+        k = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
+        v = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
+        S = torch.empty(h, s_, s_, device=dev, dtype=torch.float32)
+        P = torch.empty(h, s_, s_, device=dev, dtype=torch.bfloat16)
+        o = torch.empty(h, s_, dh, device=dev, dtype=torch.bfloat16)
+        scale = 1.0 / np.sqrt(dh)
+
+        def attention():
+            call("bee_b200_bmm", _capi.BF16, _capi.F32, q.data_ptr(), k.data_ptr(), S.data_ptr(), h, s_, dh, s_, 1,
+                 scale, st)
+            call("bee_b200_softmax_rows_to", _capi.F32, S.data_ptr(), _capi.BF16, P.data_ptr(), h * s_, s_, st)
+            call("bee_b200_bmm", _capi.BF16, _capi.BF16, P.data_ptr(), v.data_ptr(), o.data_ptr(), h, s_, s_, dh, 0,
+                 1.0, st)
+        ms = timed(attention)
+        aflop = 2.0 * 2 * h * s_ * s_ * dh
+        tf = d.world * aflop / (ms / 1e3) / 1e12
+        out["attention_bf16"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
+                                 "frac_of_measured_bf16_burst": round(tf / d.world / peaks["bf16_tflops"], 3),
+                                 "kernels": "bmm (QK^T, fp32 out) -> softmax fp32->bf16 -> bmm (PV)",
+                                 "scaling": "weak (heads sharded)", "status_ok": status_ok()}
+        del q, k, v, S, P, o
+
+        a32 = torch.rand(1024, 1024, device=dev, generator=g) * 2 - 1
+        b32 = torch.rand(1024, 1024, device=dev, generator=g) * 2 - 1
+        c32 = torch.empty_like(a32)
+        ms = timed(lambda: call("bee_b200_matmul", _capi.F32, a32.data_ptr(), b32.data_ptr(), c32.data_ptr(), 1024,
+                                1024, 1024, st))
+        out["gemm_f32_1024"] = {"ms": round(ms, 4), "TFLOP/s": round(2.0 * 1024 ** 3 / (ms / 1e3) / 1e12, 2),
+                                "unit": "TFLOP/s (per GPU)", "path": "SIMT fp32 (parity config, rel tol 1e-4)"}
+    stream.synchronize()
     return out
 
 
@@ -442,6 +578,8 @@ def main(argv=None):
     ap.add_argument("--ref-rows", type=int, default=2048, help="rows per CPU-baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the GEMM / RMSNorm+RoPE / attention configs")
+    ap.add_argument("--no-clocks", action="store_true", help="do not sample SM clocks during the timed region")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

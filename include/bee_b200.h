@@ -139,6 +139,11 @@ BEE_B200_API int bee_b200_reduce_axis(int op, int dt, const void* src, void* dst
 BEE_B200_API int bee_b200_softmax_rows(int dt, const void* src, void* dst, size_t rows, size_t cols,
                           bee_b200_stream_t stream);
 
+/* Softmax with a different output dtype (F32 or BF16 each side), e.g. fp32
+ * attention scores -> bf16 probabilities in one pass; math in fp32. */
+BEE_B200_API int bee_b200_softmax_rows_to(int src_dt, const void* src, int dst_dt, void* dst, size_t rows,
+                                          size_t cols, bee_b200_stream_t stream);
+
 /* y = x / sqrt(mean(x^2) + eps) * w over each row of [rows, cols]; w has
  * cols elements.  dt in {F32, BF16}; math in fp32. */
 BEE_B200_API int bee_b200_rms_norm_rows(int dt, const void* x, const void* w, void* y, size_t rows, size_t cols,
