@@ -13,19 +13,24 @@
 // (Bee/Tensor/Cpu/ReduceCpu.hpp:177-290): accumulate in the element type
 // (integer sums and products wrap), min/max by comparison, identities
 // 0 / 1 / numeric max / numeric lowest.
+#include <mutex>
+#include <vector>
+
 #include "reduce.cuh"
 
 namespace bee_b200 {
 
 // ---------------------------------------------------------------- axis
 
-// One CTA per row of length `axis` (inner == 1).
+// One 256-thread CTA per row of length `axis` (inner == 1), launched one CTA
+// per row so that the rows in flight on the GPU form a contiguous window of
+// memory (better DRAM locality than a grid-stride over rows).
 template <int OP, typename T>
-__global__ void __launch_bounds__(512) reduce_rows_cta_kernel(const T* __restrict__ src, T* __restrict__ dst,
+__global__ void __launch_bounds__(256) reduce_rows_cta_kernel(const T* __restrict__ src, T* __restrict__ dst,
                                                               size_t rows, size_t axis) {
     __shared__ T smem[32];
     for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
-        T v = strided_reduce<OP>(src + r * axis, 0, axis, threadIdx.x, blockDim.x);
+        T v = strided_reduce<OP, T, 8>(src + r * axis, 0, axis, threadIdx.x, blockDim.x);
         v = block_reduce<OP>(v, smem);
         if (threadIdx.x == 0) dst[r] = v;
     }
@@ -60,20 +65,65 @@ __global__ void __launch_bounds__(256) reduce_inner_kernel(const T* __restrict__
     }
 }
 
+// Scratch of the global reduce: one 16 KiB block (ticket + up to 2016
+// partials of 8 bytes) per (device, stream), taken from the stream-ordered
+// pool on a stream's first reduce, ticket zeroed once, and kept for the life
+// of the process; the kernel re-arms the ticket itself, so later calls on the
+// stream are a single launch.  Streams are keyed by cudaStreamGetId, which is
+// never reused, so a destroyed stream's block is never handed to another
+// stream.  During stream capture (and past 256 streams on one device) the call
+// instead allocates, zeroes and frees a block around the launch, stream-ordered.
+constexpr size_t kStreamScratchBytes = 16 * 1024;
+
+struct StreamScratch {
+    unsigned long long id;
+    void* ptr;
+};
+
+static int stream_scratch(cudaStream_t st, void** out) {
+    static std::mutex mu;
+    static std::vector<StreamScratch> table[64];
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return 1;
+    unsigned long long id = 0;
+    int dev = 0;
+    if (cudaStreamGetId(st, &id) != cudaSuccess || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+    std::lock_guard<std::mutex> lock(mu);
+    for (const StreamScratch& e : table[dev])
+        if (e.id == id) {
+            *out = e.ptr;
+            return 0;
+        }
+    if (table[dev].size() >= 256) return 1;
+    void* p = nullptr;
+    if (pool_malloc(&p, kStreamScratchBytes, st) != cudaSuccess) return 1;
+    if (cudaMemsetAsync(p, 0, sizeof(GlobalScratch), st) != cudaSuccess) {
+        cudaFreeAsync(p, st);
+        return 1;
+    }
+    table[dev].push_back({id, p});
+    *out = p;
+    return 0;
+}
+
 template <int OP, typename T>
 static int run_global(const void* src, void* dst, size_t n, cudaStream_t st) {
-    unsigned grid = static_cast<unsigned>(sm_count()) * 2;
-    const size_t per_cta = 512 * (16 / sizeof(T)) * 4;  // one unrolled sweep of a 512-thread CTA
-    size_t need = (n + per_cta - 1) / per_cta;
-    if (need < grid) grid = static_cast<unsigned>(need < 1 ? 1 : need);
+    const unsigned grid = global_grid<T>(n, sm_count());
     const size_t bytes = sizeof(GlobalScratch) + static_cast<size_t>(grid) * sizeof(T);
     void* scratch = nullptr;
+    if (bytes <= kStreamScratchBytes && stream_scratch(st, &scratch) == 0) {
+        cudaGetLastError();  // a failed probe above must not be reported as a launch error
+        reduce_global_kernel<OP, T><<<grid, kGlobalThreads, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst),
+                                                                     n, static_cast<GlobalScratch*>(scratch));
+        return launch_status("reduce_global");
+    }
+    cudaGetLastError();
     cudaError_t e = pool_malloc(&scratch, bytes, st);
     if (e != cudaSuccess) return fail(static_cast<int>(e), "reduce_global: scratch allocation: %s", cudaGetErrorString(e));
     e = cudaMemsetAsync(scratch, 0, sizeof(GlobalScratch), st);
     if (e == cudaSuccess) {
-        reduce_global_kernel<OP, T><<<grid, 512, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst), n,
-                                                          static_cast<GlobalScratch*>(scratch));
+        reduce_global_kernel<OP, T><<<grid, kGlobalThreads, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst),
+                                                                     n, static_cast<GlobalScratch*>(scratch));
         e = cudaGetLastError();
     }
     cudaError_t e2 = cudaFreeAsync(scratch, st);
@@ -89,8 +139,8 @@ static int run_axis(const void* src, void* dst, size_t outer, size_t axis, size_
     const size_t cap = static_cast<size_t>(sm_count()) * 16;
     if (inner == 1) {
         if (axis >= 2048) {
-            const size_t grid = outer < cap ? outer : cap;
-            reduce_rows_cta_kernel<OP, T><<<static_cast<unsigned>(grid), 512, 0, st>>>(s, d, outer, axis);
+            const size_t grid = outer < (size_t(1) << 30) ? outer : (size_t(1) << 30);
+            reduce_rows_cta_kernel<OP, T><<<static_cast<unsigned>(grid), 256, 0, st>>>(s, d, outer, axis);
         } else {
             size_t grid = (outer + 7) / 8;
             if (grid > cap) grid = cap;

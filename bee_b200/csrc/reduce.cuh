@@ -74,7 +74,7 @@ template <int OP, typename T> __device__ __forceinline__ T fold(T acc, uint4 raw
 
 // Reduces src[lo, hi) cooperatively by `nthr` threads (index `tid`); the
 // 16-byte vector path is used when src+lo is 16-byte aligned.
-template <int OP, typename T>
+template <int OP, typename T, int U = 4>
 __device__ __forceinline__ T strided_reduce(const T* __restrict__ src, size_t lo, size_t hi, size_t tid, size_t nthr) {
     constexpr size_t E = 16 / sizeof(T);
     T acc = Red<OP, T>::identity();
@@ -85,7 +85,6 @@ __device__ __forceinline__ T strided_reduce(const T* __restrict__ src, size_t lo
         const size_t nvec = len / E;
         const uint4* v = reinterpret_cast<const uint4*>(base);
         size_t i = tid;
-        constexpr int U = 4;
         for (; i + (U - 1) * nthr < nvec; i += U * nthr) {
             uint4 r[U];
 #pragma unroll
@@ -108,23 +107,62 @@ struct GlobalScratch {
     // followed by gridDim.x partials of sizeof(T), 256-byte aligned
 };
 
+// Global reduce, one launch.  The input is cut into units of 256 threads x 8
+// vectors of 16 bytes (32 KiB); CTA b folds units b, b + G, b + 2G, ... (so
+// the units in flight across the GPU form a contiguous window of memory, and
+// each thread has 8 independent 16-byte loads outstanding), reduces its
+// partial through shared memory, and the last CTA to take a ticket folds the
+// G partials in index order.  The assignment of elements to threads and the
+// folding order depend only on n and G, so float results are reproducible.
+constexpr int kGlobalThreads = 256;
+constexpr int kGlobalUnroll = 8;
+
+// Grid of the global reduce for n elements of T: at most 8 CTAs per SM, never
+// more CTAs than 32 KiB units.
+template <typename T> inline unsigned global_grid(size_t n, int sms) {
+    const size_t unit = static_cast<size_t>(kGlobalThreads) * kGlobalUnroll * (16 / sizeof(T));
+    const size_t need = (n + unit - 1) / unit;
+    const size_t cap = static_cast<size_t>(sms) * 8;
+    return static_cast<unsigned>(need < 1 ? 1 : (need < cap ? need : cap));
+}
+
 template <int OP, typename T>
-__global__ void __launch_bounds__(512) reduce_global_kernel(const T* __restrict__ src, T* __restrict__ dst, size_t n,
-                                                            GlobalScratch* scratch) {
+__global__ void __launch_bounds__(kGlobalThreads) reduce_global_kernel(const T* __restrict__ src, T* __restrict__ dst,
+                                                                       size_t n, GlobalScratch* scratch) {
+    constexpr size_t E = 16 / sizeof(T);
+    constexpr size_t UNIT = static_cast<size_t>(kGlobalThreads) * kGlobalUnroll;  // vectors per unit
     __shared__ T smem[32];
     __shared__ bool last;
     T* partials = reinterpret_cast<T*>(scratch + 1);
-    const size_t nthr = static_cast<size_t>(gridDim.x) * blockDim.x;
-    // CTA b owns the contiguous chunk [b*chunk, (b+1)*chunk) so that the
-    // partials are in element order; chunks are multiples of 16 elements.
-    const size_t chunk = ((n + gridDim.x - 1) / gridDim.x + 15) & ~size_t(15);
-    const size_t lo = min(n, static_cast<size_t>(blockIdx.x) * chunk);
-    const size_t hi = min(n, lo + chunk);
-    (void)nthr;
-    T v = strided_reduce<OP>(src, lo, hi, threadIdx.x, blockDim.x);
-    v = block_reduce<OP>(v, smem);
-    if (threadIdx.x == 0) {
-        partials[blockIdx.x] = v;
+    const unsigned tid = threadIdx.x;
+    T acc = Red<OP, T>::identity();
+    if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+        const uint4* v = reinterpret_cast<const uint4*>(src);
+        const size_t nvec = n / E;
+        for (size_t base = static_cast<size_t>(blockIdx.x) * UNIT; base < nvec; base += static_cast<size_t>(gridDim.x) * UNIT) {
+            if (base + UNIT <= nvec) {
+                uint4 r[kGlobalUnroll];
+#pragma unroll
+                for (int k = 0; k < kGlobalUnroll; ++k) r[k] = ld_stream_u4(v + base + k * kGlobalThreads + tid);
+#pragma unroll
+                for (int k = 0; k < kGlobalUnroll; ++k) acc = fold<OP>(acc, r[k]);
+            } else {
+                for (int k = 0; k < kGlobalUnroll; ++k) {
+                    const size_t idx = base + k * kGlobalThreads + tid;
+                    if (idx < nvec) acc = fold<OP>(acc, ld_stream_u4(v + idx));
+                }
+            }
+        }
+        if (blockIdx.x == 0)
+            for (size_t j = nvec * E + tid; j < n; j += kGlobalThreads) acc = Red<OP, T>::apply(acc, src[j]);
+    } else {
+        const size_t stride = static_cast<size_t>(gridDim.x) * kGlobalThreads;
+        for (size_t j = static_cast<size_t>(blockIdx.x) * kGlobalThreads + tid; j < n; j += stride)
+            acc = Red<OP, T>::apply(acc, src[j]);
+    }
+    acc = block_reduce<OP>(acc, smem);
+    if (tid == 0) {
+        partials[blockIdx.x] = acc;
         __threadfence();
         unsigned int t = atomicAdd(&scratch->ticket, 1u);
         last = (t == gridDim.x - 1);
@@ -135,10 +173,10 @@ __global__ void __launch_bounds__(512) reduce_global_kernel(const T* __restrict_
     // Last CTA: fold the partials in index order (thread-strided, then the
     // block reduce), then re-arm the ticket for the next call.
     T r = Red<OP, T>::identity();
-    for (unsigned i = threadIdx.x; i < gridDim.x; i += blockDim.x)
+    for (unsigned i = tid; i < gridDim.x; i += kGlobalThreads)
         r = Red<OP, T>::apply(r, *reinterpret_cast<volatile T*>(partials + i));
     r = block_reduce<OP>(r, smem);
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
         *dst = r;
         scratch->ticket = 0;
     }

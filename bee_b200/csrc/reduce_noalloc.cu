@@ -28,7 +28,7 @@ namespace bee_b200 {
 namespace {
 
 // Ticket header (256 bytes) plus per-CTA partials: 64 KiB holds 8160 partials
-// of 8 bytes; the kernel launches at most two CTAs per SM (296 on a B200).
+// of 8 bytes; the kernel launches at most eight CTAs per SM (1184 on a B200).
 constexpr size_t kScratchBytes = 64 * 1024;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
@@ -57,10 +57,7 @@ int scratch_address(void** out) {
 
 template <int OP, typename T>
 int run_noalloc(const void* src, void* dst, size_t n, cudaStream_t st) {
-    unsigned grid = static_cast<unsigned>(sm_count()) * 2;
-    const size_t per_cta = 512 * (16 / sizeof(T)) * 4;
-    const size_t need = (n + per_cta - 1) / per_cta;
-    if (need < grid) grid = static_cast<unsigned>(need < 1 ? 1 : need);
+    const unsigned grid = global_grid<T>(n, sm_count());
     const size_t bytes = sizeof(GlobalScratch) + static_cast<size_t>(grid) * sizeof(T);
     if (bytes > kScratchBytes)
         return fail(cudaErrorInvalidValue,
@@ -70,8 +67,8 @@ int run_noalloc(const void* src, void* dst, size_t n, cudaStream_t st) {
     if (int rc = scratch_address(&scratch)) return rc;
     cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(GlobalScratch), st);
     if (e != cudaSuccess) return fail(static_cast<int>(e), "reduce_global_noalloc: clearing the ticket: %s", cudaGetErrorString(e));
-    reduce_global_kernel<OP, T><<<grid, 512, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst), n,
-                                                      static_cast<GlobalScratch*>(scratch));
+    reduce_global_kernel<OP, T><<<grid, kGlobalThreads, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst), n,
+                                                                 static_cast<GlobalScratch*>(scratch));
     return launch_status("reduce_global_noalloc");
 }
 

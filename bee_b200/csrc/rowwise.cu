@@ -190,22 +190,29 @@ struct RopeArgs {
 // One CTA per row.  NORM: scale by 1/sqrt(mean(x^2)+eps) * w.  ROPE: rotate
 // each head's halves; the partner element of a head lives in another thread,
 // so the row passes through shared memory (fp32) between the two steps.
+// Angles: turns_i = p * f_i / (2 pi) is formed in double, its integer part
+// dropped in double, and the remaining fraction (|r| <= 1/2 turn) goes to
+// sincospif in fp32, so the angle keeps ~1e-7 rad accuracy at p = 2047
+// without a double-precision sin/cos per element.
 template <typename T, int THREADS, int NQ, bool NORM, bool ROPE>
 __global__ void __launch_bounds__(THREADS) norm_rope_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                             T* __restrict__ y, size_t rows, size_t cols, float eps,
                                                             RopeArgs rope, int vec) {
     extern __shared__ float smem[];  // ROPE: cols floats of row + head_dim/2 float2 of (cos, sin)
     __shared__ float red[THREADS / 32];
-    __shared__ double inv_freq[128];
-    const size_t half = rope.head_dim / 2;
+    __shared__ double turns_per_pos[128];  // f_i / (2 pi)
+    const uint32_t hd = static_cast<uint32_t>(rope.head_dim);
+    const uint32_t half = hd / 2;
     if (ROPE) {
-        for (size_t i = threadIdx.x; i < half; i += THREADS)
-            inv_freq[i] = exp(-(2.0 * static_cast<double>(i) / static_cast<double>(rope.head_dim)) * rope.log_theta);
+        for (uint32_t i = threadIdx.x; i < half; i += THREADS)
+            turns_per_pos[i] = exp(-(2.0 * static_cast<double>(i) / static_cast<double>(hd)) * rope.log_theta) *
+                               0.15915494309189533577;  // 1 / (2 pi)
     }
     float wv[NQ][4];
     if (NORM) load_row<T, THREADS, NQ>(w, cols, vec, 0.f, wv);
     float* rowbuf = smem;
     float2* cs = reinterpret_cast<float2*>(smem + cols);
+    const uint32_t ucols = static_cast<uint32_t>(cols);
     for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
         float v[NQ][4];
         load_row<T, THREADS, NQ>(x + r * cols, cols, vec, 0.f, v);
@@ -225,27 +232,30 @@ __global__ void __launch_bounds__(THREADS) norm_rope_kernel(const T* __restrict_
         if (ROPE) {
             const double p = static_cast<double>(r % rope.seq + rope.pos_offset);
             __syncthreads();  // previous row's readers of rowbuf / cs are done
-            for (size_t i = threadIdx.x; i < half; i += THREADS) {
-                double sn, c;
-                sincos(p * inv_freq[i], &sn, &c);
-                cs[i] = make_float2(static_cast<float>(c), static_cast<float>(sn));
+            for (uint32_t i = threadIdx.x; i < half; i += THREADS) {
+                const double t = p * turns_per_pos[i];
+                const float frac = static_cast<float>(t - rint(t));  // in [-1/2, 1/2] turns
+                float sn, c;
+                sincospif(2.0f * frac, &sn, &c);
+                cs[i] = make_float2(c, sn);
             }
 #pragma unroll
             for (int s = 0; s < NQ; ++s) {
-                const size_t e = (static_cast<size_t>(s) * THREADS + threadIdx.x) * 4;
+                const uint32_t e = (static_cast<uint32_t>(s) * THREADS + threadIdx.x) * 4;
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
-                    if (e + k < cols) rowbuf[e + k] = v[s][k];
+                    if (e + k < ucols) rowbuf[e + k] = v[s][k];
             }
             __syncthreads();
 #pragma unroll
             for (int s = 0; s < NQ; ++s) {
-                const size_t e = (static_cast<size_t>(s) * THREADS + threadIdx.x) * 4;
+                const uint32_t e = (static_cast<uint32_t>(s) * THREADS + threadIdx.x) * 4;
+                uint32_t d = e % hd;  // one 32-bit modulo per quad
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const size_t idx = e + k;
-                    if (idx >= cols) continue;
-                    const size_t d = idx % rope.head_dim;
+                for (int k = 0; k < 4; ++k, ++d) {
+                    if (d >= hd) d -= hd;
+                    const uint32_t idx = e + k;
+                    if (idx >= ucols) continue;
                     if (d < half) {
                         const float2 t = cs[d];
                         v[s][k] = v[s][k] * t.x - rowbuf[idx + half] * t.y;
@@ -258,6 +268,230 @@ __global__ void __launch_bounds__(THREADS) norm_rope_kernel(const T* __restrict_
         }
         store_row<T, THREADS, NQ>(y + r * cols, cols, vec, v);
     }
+}
+
+// Pipelined RMSNorm / RoPE for rows whose length is a whole number of 16-byte
+// chunks (and head_dim a multiple of two chunks when rotating): every thread
+// streams its share of upcoming rows into a shared-memory ring with cp.async
+// (S rows per CTA in flight, no spin-waits: cp.async.wait_group), so HBM keeps
+// streaming while earlier rows are reduced, rotated and written back with
+// 16-byte stores.  The rotate-half partner chunk is read from the same ring
+// slot, so no extra exchange pass is needed.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+                 "l"(gmem_src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <typename T> struct Chunk;
+template <> struct Chunk<float> {
+    static constexpr int E = 4;
+    static __device__ __forceinline__ void unpack(uint4 q, float v[4]) {
+        v[0] = __uint_as_float(q.x); v[1] = __uint_as_float(q.y); v[2] = __uint_as_float(q.z); v[3] = __uint_as_float(q.w);
+    }
+    static __device__ __forceinline__ uint4 pack(const float v[4]) {
+        return make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
+    }
+};
+template <> struct Chunk<uint16_t> {
+    static constexpr int E = 8;
+    static __device__ __forceinline__ void unpack(uint4 q, float v[8]) {
+        v[0] = bf16_lo(q.x); v[1] = bf16_hi(q.x); v[2] = bf16_lo(q.y); v[3] = bf16_hi(q.y);
+        v[4] = bf16_lo(q.z); v[5] = bf16_hi(q.z); v[6] = bf16_lo(q.w); v[7] = bf16_hi(q.w);
+    }
+    static __device__ __forceinline__ uint4 pack(const float v[8]) {
+        return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+    }
+};
+
+// Work assignment: a "unit" is one 16-byte chunk (RMSNorm only) or, with RoPE,
+// a rotate-half pair of chunks — chunk c of the first half of a head and chunk
+// c + half/E of its second half — so a thread holds both partners.  Thread t
+// owns units t + k*THREADS (k < NP) of every row and copies exactly those
+// chunks into its own part of the ring, so row data needs no block barrier:
+// cp.async.wait_group makes the thread's own copies visible to itself.  The
+// only barriers per row are the two of the sum-of-squares reduction (RMSNorm)
+// or one publishing the cos/sin table (RoPE alone).  Weights and per-unit
+// offsets stay in registers for the whole kernel; 1/rms is folded into the
+// row's cos/sin values, leaving about three FP instructions per element.
+template <typename T, int THREADS, int NP, int S, bool NORM, bool ROPE>
+__global__ void __launch_bounds__(THREADS) norm_rope_pipe_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                                 T* __restrict__ y, size_t rows, uint32_t cols,
+                                                                 float eps, RopeArgs rope) {
+    using CK = Chunk<T>;
+    constexpr int E = CK::E;
+    constexpr int CPU = ROPE ? 2 : 1;  // chunks per unit
+    extern __shared__ __align__(16) uint8_t pipe_smem[];
+    __shared__ float red[THREADS / 32];
+    __shared__ double turns_per_pos[128];
+    const uint32_t chunks = cols / E;
+    const uint32_t units = chunks / CPU;
+    const uint32_t row_bytes = cols * static_cast<uint32_t>(sizeof(T));
+    uint8_t* ring = pipe_smem;
+    // cos / sin tables of the current and previous row: [2][half] floats each
+    float* cos_t = reinterpret_cast<float*>(pipe_smem + S * row_bytes);
+    float* sin_t = cos_t + rope.head_dim;
+    const uint32_t hd = static_cast<uint32_t>(rope.head_dim);
+    const uint32_t half = hd / 2;
+    const uint32_t tid = threadIdx.x;
+
+    // Per-unit constants: chunk indices, table offset, weights.
+    uint32_t cidx[NP][CPU];
+    uint32_t toff[NP];
+    bool live[NP];
+    float wv[NP][CPU][E];
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+        const uint32_t unit = tid + u * THREADS;
+        live[u] = unit < units;
+        if (ROPE) {
+            const uint32_t pairs_per_head = half / E;
+            const uint32_t h = live[u] ? unit / pairs_per_head : 0, j = live[u] ? unit % pairs_per_head : 0;
+            cidx[u][0] = h * (hd / E) + j;
+            cidx[u][CPU - 1] = cidx[u][0] + pairs_per_head;
+            toff[u] = j * E;
+        } else {
+            cidx[u][0] = live[u] ? unit : 0;
+            toff[u] = 0;
+        }
+#pragma unroll
+        for (int q = 0; q < CPU; ++q) {
+            if (NORM && live[u]) {
+                CK::unpack(reinterpret_cast<const uint4*>(w)[cidx[u][q]], wv[u][q]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < E; ++k) wv[u][q][k] = 1.0f;
+            }
+        }
+    }
+    if (ROPE)
+        for (uint32_t i = tid; i < half; i += THREADS)
+            turns_per_pos[i] = exp(-(2.0 * static_cast<double>(i) / static_cast<double>(hd)) * rope.log_theta) *
+                               0.15915494309189533577;  // 1 / (2 pi)
+    if (ROPE) __syncthreads();  // turns_per_pos is read by other threads below
+
+    // Row order.  RMSNorm alone: CTA b takes rows b, b + G, ... .  With RoPE the
+    // rows are visited in position-major order — item i is position p = i / B
+    // of batch entry m = i % B, i.e. row m * seq + p (B = rows / seq) — and
+    // CTA b takes the contiguous items [b * chunk, (b + 1) * chunk), so its
+    // rows share a position for B items at a time and the cos/sin table is
+    // rebuilt only when the position changes.
+    const size_t G = gridDim.x;
+    const size_t B = rows / rope.seq;
+    const size_t chunk = (rows + G - 1) / G;
+    const size_t i_begin = ROPE ? blockIdx.x * chunk : blockIdx.x;
+    const size_t i_end = ROPE ? (i_begin + chunk < rows ? i_begin + chunk : rows) : rows;
+    const size_t i_step = ROPE ? 1 : G;
+    auto row_of = [&](size_t i) -> size_t { return ROPE ? (i % B) * rope.seq + i / B : i; };
+    auto pos_of = [&](size_t i) -> size_t { return ROPE ? i / B : 0; };
+
+    size_t i_issue = i_begin;
+    int slot_issue = 0;
+    auto issue = [&]() {
+        if (i_issue < i_end) {
+            const uint4* src = reinterpret_cast<const uint4*>(x + row_of(i_issue) * cols);
+            uint4* dst = reinterpret_cast<uint4*>(ring + slot_issue * row_bytes);
+#pragma unroll
+            for (int u = 0; u < NP; ++u)
+#pragma unroll
+                for (int q = 0; q < CPU; ++q)
+                    if (live[u]) cp_async16(dst + cidx[u][q], src + cidx[u][q]);
+        }
+        cp_async_commit();  // one group per row slot, empty past the end, so wait counts stay uniform
+        i_issue += i_step;
+        slot_issue = slot_issue + 1 == S ? 0 : slot_issue + 1;
+    };
+#pragma unroll
+    for (int j = 0; j < S - 1; ++j) issue();
+
+    int slot = 0;
+    uint32_t parity = 1;
+    size_t cur_pos = ~size_t(0);
+    for (size_t i = i_begin; i < i_end; i += i_step, slot = slot + 1 == S ? 0 : slot + 1) {
+        issue();
+        cp_async_wait<S - 1>();  // this thread's copies of this row have landed
+        const size_t r = row_of(i);
+        const uint4* row = reinterpret_cast<const uint4*>(ring + slot * row_bytes);
+        bool new_table = false;
+        if (ROPE) {
+            const size_t pos = pos_of(i);
+            if (pos != cur_pos) {
+                cur_pos = pos;
+                parity ^= 1u;
+                new_table = true;
+                const double p = static_cast<double>(pos + rope.pos_offset);
+                float* cw = cos_t + parity * half;
+                float* sw = sin_t + parity * half;
+                for (uint32_t k = tid; k < half; k += THREADS) {
+                    const double t = p * turns_per_pos[k];
+                    const float frac = static_cast<float>(t - rint(t));
+                    float sn, c;
+                    sincospif(2.0f * frac, &sn, &c);
+                    cw[k] = c;
+                    sw[k] = sn;
+                }
+            }
+        }
+        const float* cosj = cos_t + parity * half;
+        const float* sinj = sin_t + parity * half;
+        float v[NP][CPU][E];
+        float ss = 0.f;
+#pragma unroll
+        for (int u = 0; u < NP; ++u)
+#pragma unroll
+            for (int q = 0; q < CPU; ++q) {
+                if (live[u]) {
+                    CK::unpack(row[cidx[u][q]], v[u][q]);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < E; ++k) v[u][q][k] = 0.f;
+                }
+                if (NORM) {
+#pragma unroll
+                    for (int k = 0; k < E; ++k) ss = fmaf(v[u][q][k], v[u][q][k], ss);
+                }
+            }
+        float inv = 1.0f;
+        if (NORM) {
+            ss = block_sum<THREADS>(ss, red);  // also publishes a rebuilt cos / sin table
+            inv = rsqrtf(ss / static_cast<float>(cols) + eps);
+        } else if (new_table) {
+            __syncthreads();  // publish the rebuilt cos / sin table (uniform: every thread sees the same position)
+        }
+        uint4* dst = reinterpret_cast<uint4*>(y + r * cols);
+#pragma unroll
+        for (int u = 0; u < NP; ++u) {
+            if (!live[u]) continue;
+            if (ROPE) {
+                float a[E], b[E];
+#pragma unroll
+                for (int k = 0; k < E; k += 4) {
+                    const float4 c4 = *reinterpret_cast<const float4*>(cosj + toff[u] + k);
+                    const float4 s4 = *reinterpret_cast<const float4*>(sinj + toff[u] + k);
+                    const float cv[4] = {c4.x * inv, c4.y * inv, c4.z * inv, c4.w * inv};
+                    const float sv[4] = {s4.x * inv, s4.y * inv, s4.z * inv, s4.w * inv};
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                        const float a0 = v[u][0][k + m] * wv[u][0][k + m], b0 = v[u][1][k + m] * wv[u][1][k + m];
+                        a[k + m] = fmaf(a0, cv[m], -b0 * sv[m]);
+                        b[k + m] = fmaf(b0, cv[m], a0 * sv[m]);
+                    }
+                }
+                __stcs(dst + cidx[u][0], CK::pack(a));
+                __stcs(dst + cidx[u][1], CK::pack(b));
+            } else {
+                float a[E];
+#pragma unroll
+                for (int k = 0; k < E; ++k) a[k] = v[u][0][k] * inv * wv[u][0][k];
+                __stcs(dst + cidx[u][0], CK::pack(a));
+            }
+        }
+        // No barrier here: ring slots are private per thread, and a table
+        // buffer is rewritten only after the barrier that published the other.
+    }
+    cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------- launchers
@@ -281,12 +515,59 @@ static int launch_softmax(const void* src, void* dst, size_t rows, size_t cols, 
     return launch_status("softmax_rows");
 }
 
+template <typename T, int THREADS, int NP, int S, bool NORM, bool ROPE>
+static int launch_pipe(const T* px, const T* pw, T* py, size_t rows, size_t cols, float eps, RopeArgs rope,
+                       cudaStream_t st) {
+    const size_t row_bytes = cols * sizeof(T);
+    const size_t smem = S * row_bytes + (ROPE ? 2 * rope.head_dim * sizeof(float) : 0);
+    auto k = norm_rope_pipe_kernel<T, THREADS, NP, S, NORM, ROPE>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return fail(static_cast<int>(e), "rms_norm/rope: shared memory attribute: %s", cudaGetErrorString(e));
+    }
+    int per_sm = static_cast<int>((220 * 1024) / (smem + 1024 + 1024));
+    const int by_threads = 2048 / THREADS;
+    per_sm = per_sm < 1 ? 1 : (per_sm > by_threads ? by_threads : per_sm);
+    k<<<row_grid(rows, per_sm), THREADS, smem, st>>>(px, pw, py, rows, static_cast<uint32_t>(cols), eps, rope);
+    return launch_status(NORM ? (ROPE ? "rms_norm_rope" : "rms_norm_rows") : "rope");
+}
+
+// Picks threads-per-CTA and units-per-thread for the pipelined kernel (at most
+// four 16-byte chunks per thread, so values and weights stay in registers);
+// returns -1 when the row is too long for it.
+template <typename T, int S, bool NORM, bool ROPE>
+static int dispatch_pipe(const T* px, const T* pw, T* py, size_t rows, size_t cols, float eps, RopeArgs rope,
+                         cudaStream_t st) {
+    constexpr size_t E = 16 / sizeof(T);
+    const size_t chunks = cols / E;
+    const size_t units = chunks / (ROPE ? 2 : 1);
+    if constexpr (ROPE) {
+        if (units <= 128) return launch_pipe<T, 128, 1, S, NORM, ROPE>(px, pw, py, rows, cols, eps, rope, st);
+        if (units <= 256) return launch_pipe<T, 128, 2, S, NORM, ROPE>(px, pw, py, rows, cols, eps, rope, st);
+        if (units <= 512) return launch_pipe<T, 256, 2, S, NORM, ROPE>(px, pw, py, rows, cols, eps, rope, st);
+    } else {
+        if (units <= 128) return launch_pipe<T, 128, 1, S, NORM, ROPE>(px, pw, py, rows, cols, eps, rope, st);
+        if (units <= 256) return launch_pipe<T, 128, 2, S, NORM, ROPE>(px, pw, py, rows, cols, eps, rope, st);
+        if (units <= 512) return launch_pipe<T, 128, 4, S, NORM, ROPE>(px, pw, py, rows, cols, eps, rope, st);
+        if (units <= 1024) return launch_pipe<T, 256, 4, S, NORM, ROPE>(px, pw, py, rows, cols, eps, rope, st);
+    }
+    return -1;
+}
+
 template <typename T, bool NORM, bool ROPE>
 static int launch_norm_rope(const void* x, const void* w, void* y, size_t rows, size_t cols, float eps, RopeArgs rope,
                             cudaStream_t st) {
     const T* px = static_cast<const T*>(x);
     const T* pw = static_cast<const T*>(w);
     T* py = static_cast<T*>(y);
+    constexpr size_t E = 16 / sizeof(T);
+    const size_t row_bytes = cols * sizeof(T);
+    const bool pipe_ok = cols % E == 0 && aligned16(x) && aligned16(y) && (!NORM || aligned16(w)) &&
+                         (!ROPE || rope.head_dim % (2 * E) == 0) && row_bytes <= 16 * 1024;
+    if (pipe_ok) {
+        const int rc = dispatch_pipe<T, 4, NORM, ROPE>(px, pw, py, rows, cols, eps, rope, st);
+        if (rc != -1) return rc;
+    }
     const int vec = (cols % 4 == 0) && aligned16(x) && aligned16(y) && (!NORM || aligned16(w)) ? 1 : 0;
     const size_t smem = ROPE ? cols * sizeof(float) + (rope.head_dim / 2) * sizeof(float2) : 0;
     if (smem > 200 * 1024) return fail(cudaErrorInvalidValue, "rope: row of %zu elements exceeds shared memory", cols);

@@ -97,8 +97,10 @@ BEE_B200_API int bee_b200_scale_fp(int dt, void* buf, double factor, size_t n, b
  * (Bee/Tensor/Cpu/ReduceCpu.hpp:190-193) and are bit-exact under any order.
  * Float results are deterministic (fixed reduction tree).  n == 0 is an
  * error, as in Bee/CUDA/Api.cpp:237-238.  Scratch for the per-block partials
- * is taken from the stream-ordered pool for the duration of the call, as the
- * reference does (Bee/CUDA/Ops/Reduce.cu:196-224).  Replaces
+ * comes from the stream-ordered pool, as in the reference
+ * (Bee/CUDA/Ops/Reduce.cu:196-224), but is allocated once per (device, stream)
+ * (16 KiB, kept until exit) so later calls are one kernel launch; during
+ * stream capture it is allocated and freed around the launch.  Replaces
  * ops_reduce_global (Bee/CUDA/Ops/OpsBridge.hpp:31) behind
  * tensor::cuda::reduce_global (Bee/Tensor/Cuda/Backend.hpp:60). */
 BEE_B200_API int bee_b200_reduce_global(int op, int dt, const void* src, void* dst, size_t n,
