@@ -317,7 +317,7 @@ template <> struct Chunk<uint16_t> {
 // offsets stay in registers for the whole kernel; 1/rms is folded into the
 // row's cos/sin values, leaving about three FP instructions per element.
 template <typename T, int THREADS, int NP, int S, bool NORM, bool ROPE>
-__global__ void __launch_bounds__(THREADS) norm_rope_pipe_kernel(const T* __restrict__ x, const T* __restrict__ w,
+__global__ void __launch_bounds__(THREADS, 1024 / THREADS) norm_rope_pipe_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                                  T* __restrict__ y, size_t rows, uint32_t cols,
                                                                  float eps, RopeArgs rope) {
     using CK = Chunk<T>;
@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(THREADS) norm_rope_pipe_kernel(const T* __rest
     uint32_t cidx[NP][CPU];
     uint32_t toff[NP];
     bool live[NP];
-    float wv[NP][CPU][E];
+    uint4 wraw[NP][CPU];  // weights kept packed; unpacked where used
 #pragma unroll
     for (int u = 0; u < NP; ++u) {
         const uint32_t unit = tid + u * THREADS;
@@ -357,14 +357,8 @@ __global__ void __launch_bounds__(THREADS) norm_rope_pipe_kernel(const T* __rest
             toff[u] = 0;
         }
 #pragma unroll
-        for (int q = 0; q < CPU; ++q) {
-            if (NORM && live[u]) {
-                CK::unpack(reinterpret_cast<const uint4*>(w)[cidx[u][q]], wv[u][q]);
-            } else {
-#pragma unroll
-                for (int k = 0; k < E; ++k) wv[u][q][k] = 1.0f;
-            }
-        }
+        for (int q = 0; q < CPU; ++q)
+            wraw[u][q] = (NORM && live[u]) ? reinterpret_cast<const uint4*>(w)[cidx[u][q]] : make_uint4(0, 0, 0, 0);
     }
     if (ROPE)
         for (uint32_t i = tid; i < half; i += THREADS)
@@ -436,23 +430,19 @@ __global__ void __launch_bounds__(THREADS) norm_rope_pipe_kernel(const T* __rest
         }
         const float* cosj = cos_t + parity * half;
         const float* sinj = sin_t + parity * half;
-        float v[NP][CPU][E];
         float ss = 0.f;
+        if (NORM) {
 #pragma unroll
-        for (int u = 0; u < NP; ++u)
+            for (int u = 0; u < NP; ++u)
 #pragma unroll
-            for (int q = 0; q < CPU; ++q) {
-                if (live[u]) {
-                    CK::unpack(row[cidx[u][q]], v[u][q]);
-                } else {
+                for (int q = 0; q < CPU; ++q)
+                    if (live[u]) {
+                        float t[E];
+                        CK::unpack(row[cidx[u][q]], t);
 #pragma unroll
-                    for (int k = 0; k < E; ++k) v[u][q][k] = 0.f;
-                }
-                if (NORM) {
-#pragma unroll
-                    for (int k = 0; k < E; ++k) ss = fmaf(v[u][q][k], v[u][q][k], ss);
-                }
-            }
+                        for (int k = 0; k < E; ++k) ss = fmaf(t[k], t[k], ss);
+                    }
+        }
         float inv = 1.0f;
         if (NORM) {
             ss = block_sum<THREADS>(ss, red);  // also publishes a rebuilt cos / sin table
@@ -466,6 +456,18 @@ __global__ void __launch_bounds__(THREADS) norm_rope_pipe_kernel(const T* __rest
             if (!live[u]) continue;
             if (ROPE) {
                 float a[E], b[E];
+                CK::unpack(row[cidx[u][0]], a);
+                CK::unpack(row[cidx[u][1]], b);
+                if (NORM) {
+                    float wa[E], wb[E];
+                    CK::unpack(wraw[u][0], wa);
+                    CK::unpack(wraw[u][1], wb);
+#pragma unroll
+                    for (int k = 0; k < E; ++k) {
+                        a[k] *= wa[k];
+                        b[k] *= wb[k];
+                    }
+                }
 #pragma unroll
                 for (int k = 0; k < E; k += 4) {
                     const float4 c4 = *reinterpret_cast<const float4*>(cosj + toff[u] + k);
@@ -474,7 +476,7 @@ __global__ void __launch_bounds__(THREADS) norm_rope_pipe_kernel(const T* __rest
                     const float sv[4] = {s4.x * inv, s4.y * inv, s4.z * inv, s4.w * inv};
 #pragma unroll
                     for (int m = 0; m < 4; ++m) {
-                        const float a0 = v[u][0][k + m] * wv[u][0][k + m], b0 = v[u][1][k + m] * wv[u][1][k + m];
+                        const float a0 = a[k + m], b0 = b[k + m];
                         a[k + m] = fmaf(a0, cv[m], -b0 * sv[m]);
                         b[k + m] = fmaf(b0, cv[m], a0 * sv[m]);
                     }
@@ -482,9 +484,11 @@ __global__ void __launch_bounds__(THREADS) norm_rope_pipe_kernel(const T* __rest
                 __stcs(dst + cidx[u][0], CK::pack(a));
                 __stcs(dst + cidx[u][1], CK::pack(b));
             } else {
-                float a[E];
+                float a[E], wa[E];
+                CK::unpack(row[cidx[u][0]], a);
+                CK::unpack(wraw[u][0], wa);
 #pragma unroll
-                for (int k = 0; k < E; ++k) a[k] = v[u][0][k] * inv * wv[u][0][k];
+                for (int k = 0; k < E; ++k) a[k] = a[k] * inv * wa[k];
                 __stcs(dst + cidx[u][0], CK::pack(a));
             }
         }
@@ -521,7 +525,7 @@ static int launch_pipe(const T* px, const T* pw, T* py, size_t rows, size_t cols
     const size_t row_bytes = cols * sizeof(T);
     const size_t smem = S * row_bytes + (ROPE ? 2 * rope.head_dim * sizeof(float) : 0);
     auto k = norm_rope_pipe_kernel<T, THREADS, NP, S, NORM, ROPE>;
-    if (smem > 48 * 1024) {
+    if (smem + 2048 > 48 * 1024) {  // dynamic + static shared memory above the default 48 KiB
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return fail(static_cast<int>(e), "rms_norm/rope: shared memory attribute: %s", cudaGetErrorString(e));
     }
@@ -565,7 +569,7 @@ static int launch_norm_rope(const void* x, const void* w, void* y, size_t rows, 
     const bool pipe_ok = cols % E == 0 && aligned16(x) && aligned16(y) && (!NORM || aligned16(w)) &&
                          (!ROPE || rope.head_dim % (2 * E) == 0) && row_bytes <= 16 * 1024;
     if (pipe_ok) {
-        const int rc = dispatch_pipe<T, 4, NORM, ROPE>(px, pw, py, rows, cols, eps, rope, st);
+        const int rc = dispatch_pipe<T, 3, NORM, ROPE>(px, pw, py, rows, cols, eps, rope, st);
         if (rc != -1) return rc;
     }
     const int vec = (cols % 4 == 0) && aligned16(x) && aligned16(y) && (!NORM || aligned16(w)) ? 1 : 0;
@@ -574,7 +578,7 @@ static int launch_norm_rope(const void* x, const void* w, void* y, size_t rows, 
 #define BEE_NR_LAUNCH(THREADS, NQ, CTAS)                                                                              \
     do {                                                                                                              \
         auto k = norm_rope_kernel<T, THREADS, NQ, NORM, ROPE>;                                                       \
-        if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));         \
+        if (smem + 2048 > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));  \
         k<<<row_grid(rows, CTAS), THREADS, smem, st>>>(px, pw, py, rows, cols, eps, rope, vec);                       \
     } while (0)
     if (cols <= 128 * 4 * 2) BEE_NR_LAUNCH(128, 2, 12);

@@ -149,6 +149,9 @@ class Dist:
         import torch
         torch.cuda.set_device(self.local)
         if self.world > 1:
+            # NCCL prints a version banner on stdout unless told otherwise; rank 0's
+            # only stdout line must be the JSON result.
+            os.environ.setdefault("NCCL_DEBUG", "WARN")
             import datetime
             import torch.distributed as dist
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
