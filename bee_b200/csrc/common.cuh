@@ -12,7 +12,7 @@
 #include <cstddef>
 #include <cstdint>
 
-#include "../../include/bee_b200.h"
+#include "bee_b200.h"
 
 namespace bee_b200 {
 

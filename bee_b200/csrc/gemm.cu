@@ -73,6 +73,49 @@ __device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& 
     nb = r / gsize;
 }
 
+// Stores one thread's 32 consecutive accumulator columns (row `row_off`,
+// columns col0..col0+31) scaled by alpha, as fp32 or bf16 (RNE), with 16-byte
+// stores when the whole chunk is in range and rows are 16-byte aligned.
+template <bool OUT_F32>
+__device__ __forceinline__ void store_chunk32(const GemmParams& p, const uint32_t (&r)[32], bool row_ok,
+                                              long long row_off, int col0) {
+    if (!row_ok || col0 >= p.N) return;
+    if constexpr (OUT_F32) {
+        float* dst = static_cast<float*>(p.C) + row_off + col0;
+        if (col0 + 32 <= p.N && (p.ldc & 3) == 0) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+                reinterpret_cast<float4*>(dst)[v] =
+                    make_float4(__uint_as_float(r[4 * v]) * p.alpha, __uint_as_float(r[4 * v + 1]) * p.alpha,
+                                __uint_as_float(r[4 * v + 2]) * p.alpha, __uint_as_float(r[4 * v + 3]) * p.alpha);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) dst[j] = __uint_as_float(r[j]) * p.alpha;
+        }
+    } else {
+        uint16_t* dst = static_cast<uint16_t*>(p.C) + row_off + col0;
+        if (col0 + 32 <= p.N && (p.ldc & 7) == 0) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                uint4 o;
+                o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * p.alpha, __uint_as_float(r[8 * v + 1]) * p.alpha);
+                o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * p.alpha, __uint_as_float(r[8 * v + 3]) * p.alpha);
+                o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * p.alpha, __uint_as_float(r[8 * v + 5]) * p.alpha);
+                o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * p.alpha, __uint_as_float(r[8 * v + 7]) * p.alpha);
+                reinterpret_cast<uint4*>(dst)[v] = o;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) {
+                    __nv_bfloat16 h = __float2bfloat16_rn(__uint_as_float(r[j]) * p.alpha);
+                    dst[j] = *reinterpret_cast<uint16_t*>(&h);
+                }
+        }
+    }
+}
+
 template <int BN, bool B_KMAJOR, bool OUT_F32>
 __global__ void __launch_bounds__(192, 1) gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                    const __grid_constant__ CUtensorMap tmB,
@@ -238,43 +281,7 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tcgen05_kernel(const __grid_
                                        (static_cast<uint32_t>(q * 32) << 16),
                                    r);
                 tmem_ld_wait();
-                const int col0 = nb * BN + c * 32;
-                if (!row_ok || col0 >= p.N) continue;
-                if constexpr (OUT_F32) {
-                    float* dst = static_cast<float*>(p.C) + row_off + col0;
-                    if (col0 + 32 <= p.N && (p.ldc & 3) == 0) {
-#pragma unroll
-                        for (int v = 0; v < 8; ++v)
-                            reinterpret_cast<float4*>(dst)[v] =
-                                make_float4(__uint_as_float(r[4 * v]) * p.alpha, __uint_as_float(r[4 * v + 1]) * p.alpha,
-                                            __uint_as_float(r[4 * v + 2]) * p.alpha,
-                                            __uint_as_float(r[4 * v + 3]) * p.alpha);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (col0 + j < p.N) dst[j] = __uint_as_float(r[j]) * p.alpha;
-                    }
-                } else {
-                    uint16_t* dst = static_cast<uint16_t*>(p.C) + row_off + col0;
-                    if (col0 + 32 <= p.N && (p.ldc & 7) == 0) {
-#pragma unroll
-                        for (int v = 0; v < 4; ++v) {
-                            uint4 o;
-                            o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * p.alpha, __uint_as_float(r[8 * v + 1]) * p.alpha);
-                            o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * p.alpha, __uint_as_float(r[8 * v + 3]) * p.alpha);
-                            o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * p.alpha, __uint_as_float(r[8 * v + 5]) * p.alpha);
-                            o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * p.alpha, __uint_as_float(r[8 * v + 7]) * p.alpha);
-                            reinterpret_cast<uint4*>(dst)[v] = o;
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (col0 + j < p.N) {
-                                __nv_bfloat16 h = __float2bfloat16_rn(__uint_as_float(r[j]) * p.alpha);
-                                dst[j] = *reinterpret_cast<uint16_t*>(&h);
-                            }
-                    }
-                }
+                store_chunk32<OUT_F32>(p, r, row_ok, row_off, nb * BN + c * 32);
             }
             tc_fence_before();
             mbar_arrive(&tempty_bar[acc]);
@@ -285,6 +292,222 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tcgen05_kernel(const __grid_
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc<Cfg::TMEM_COLS>(tmem_base);
+}
+
+// ---------------------------------------------------------------- 2-SM variant
+// Two CTAs of a (2,1,1) cluster compute one 256x256 output tile with
+// tcgen05.mma.cta_group::2 (M=256, N=256, K=16): each CTA TMA-loads its own
+// 128 rows of A and its own 128 columns of B (no multicast), so per SM the
+// operand traffic per MMA is 2/3 of the 1-SM 128x256 tile.  Both CTAs' loads
+// complete on the leader CTA's (rank 0) full barrier, armed by the leader for
+// both halves; only the leader issues MMAs; each commit multicasts its arrive
+// to both CTAs (ring slots free, accumulator ready); both CTAs' epilogues read
+// their own 128 TMEM lanes and arrive remotely on the leader's
+// accumulator-empty barrier.  All waits are bounded as in the 1-SM kernel.
+// BK = 128 per stage: every TMA box is 16 KiB (A: two 128x64 K-halves; B:
+// two 64-wide column chunks of 128 K-rows, or two 128x64 K-halves when B is
+// K-major) — fewer, larger boxes deliver more L2->SMEM bandwidth than 8 KiB ones.
+struct Pair2Cfg {
+    static constexpr int BM = 256, BN = 256, BK = 128;
+    static constexpr int A_HALF = 128 * 64 * 2;   // one 128-row x 64-K swizzled half (16 KiB)
+    static constexpr int A_BYTES = 128 * BK * 2;  // this CTA's 128 rows
+    static constexpr int B_BYTES = 128 * BK * 2;  // this CTA's 128 columns
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = 3;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+    static constexpr uint32_t TMEM_COLS = 512;
+};
+
+template <bool B_KMAJOR, bool OUT_F32>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_bf16_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                                 const GemmParams p) {
+    using Cfg = Pair2Cfg;
+    constexpr int STAGES = Cfg::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[STAGES];
+    __shared__ __align__(8) uint64_t empty_bar[STAGES];
+    __shared__ __align__(8) uint64_t tfull_bar[2];
+    __shared__ __align__(8) uint64_t tempty_bar[2];
+    __shared__ __align__(8) uint64_t done_bar;
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int abort_sh;
+
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    volatile int* abort_flag = &abort_sh;
+    int* status = &g_gemm_status;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();  // 0 = leader
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull_bar[a], 1);
+            mbar_init(&tempty_bar[a], 8);  // 4 epilogue warps in each CTA of the pair
+        }
+        mbar_init(&done_bar, 1);
+        abort_sh = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch(&tmA);
+        tma_prefetch(&tmB);
+    }
+    if (warp == 1) tmem_alloc_pair<Cfg::TMEM_COLS>(&tmem_base_sh);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers and TMEM exist before any cross-CTA traffic
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_base_sh;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer (both CTAs)
+        int stage = 0;
+        uint32_t phase = 0;
+        long long issued = 0;
+        for (int tile = pair; tile < p.total_tiles; tile += npairs) {
+            if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+            int b, mb, nb;
+            tile_coords(tile, p, b, mb, nb);
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, status, 11);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                if (lane == 0) {
+                    uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+                    uint8_t* sb = sa + Cfg::A_BYTES;
+                    const uint32_t full_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
+                    if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::STAGE_BYTES);
+                    const int m0 = mb * Cfg::BM + static_cast<int>(rank) * 128;
+                    const int n0 = nb * Cfg::BN + static_cast<int>(rank) * 128;
+                    const int k0 = kb * Cfg::BK;
+                    tma_load_3d_pair(sa, &tmA, full_leader, k0, m0, b);
+                    tma_load_3d_pair(sa + Cfg::A_HALF, &tmA, full_leader, k0 + 64, m0, b);
+                    if constexpr (B_KMAJOR) {
+                        tma_load_3d_pair(sb, &tmB, full_leader, k0, n0, b);
+                        tma_load_3d_pair(sb + Cfg::A_HALF, &tmB, full_leader, k0 + 64, n0, b);
+                    } else {
+                        tma_load_3d_pair(sb, &tmB, full_leader, n0, k0, b);
+                        tma_load_3d_pair(sb + 64 * Cfg::BK * 2, &tmB, full_leader, n0 + 64, k0, b);
+                    }
+                }
+                __syncwarp();
+                ++issued;
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        // Drain: the leader's full barriers count both CTAs' loads, so the
+        // leader waits for the last (up to) STAGES of them before the final
+        // cluster barrier lets either CTA exit.
+        if (lane == 0 && leader) {
+            const long long first = issued > STAGES ? issued - STAGES : 0;
+            for (long long it = first; it < issued; ++it)
+                mbar_wait(&full_bar[it % STAGES], static_cast<uint32_t>((it / STAGES) & 1), abort_flag, status, 12,
+                          200000000ull);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer (leader CTA only)
+        if (leader) {
+            constexpr uint32_t idesc = idesc_bf16_f32(256, 256, !B_KMAJOR);
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            bool issued_any = false;
+            for (int tile = pair; tile < p.total_tiles; tile += npairs, ++local) {
+                if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+                const int acc = local & 1;
+                const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait_cluster(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, status, 13);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::BN);
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (lane == 0) ok = mbar_wait(&full_bar[stage], phase, abort_flag, status, 14);
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) break;
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t a_base = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+                        const uint32_t b_base = a_base + Cfg::A_BYTES;
+#pragma unroll
+                        for (int k = 0; k < Cfg::BK / 16; ++k) {
+                            // K-major tiles: 64-wide K halves of 16 KiB, 32 bytes per 16-K step inside a half
+                            const uint32_t kmaj = (k / 4) * Cfg::A_HALF + (k % 4) * 32;
+                            const uint64_t adesc = sdesc_sw128(a_base + kmaj, 16, 1024);
+                            const uint64_t bdesc = B_KMAJOR ? sdesc_sw128(b_base + kmaj, 16, 1024)
+                                                            : sdesc_sw128(b_base + k * 16 * 128, 64 * Cfg::BK * 2, 1024);
+                            mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+                        }
+                        mma_commit_pair(&empty_bar[stage], 0x3);
+                        issued_any = true;
+                    }
+                    __syncwarp();
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                if (lane == 0) mma_commit_pair(&tfull_bar[acc], 0x3);
+                __syncwarp();
+            }
+            if (lane == 0 && issued_any) {
+                mma_commit_pair(&done_bar, 0x1);
+                mbar_wait(&done_bar, 0, abort_flag, status, 15, 200000000ull);
+            }
+            __syncwarp();
+        }
+    } else {
+        // ------------------------------------------------ epilogue (warps 2-5, both CTAs)
+        const int q = warp & 3;
+        const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);
+        const uint32_t tempty_leader1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
+        int local = 0;
+        for (int tile = pair; tile < p.total_tiles; tile += npairs, ++local) {
+            if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+            int b, mb, nb;
+            tile_coords(tile, p, b, mb, nb);
+            const int acc = local & 1;
+            const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+            bool ok = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, status, 16);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            const int row = mb * Cfg::BM + static_cast<int>(rank) * 128 + q * 32 + lane;
+            const bool row_ok = row < p.M;
+            const long long row_off = static_cast<long long>(b) * p.batch_stride_c + static_cast<long long>(row) * p.ldc;
+#pragma unroll 1
+            for (int c = 0; c < Cfg::BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(acc * Cfg::BN + c * 32) +
+                                       (static_cast<uint32_t>(q * 32) << 16),
+                                   r);
+                tmem_ld_wait();
+                store_chunk32<OUT_F32>(p, r, row_ok, row_off, nb * Cfg::BN + c * 32);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // no CTA leaves while its peer may still touch its barriers or shared memory
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair<Cfg::TMEM_COLS>(tmem_base);
 }
 
 // ---------------------------------------------------------------- SIMT GEMM
@@ -434,36 +657,61 @@ static int dispatch_tc_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, 
     return bn == 256 ? launch_tc<256, B_KMAJOR, OUT_F32>(ta, tb, p, st) : launch_tc<128, B_KMAJOR, OUT_F32>(ta, tb, p, st);
 }
 
+template <bool B_KMAJOR, bool OUT_F32>
+static int launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
+    auto kern = gemm_bf16_tcgen05_2sm_kernel<B_KMAJOR, OUT_F32>;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Pair2Cfg::SMEM);
+        if (e != cudaSuccess) return fail(static_cast<int>(e), "bmm: shared memory attribute: %s", cudaGetErrorString(e));
+        attr_set[dev] = true;
+    }
+    const int pairs = sm_count() / 2;
+    const int grid = 2 * (p.total_tiles < pairs ? p.total_tiles : pairs);
+    kern<<<grid, 192, Pair2Cfg::SMEM, st>>>(ta, tb, p);
+    return launch_status("bmm(tcgen05 2-SM)");
+}
+
 // bf16 x bf16 -> (bf16 | fp32) on the tensor cores.  Returns 0, an error, or
 // -1 when the shape cannot be expressed with TMA (caller falls back).
+// M > 128 and N > 128 use 256x256 tiles on CTA pairs (cta_group::2); smaller
+// problems use 128xBN tiles on single CTAs.
 static int bmm_bf16_tc(int dt_out, const void* A, const void* B, void* C, size_t batch, size_t M, size_t K, size_t N,
                        int b_trans, float alpha, cudaStream_t st) {
     if (K % 8 != 0 || (!b_trans && N % 8 != 0) || !aligned16(A) || !aligned16(B)) return -1;
     if (M > (1u << 31) || N > (1u << 31) || K > (1u << 31) || batch > 65535) return -1;
     const int bn = N > 128 ? 256 : 128;
+    const bool pair = N > 128 && M > 128;
     CUtensorMap ta, tb;
     if (int rc = make_map(&ta, A, K, M, batch, K, M * K, 64, 128)) return rc;
     if (b_trans) {
-        if (int rc = make_map(&tb, B, K, N, batch, K, N * K, 64, static_cast<uint32_t>(bn))) return rc;
+        if (int rc = make_map(&tb, B, K, N, batch, K, N * K, 64, pair ? 128u : static_cast<uint32_t>(bn))) return rc;
     } else {
-        if (int rc = make_map(&tb, B, N, K, batch, N, K * N, 64, 64)) return rc;
+        if (int rc = make_map(&tb, B, N, K, batch, N, K * N, 64, pair ? static_cast<uint32_t>(Pair2Cfg::BK) : 64u))
+            return rc;
     }
     GemmParams p;
     p.M = static_cast<int>(M);
     p.N = static_cast<int>(N);
     p.K = static_cast<int>(K);
-    p.m_tiles = static_cast<int>((M + 127) / 128);
+    p.m_tiles = static_cast<int>(pair ? (M + 255) / 256 : (M + 127) / 128);
     p.n_tiles = static_cast<int>((N + bn - 1) / bn);
     p.tiles_per_batch = p.m_tiles * p.n_tiles;
     const long long total = static_cast<long long>(p.tiles_per_batch) * static_cast<long long>(batch);
     if (total > (1ll << 31) - 1) return -1;
     p.total_tiles = static_cast<int>(total);
-    p.num_kb = static_cast<int>((K + 63) / 64);
+    p.num_kb = static_cast<int>(pair ? (K + Pair2Cfg::BK - 1) / Pair2Cfg::BK : (K + 63) / 64);
     p.ldc = static_cast<long long>(N);
     p.batch_stride_c = static_cast<long long>(M) * static_cast<long long>(N);
     p.alpha = alpha;
     p.C = C;
     const bool f32 = dt_out == DT_F32;
+    if (pair) {
+        if (b_trans) return f32 ? launch_tc_pair<true, true>(ta, tb, p, st) : launch_tc_pair<true, false>(ta, tb, p, st);
+        return f32 ? launch_tc_pair<false, true>(ta, tb, p, st) : launch_tc_pair<false, false>(ta, tb, p, st);
+    }
     if (b_trans) return f32 ? dispatch_tc_bn<true, true>(bn, ta, tb, p, st) : dispatch_tc_bn<true, false>(bn, ta, tb, p, st);
     return f32 ? dispatch_tc_bn<false, true>(bn, ta, tb, p, st) : dispatch_tc_bn<false, false>(bn, ta, tb, p, st);
 }
