@@ -47,13 +47,16 @@ struct GemmParams {
     void* C;
 };
 
+// 1-SM tiles: 128xBN.  BN = 128 streams K in 128-wide stages (every TMA box
+// 16 KiB, 3 stages); BN = 256 keeps 64-wide stages so that 4 stages fit.
 template <int BN> struct TileCfg {
     static constexpr int BM = 128;
-    static constexpr int BK = 64;
+    static constexpr int BK = (BN == 128) ? 128 : 64;
+    static constexpr int K_HALF = BM * 64 * 2;  // one 128-row x 64-K swizzled block (16 KiB)
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (BN == 256) ? 4 : 6;
+    static constexpr int STAGES = (BN == 256) ? 4 : 3;
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
     static constexpr uint32_t TMEM_COLS = 2 * BN;
     static constexpr int THREADS = 192;
@@ -180,14 +183,18 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tcgen05_kernel(const __grid_
                     uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
                     uint8_t* sb = sa + Cfg::A_BYTES;
                     mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
-                    tma_load_3d(sa, &tmA, &full_bar[stage], kb * Cfg::BK, mb * Cfg::BM, b);
+                    const int k0 = kb * Cfg::BK;
+#pragma unroll
+                    for (int h = 0; h < Cfg::BK / 64; ++h)
+                        tma_load_3d(sa + h * Cfg::K_HALF, &tmA, &full_bar[stage], k0 + h * 64, mb * Cfg::BM, b);
                     if constexpr (B_KMAJOR) {
-                        tma_load_3d(sb, &tmB, &full_bar[stage], kb * Cfg::BK, nb * BN, b);
+#pragma unroll
+                        for (int h = 0; h < Cfg::BK / 64; ++h)
+                            tma_load_3d(sb + h * (BN * 64 * 2), &tmB, &full_bar[stage], k0 + h * 64, nb * BN, b);
                     } else {
 #pragma unroll
                         for (int j = 0; j < BN / 64; ++j)
-                            tma_load_3d(sb + j * (64 * Cfg::BK * 2), &tmB, &full_bar[stage], nb * BN + j * 64,
-                                        kb * Cfg::BK, b);
+                            tma_load_3d(sb + j * (64 * Cfg::BK * 2), &tmB, &full_bar[stage], nb * BN + j * 64, k0, b);
                     }
                 }
                 __syncwarp();
@@ -234,8 +241,11 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tcgen05_kernel(const __grid_
                     const uint32_t b_base = a_base + Cfg::A_BYTES;
 #pragma unroll
                     for (int k = 0; k < Cfg::BK / 16; ++k) {
-                        const uint64_t adesc = sdesc_sw128(a_base + k * 32, 16, 1024);
-                        const uint64_t bdesc = B_KMAJOR ? sdesc_sw128(b_base + k * 32, 16, 1024)
+                        // K-major tiles: 64-wide K blocks, 32 bytes per 16-K step inside a block
+                        const uint32_t a_off = (k / 4) * Cfg::K_HALF + (k % 4) * 32;
+                        const uint32_t b_off = (k / 4) * (BN * 64 * 2) + (k % 4) * 32;
+                        const uint64_t adesc = sdesc_sw128(a_base + a_off, 16, 1024);
+                        const uint64_t bdesc = B_KMAJOR ? sdesc_sw128(b_base + b_off, 16, 1024)
                                                         : sdesc_sw128(b_base + k * 16 * 128, 64 * Cfg::BK * 2, 1024);
                         mma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
                     }
@@ -689,8 +699,8 @@ static int bmm_bf16_tc(int dt_out, const void* A, const void* B, void* C, size_t
     if (b_trans) {
         if (int rc = make_map(&tb, B, K, N, batch, K, N * K, 64, pair ? 128u : static_cast<uint32_t>(bn))) return rc;
     } else {
-        if (int rc = make_map(&tb, B, N, K, batch, N, K * N, 64, pair ? static_cast<uint32_t>(Pair2Cfg::BK) : 64u))
-            return rc;
+        const uint32_t kbox = pair ? Pair2Cfg::BK : (bn == 256 ? TileCfg<256>::BK : TileCfg<128>::BK);
+        if (int rc = make_map(&tb, B, N, K, batch, N, K * N, 64, kbox)) return rc;
     }
     GemmParams p;
     p.M = static_cast<int>(M);
@@ -702,7 +712,8 @@ static int bmm_bf16_tc(int dt_out, const void* A, const void* B, void* C, size_t
     const long long total = static_cast<long long>(p.tiles_per_batch) * static_cast<long long>(batch);
     if (total > (1ll << 31) - 1) return -1;
     p.total_tiles = static_cast<int>(total);
-    p.num_kb = static_cast<int>(pair ? (K + Pair2Cfg::BK - 1) / Pair2Cfg::BK : (K + 63) / 64);
+    const size_t bk = pair ? Pair2Cfg::BK : (bn == 256 ? TileCfg<256>::BK : TileCfg<128>::BK);
+    p.num_kb = static_cast<int>((K + bk - 1) / bk);
     p.ldc = static_cast<long long>(N);
     p.batch_stride_c = static_cast<long long>(M) * static_cast<long long>(N);
     p.alpha = alpha;
