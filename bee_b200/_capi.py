@@ -58,6 +58,7 @@ SIGNATURES = {
     "bee_b200_rms_norm_rope": [_i, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _f, _d, _sz, _vp],
     "bee_b200_matmul": [_i, _vp, _vp, _vp, _sz, _sz, _sz, _vp],
     "bee_b200_bmm": [_i, _i, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _i, _f, _vp],
+    "bee_b200_attention": [_i, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _f, _vp],
     "bee_b200_device_status": [_c.POINTER(_i)],
 }
 _RESTYPES = {"bee_b200_last_error": _c.c_char_p, "bee_b200_status_string": _c.c_char_p}

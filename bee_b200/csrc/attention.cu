@@ -1,0 +1,406 @@
+// Fused attention forward: O = softmax(Q K^T * scale) V, per head, bf16 in/out,
+// fp32 scores and softmax, fp32 accumulation.
+//
+// The reference has no attention (its user composes per-head matmul, scale,
+// softmax and matmul, each round-tripping through memory).  Here one CTA owns
+// one head's block of 128 queries and streams the keys/values past it in
+// blocks of 128, so S and P never leave the SM:
+//   * warp 0 — TMA: Q once, then K_j / V_j into two-deep rings (the same
+//     64x128 box shape serves all three; K is read as the K-major operand of
+//     Q.K^T, V as the MN-major operand of P.V);
+//   * warp 1 — MMA: S_j = Q.K_j^T into one of two TMEM score buffers
+//     (tcgen05.mma M=128 N=128, K=128 head dims), issued one block ahead so
+//     the tensor core computes S_{j+1} while the softmax warps work on S_j;
+//     then O += P_j.V_j into a TMEM accumulator;
+//   * warps 2-5 — softmax: each thread owns one query row, reads its 128
+//     scores from TMEM, keeps a running max m (log2 units) and sum l, writes
+//     P_j = 2^(s - m) as bf16 into shared memory (double-buffered) in the
+//     swizzled K-major layout the MMA reads, and at the end divides O by l.
+//     The running max is only raised when a block's max exceeds it by more
+//     than 8 (a factor 2^8): until then P <= 256, which bf16 and fp32 hold
+//     exactly enough, and the result O / l is unchanged; when it is raised,
+//     the row of O in TMEM (and l) is rescaled after the previous P.V is done.
+// Every wait is bounded; a wait that gives up records a code in the status
+// word read by bee_b200_device_status and the CTA abandons its work.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace bee_b200 {
+
+using namespace sm100;
+
+__device__ int g_attn_status = 0;
+
+namespace {
+
+constexpr int kBlock = 128;                       // queries per CTA, keys per step
+constexpr int kHead = 128;                        // head dim
+constexpr int kHalf = 128 * 64 * 2;               // one 128-row x 64-col bf16 swizzled block
+constexpr int kTile = 2 * kHalf;                  // 128 x 128 bf16
+constexpr int kSmem = kTile /*Q*/ + 2 * kTile /*K*/ + 2 * kTile /*V*/ + 2 * kTile /*P*/ + 1024;
+constexpr float kRescaleThreshold = 8.0f;         // log2 units
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+struct AttnParams {
+    int seq;          // queries == keys per head (multiple of 128)
+    int nkv;          // seq / 128
+    float scale_log2; // scale * log2(e)
+    uint16_t* O;      // [heads, seq, 128] bf16
+};
+
+__global__ void __launch_bounds__(192, 1) attention_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                                               const __grid_constant__ CUtensorMap tmK,
+                                                               const __grid_constant__ CUtensorMap tmV,
+                                                               const AttnParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t q_full;
+    __shared__ __align__(8) uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+    __shared__ __align__(8) uint64_t s_full[2], s_empty[2];
+    __shared__ __align__(8) uint64_t p_full[2], o_done[2];
+    __shared__ __align__(8) uint64_t done_bar;
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int abort_sh;
+
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = sQ + kTile;      // [2]
+    uint8_t* sV = sK + 2 * kTile;  // [2]
+    uint8_t* sP = sV + 2 * kTile;  // [2]
+    volatile int* abort_flag = &abort_sh;
+    int* status = &g_attn_status;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qtile = blockIdx.x, head = blockIdx.y;
+    const int nkv = p.nkv;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_empty[i], 4);  // one arrive per softmax warp
+            mbar_init(&p_full[i], 4);
+            mbar_init(&o_done[i], 1);
+        }
+        mbar_init(&done_bar, 1);
+        abort_sh = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch(&tmQ);
+        tma_prefetch(&tmK);
+        tma_prefetch(&tmV);
+    }
+    if (warp == 1) tmem_alloc<512>(&tmem_base_sh);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_sh;  // S0: cols 0-127, S1: 128-255, O: 256-383
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&q_full, kTile);
+            tma_load_3d(sQ, &tmQ, &q_full, 0, qtile * kBlock, head);
+            tma_load_3d(sQ + kHalf, &tmQ, &q_full, 64, qtile * kBlock, head);
+            int k_issued = 0, v_issued = 0;
+            for (int j = 0; j < nkv; ++j) {
+                const int s = j & 1;
+                const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
+                if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag, status, 21)) break;
+                mbar_arrive_expect_tx(&k_full[s], kTile);
+                tma_load_3d(sK + s * kTile, &tmK, &k_full[s], 0, j * kBlock, head);
+                tma_load_3d(sK + s * kTile + kHalf, &tmK, &k_full[s], 64, j * kBlock, head);
+                k_issued = j + 1;
+                if (!mbar_wait(&v_empty[s], ph ^ 1u, abort_flag, status, 22)) break;
+                mbar_arrive_expect_tx(&v_full[s], kTile);
+                tma_load_3d(sV + s * kTile, &tmV, &v_full[s], 0, j * kBlock, head);
+                tma_load_3d(sV + s * kTile + kHalf, &tmV, &v_full[s], 64, j * kBlock, head);
+                v_issued = j + 1;
+            }
+            // the last loads of each ring must have landed before the CTA may exit
+            // (normally the MMA warp consumed them already)
+            mbar_wait(&q_full, 0, abort_flag, status, 33, 200000000ull);
+            for (int j = k_issued > 2 ? k_issued - 2 : 0; j < k_issued; ++j)
+                mbar_wait(&k_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, status, 34, 200000000ull);
+            for (int j = v_issued > 2 ? v_issued - 2 : 0; j < v_issued; ++j)
+                mbar_wait(&v_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, status, 35, 200000000ull);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false);  // B = K rows, K-major
+            constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, true);   // B = V, MN-major
+            const uint32_t q_base = smem_u32(sQ);
+            bool ok = mbar_wait(&q_full, 0, abort_flag, status, 23);
+            bool issued = false;
+            // S_j = Q . K_j^T into score buffer j & 1
+            auto issue_s = [&](int j) -> bool {
+                const int s = j & 1;
+                const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
+                if (!mbar_wait(&k_full[s], ph, abort_flag, status, 24)) return false;
+                if (!mbar_wait(&s_empty[s], ph ^ 1u, abort_flag, status, 25)) return false;
+                tc_fence_after();
+                const uint32_t k_base = smem_u32(sK + s * kTile);
+#pragma unroll
+                for (int k = 0; k < kHead / 16; ++k) {
+                    const uint32_t off = (k / 4) * kHalf + (k % 4) * 32;
+                    mma_f16_ss(tmem + static_cast<uint32_t>(s * 128), sdesc_sw128(q_base + off, 16, 1024),
+                               sdesc_sw128(k_base + off, 16, 1024), idesc_s, k != 0 ? 1u : 0u);
+                }
+                mma_commit(&k_empty[s]);
+                mma_commit(&s_full[s]);
+                issued = true;
+                return true;
+            };
+            // O += P_j . V_j
+            auto issue_o = [&](int j) -> bool {
+                const int s = j & 1;
+                const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
+                if (!mbar_wait(&p_full[s], ph, abort_flag, status, 26)) return false;
+                if (!mbar_wait(&v_full[s], ph, abort_flag, status, 27)) return false;
+                tc_fence_after();
+                const uint32_t p_base = smem_u32(sP + s * kTile);
+                const uint32_t v_base = smem_u32(sV + s * kTile);
+#pragma unroll
+                for (int k = 0; k < kBlock / 16; ++k) {
+                    const uint32_t a_off = (k / 4) * kHalf + (k % 4) * 32;
+                    mma_f16_ss(tmem + 256u, sdesc_sw128(p_base + a_off, 16, 1024),
+                               sdesc_sw128(v_base + k * 16 * 128, kHalf, 1024), idesc_o, (j | k) != 0 ? 1u : 0u);
+                }
+                mma_commit(&v_empty[s]);
+                mma_commit(&o_done[s]);
+                issued = true;
+                return true;
+            };
+            if (ok && nkv > 0) ok = issue_s(0);
+            for (int j = 0; ok && j < nkv; ++j) {
+                if (j + 1 < nkv) ok = issue_s(j + 1);
+                if (ok) ok = issue_o(j);
+            }
+            if (issued) {
+                mma_commit(&done_bar);
+                mbar_wait(&done_bar, 0, abort_flag, status, 28, 200000000ull);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ softmax / epilogue (warps 2-5)
+        const int q = warp & 3;                 // TMEM lane quarter
+        const int row = q * 32 + lane;          // query row within the tile
+        const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nkv; ++j) {
+            const int s = j & 1;
+            const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
+            ok = mbar_wait(&s_full[s], ph, abort_flag, status, 29);
+            if (!__all_sync(0xffffffffu, ok)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float t[kBlock];
+#pragma unroll
+            for (int c = 0; c < kBlock / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem + static_cast<uint32_t>(s * 128 + c * 32) + lane_addr, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) t[c * 32 + i] = __uint_as_float(r[i]) * p.scale_log2;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_empty[s]);
+            float mx = t[0];
+#pragma unroll
+            for (int i = 1; i < kBlock; ++i) mx = fmaxf(mx, t[i]);
+            // P_{j} goes to buffer s, last read by P.V_{j-2}: wait for it (and,
+            // before touching O, for P.V_{j-1})
+            if (j >= 2) {
+                ok = mbar_wait(&o_done[s], static_cast<uint32_t>(((j - 2) >> 1) & 1), abort_flag, status, 30);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (j == 0) {
+                m = mx;
+            } else if (__any_sync(0xffffffffu, mx > m + kRescaleThreshold)) {
+                // raise the running max of the rows that need it; O must be final up to P.V_{j-1}
+                const int sp = (j - 1) & 1;
+                ok = mbar_wait(&o_done[sp], static_cast<uint32_t>(((j - 1) >> 1) & 1), abort_flag, status, 31);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const float m_new = mx > m + kRescaleThreshold ? mx : m;
+                const float alpha = ex2(m - m_new);
+#pragma unroll 1
+                for (int c = 0; c < kHead / 32; ++c) {
+                    uint32_t r[32];
+                    const uint32_t addr = tmem + 256u + static_cast<uint32_t>(c * 32) + lane_addr;
+                    tmem_ld_32x32b_x32(addr, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                    tmem_st_32x32b_x32(addr, r);
+                }
+                tmem_st_wait();
+                tc_fence_before();
+                l *= alpha;
+                m = m_new;
+            }
+            // P = 2^(t - m) as bf16 into the swizzled K-major tile: row `row`,
+            // 16-byte chunk c of 64-key half h at physical chunk c ^ (row & 7)
+            uint8_t* prow = sP + s * kTile + row * 128;
+            float rs = 0.f;
+#pragma unroll
+            for (int c = 0; c < kBlock / 8; ++c) {
+                float e[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    e[i] = ex2(t[c * 8 + i] - m);
+                    rs += e[i];
+                }
+                const uint4 packed = make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]),
+                                                pack_bf16x2(e[4], e[5]), pack_bf16x2(e[6], e[7]));
+                const int h = c >> 3, cc = c & 7;
+                *reinterpret_cast<uint4*>(prow + h * kHalf + ((cc ^ (row & 7)) << 4)) = packed;
+            }
+            l += rs;
+            fence_proxy_async_smem();  // generic-proxy writes of P -> visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[s]);
+        }
+        // epilogue: O / l -> bf16
+        if (ok && nkv > 0) {
+            const int sl = (nkv - 1) & 1;
+            ok = mbar_wait(&o_done[sl], static_cast<uint32_t>(((nkv - 1) >> 1) & 1), abort_flag, status, 32);
+            if (__all_sync(0xffffffffu, ok)) {
+                tc_fence_after();
+                const float inv = 1.0f / l;
+                uint16_t* orow = p.O + (static_cast<size_t>(head) * p.seq + static_cast<size_t>(qtile) * kBlock + row) * kHead;
+#pragma unroll 1
+                for (int c = 0; c < kHead / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(tmem + 256u + static_cast<uint32_t>(c * 32) + lane_addr, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        uint4 o;
+                        o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * inv, __uint_as_float(r[8 * v + 1]) * inv);
+                        o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
+                        o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
+                        o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
+                        reinterpret_cast<uint4*>(orow + c * 32)[v] = o;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc<512>(tmem);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }();
+    return fn;
+}
+
+// [heads, seq, 128] bf16 viewed as {128, seq, heads}, 64x128 boxes, 128-byte swizzle.
+int make_qkv_map(CUtensorMap* map, const void* ptr, size_t heads, size_t seq) {
+    auto enc = encode();
+    if (!enc) return fail(cudaErrorNotSupported, "attention: cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHead), static_cast<cuuint64_t>(seq), static_cast<cuuint64_t>(heads)};
+    cuuint64_t strides[2] = {kHead * 2, static_cast<cuuint64_t>(seq) * kHead * 2};
+    cuuint32_t box[3] = {64, kBlock, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(cudaErrorInvalidValue, "attention: tensor map encoding failed (CUresult %d)", int(r));
+    return 0;
+}
+
+}  // namespace
+
+int attention_status_take(int* code) {
+    int zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(code, g_attn_status, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_attn_status, &zero, sizeof(int));
+    return static_cast<int>(e);
+}
+
+}  // namespace bee_b200
+
+using namespace bee_b200;
+
+extern "C" int bee_b200_attention(int dt, const void* q, const void* k, const void* v, void* o, size_t heads,
+                                  size_t seq, size_t head_dim, float scale, bee_b200_stream_t stream) {
+    if (heads == 0 || seq == 0) return ok();
+    if (!q || !k || !v || !o) return fail(cudaErrorInvalidValue, "attention: null pointer");
+    if (dt != DT_BF16) return fail(cudaErrorInvalidValue, "attention: dtype %d unsupported (BF16 only)", dt);
+    if (head_dim != static_cast<size_t>(kHead))
+        return fail(cudaErrorInvalidValue, "attention: head_dim %zu unsupported (128 only)", head_dim);
+    if (seq % kBlock != 0 || seq > (1u << 30) || heads > 65535)
+        return fail(cudaErrorInvalidValue, "attention: seq %zu must be a multiple of %d", seq, kBlock);
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+        return fail(cudaErrorInvalidValue, "attention: buffers must be 16-byte aligned");
+    CUtensorMap tq, tk, tv;
+    if (int rc = make_qkv_map(&tq, q, heads, seq)) return rc;
+    if (int rc = make_qkv_map(&tk, k, heads, seq)) return rc;
+    if (int rc = make_qkv_map(&tv, v, heads, seq)) return rc;
+    AttnParams p;
+    p.seq = static_cast<int>(seq);
+    p.nkv = static_cast<int>(seq / kBlock);
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.O = static_cast<uint16_t*>(o);
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(attention_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+        if (e != cudaSuccess) return fail(static_cast<int>(e), "attention: shared memory attribute: %s", cudaGetErrorString(e));
+        attr_set[dev] = true;
+    }
+    dim3 grid(static_cast<unsigned>(seq / kBlock), static_cast<unsigned>(heads));
+    attention_fwd_kernel<<<grid, 192, kSmem, as_stream(stream)>>>(tq, tk, tv, p);
+    return launch_status("attention");
+}

@@ -46,6 +46,9 @@ int sm_count();
 // so freed blocks stay reserved and later allocations are sub-allocations.
 cudaError_t pool_malloc(void** ptr, size_t bytes, cudaStream_t st);
 
+// Reads and clears the status word of the fused attention kernel (cudaError_t).
+int attention_status_take(int* code);
+
 inline cudaStream_t as_stream(bee_b200_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // ---------------------------------------------------------------- device side

@@ -428,18 +428,26 @@ def run_extras(args, d, dev, stream, peaks):
         o = torch.empty(h, s_, dh, device=dev, dtype=torch.bfloat16)
         scale = 1.0 / np.sqrt(dh)
 
-        def attention():
+        def attention_chain():
             call("bee_b200_bmm", _capi.BF16, _capi.F32, q.data_ptr(), k.data_ptr(), S.data_ptr(), h, s_, dh, s_, 1,
                  scale, st)
             call("bee_b200_softmax_rows_to", _capi.F32, S.data_ptr(), _capi.BF16, P.data_ptr(), h * s_, s_, st)
             call("bee_b200_bmm", _capi.BF16, _capi.BF16, P.data_ptr(), v.data_ptr(), o.data_ptr(), h, s_, s_, dh, 0,
                  1.0, st)
-        ms = timed(attention)
+
+        def attention_fused():
+            call("bee_b200_attention", _capi.BF16, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), h, s_, dh,
+                 scale, st)
         aflop = 2.0 * 2 * h * s_ * s_ * dh
+        ms = timed(attention_fused)
         tf = d.world * aflop / (ms / 1e3) / 1e12
+        ms_c = timed(attention_chain)
+        tf_c = d.world * aflop / (ms_c / 1e3) / 1e12
         out["attention_bf16"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
                                  "frac_of_measured_bf16_burst": round(tf / d.world / peaks["bf16_tflops"], 3),
-                                 "kernels": "bmm (QK^T, fp32 out) -> softmax fp32->bf16 -> bmm (PV)",
+                                 "kernels": "fused (scores and probabilities stay on chip)",
+                                 "unfused_chain": {"ms": round(ms_c, 4), "TFLOP/s": round(tf_c, 1),
+                                                   "kernels": "bmm (QK^T, fp32 out) -> softmax fp32->bf16 -> bmm (PV)"},
                                  "scaling": "weak (heads sharded)", "status_ok": status_ok()}
         del q, k, v, S, P, o
 

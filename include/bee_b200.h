@@ -184,6 +184,15 @@ BEE_B200_API int bee_b200_matmul(int dt, const void* A, const void* B, void* C, 
 BEE_B200_API int bee_b200_bmm(int dt_in, int dt_out, const void* A, const void* B, void* C, size_t batch, size_t M,
                               size_t K, size_t N, int b_trans, float alpha, bee_b200_stream_t stream);
 
+/* Fused attention forward, per head: O = softmax(Q.K^T * scale) . V with
+ * fp32 scores, softmax and accumulation; Q, K, V, O are [heads, seq, head_dim]
+ * bf16, contiguous, 16-byte aligned.  One pass: scores and probabilities stay
+ * in tensor memory / shared memory.  head_dim must be 128 and seq a multiple
+ * of 128 (other shapes: compose bee_b200_bmm, bee_b200_softmax_rows_to and
+ * bee_b200_bmm).  New: the reference has no attention. */
+BEE_B200_API int bee_b200_attention(int dt, const void* q, const void* k, const void* v, void* o, size_t heads,
+                                    size_t seq, size_t head_dim, float scale, bee_b200_stream_t stream);
+
 /* Reads and clears the device status word of the tensor-core kernels on the
  * current device: 0, or the code of the first bounded pipeline wait that gave
  * up (the kernel then abandons its remaining tiles instead of hanging).
