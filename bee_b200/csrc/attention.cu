@@ -12,10 +12,13 @@
 //     (tcgen05.mma M=128 N=128, K=128 head dims), issued one block ahead so
 //     the tensor core computes S_{j+1} while the softmax warps work on S_j;
 //     then O += P_j.V_j into a TMEM accumulator;
-//   * warps 2-5 — softmax: each thread owns one query row, reads its 128
-//     scores from TMEM, keeps a running max m (log2 units) and sum l, writes
-//     P_j = 2^(s - m) as bf16 into shared memory (double-buffered) in the
-//     swizzled K-major layout the MMA reads, and at the end divides O by l.
+//   * warps 2-9 — softmax: two threads share each query row, one per half of
+//     the 128 keys of a block (warps 2-5 and 6-9 cover the same TMEM lanes);
+//     each reads its 64 scores from TMEM, the pair combines row maxima through
+//     shared memory, keeps a running max m (log2 units) and a partial sum l,
+//     writes its half of P_j = 2^(s - m) as bf16 into shared memory (once
+//     P.V_{j-1} has consumed P_{j-1}) in the swizzled K-major layout the MMA
+//     reads, and at the end divides its half of the O row by the pair's l.
 //     The running max is only raised when a block's max exceeds it by more
 //     than 8 (a factor 2^8): until then P <= 256, which bf16 and fp32 hold
 //     exactly enough, and the result O / l is unchanged; when it is raised,
@@ -40,7 +43,7 @@ constexpr int kBlock = 128;                       // queries per CTA, keys per s
 constexpr int kHead = 128;                        // head dim
 constexpr int kHalf = 128 * 64 * 2;               // one 128-row x 64-col bf16 swizzled block
 constexpr int kTile = 2 * kHalf;                  // 128 x 128 bf16
-constexpr int kSmem = kTile /*Q*/ + 2 * kTile /*K*/ + 2 * kTile /*V*/ + 2 * kTile /*P*/ + 1024;
+constexpr int kSmem = kTile /*Q*/ + 2 * kTile /*K*/ + 2 * kTile /*V*/ + kTile /*P*/ + 1024;
 constexpr float kRescaleThreshold = 8.0f;         // log2 units
 
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -70,7 +73,9 @@ struct AttnParams {
     uint16_t* O;      // [heads, seq, 128] bf16
 };
 
-__global__ void __launch_bounds__(192, 1) attention_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+constexpr int kThreads = 320;  // TMA warp, MMA warp, 8 softmax warps
+
+__global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                                const __grid_constant__ CUtensorMap tmK,
                                                                const __grid_constant__ CUtensorMap tmV,
                                                                const AttnParams p) {
@@ -78,16 +83,19 @@ __global__ void __launch_bounds__(192, 1) attention_fwd_kernel(const __grid_cons
     __shared__ __align__(8) uint64_t q_full;
     __shared__ __align__(8) uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
     __shared__ __align__(8) uint64_t s_full[2], s_empty[2];
-    __shared__ __align__(8) uint64_t p_full[2], o_done[2];
+    __shared__ __align__(8) uint64_t p_full, o_done;
     __shared__ __align__(8) uint64_t done_bar;
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
+    __shared__ float xch[2][2][kBlock];  // [step parity][half][row]: partial row maxima
+    __shared__ float xl[2][kBlock];      // [half][row]: partial row sums, exchanged at the end
+    __shared__ __align__(8) uint64_t x_bar[2], l_bar;  // the exchanges' mbarriers (bounded waits)
 
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;
     uint8_t* sK = sQ + kTile;      // [2]
     uint8_t* sV = sK + 2 * kTile;  // [2]
-    uint8_t* sP = sV + 2 * kTile;  // [2]
+    uint8_t* sP = sV + 2 * kTile;
     volatile int* abort_flag = &abort_sh;
     int* status = &g_attn_status;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -102,11 +110,14 @@ __global__ void __launch_bounds__(192, 1) attention_fwd_kernel(const __grid_cons
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_empty[i], 4);  // one arrive per softmax warp
-            mbar_init(&p_full[i], 4);
-            mbar_init(&o_done[i], 1);
+            mbar_init(&s_empty[i], 8);  // one arrive per softmax warp
         }
+        mbar_init(&p_full, 8);
+        mbar_init(&o_done, 1);
         mbar_init(&done_bar, 1);
+        mbar_init(&x_bar[0], 8);
+        mbar_init(&x_bar[1], 8);
+        mbar_init(&l_bar, 8);
         abort_sh = 0;
         fence_mbar_init();
     }
@@ -182,10 +193,10 @@ __global__ void __launch_bounds__(192, 1) attention_fwd_kernel(const __grid_cons
             auto issue_o = [&](int j) -> bool {
                 const int s = j & 1;
                 const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
-                if (!mbar_wait(&p_full[s], ph, abort_flag, status, 26)) return false;
+                if (!mbar_wait(&p_full, static_cast<uint32_t>(j & 1), abort_flag, status, 26)) return false;
                 if (!mbar_wait(&v_full[s], ph, abort_flag, status, 27)) return false;
                 tc_fence_after();
-                const uint32_t p_base = smem_u32(sP + s * kTile);
+                const uint32_t p_base = smem_u32(sP);
                 const uint32_t v_base = smem_u32(sV + s * kTile);
 #pragma unroll
                 for (int k = 0; k < kBlock / 16; ++k) {
@@ -194,7 +205,7 @@ __global__ void __launch_bounds__(192, 1) attention_fwd_kernel(const __grid_cons
                                sdesc_sw128(v_base + k * 16 * 128, kHalf, 1024), idesc_o, (j | k) != 0 ? 1u : 0u);
                 }
                 mma_commit(&v_empty[s]);
-                mma_commit(&o_done[s]);
+                mma_commit(&o_done);
                 issued = true;
                 return true;
             };
@@ -210,8 +221,9 @@ __global__ void __launch_bounds__(192, 1) attention_fwd_kernel(const __grid_cons
         }
         __syncwarp();
     } else {
-        // ------------------------------------------------ softmax / epilogue (warps 2-5)
+        // ------------------------------------------------ softmax / epilogue (warps 2-9)
         const int q = warp & 3;                 // TMEM lane quarter
+        const int half = (warp - 2) >> 2;       // which 64 keys of a block (and 64 O columns) this thread owns
         const int row = q * 32 + lane;          // query row within the tile
         const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
         float m = -INFINITY, l = 0.f;
@@ -225,11 +237,11 @@ __global__ void __launch_bounds__(192, 1) attention_fwd_kernel(const __grid_cons
                 break;
             }
             tc_fence_after();
-            float t[kBlock];
+            float t[64];
 #pragma unroll
-            for (int c = 0; c < kBlock / 32; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem + static_cast<uint32_t>(s * 128 + c * 32) + lane_addr, r);
+                tmem_ld_32x32b_x32(tmem + static_cast<uint32_t>(s * 128 + half * 64 + c * 32) + lane_addr, r);
                 tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 32; ++i) t[c * 32 + i] = __uint_as_float(r[i]) * p.scale_log2;
@@ -237,13 +249,24 @@ __global__ void __launch_bounds__(192, 1) attention_fwd_kernel(const __grid_cons
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_empty[s]);
-            float mx = t[0];
+            float pm = t[0];
 #pragma unroll
-            for (int i = 1; i < kBlock; ++i) mx = fmaxf(mx, t[i]);
-            // P_{j} goes to buffer s, last read by P.V_{j-2}: wait for it (and,
-            // before touching O, for P.V_{j-1})
-            if (j >= 2) {
-                ok = mbar_wait(&o_done[s], static_cast<uint32_t>(((j - 2) >> 1) & 1), abort_flag, status, 30);
+            for (int i = 1; i < 64; ++i) pm = fmaxf(pm, t[i]);
+            // Exchange partial maxima with the partner warp.  Buffer s is rewritten
+            // two steps later, only after every warp has arrived on x_bar for the
+            // step in between, i.e. after every warp has read it.
+            xch[s][half][row] = pm;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&x_bar[s]);
+            ok = mbar_wait(&x_bar[s], ph, abort_flag, status, 36);
+            if (!__all_sync(0xffffffffu, ok)) {
+                ok = false;
+                break;
+            }
+            const float mx = fmaxf(xch[s][0][row], xch[s][1][row]);
+            // P_j overwrites P_{j-1} and may rescale O: both need P.V_{j-1} done
+            if (j >= 1) {
+                ok = mbar_wait(&o_done, static_cast<uint32_t>((j - 1) & 1), abort_flag, status, 30);
                 if (!__all_sync(0xffffffffu, ok)) {
                     ok = false;
                     break;
@@ -252,20 +275,14 @@ __global__ void __launch_bounds__(192, 1) attention_fwd_kernel(const __grid_cons
             if (j == 0) {
                 m = mx;
             } else if (__any_sync(0xffffffffu, mx > m + kRescaleThreshold)) {
-                // raise the running max of the rows that need it; O must be final up to P.V_{j-1}
-                const int sp = (j - 1) & 1;
-                ok = mbar_wait(&o_done[sp], static_cast<uint32_t>(((j - 1) >> 1) & 1), abort_flag, status, 31);
-                if (!__all_sync(0xffffffffu, ok)) {
-                    ok = false;
-                    break;
-                }
+                // raise the running max of the rows that need it
                 tc_fence_after();
                 const float m_new = mx > m + kRescaleThreshold ? mx : m;
                 const float alpha = ex2(m - m_new);
 #pragma unroll 1
-                for (int c = 0; c < kHead / 32; ++c) {
+                for (int c = 0; c < 2; ++c) {
                     uint32_t r[32];
-                    const uint32_t addr = tmem + 256u + static_cast<uint32_t>(c * 32) + lane_addr;
+                    const uint32_t addr = tmem + 256u + static_cast<uint32_t>(half * 64 + c * 32) + lane_addr;
                     tmem_ld_32x32b_x32(addr, r);
                     tmem_ld_wait();
 #pragma unroll
@@ -277,12 +294,12 @@ __global__ void __launch_bounds__(192, 1) attention_fwd_kernel(const __grid_cons
                 l *= alpha;
                 m = m_new;
             }
-            // P = 2^(t - m) as bf16 into the swizzled K-major tile: row `row`,
-            // 16-byte chunk c of 64-key half h at physical chunk c ^ (row & 7)
-            uint8_t* prow = sP + s * kTile + row * 128;
+            // this thread's half of P = 2^(t - m) as bf16: K-half `half` of the
+            // swizzled tile, row `row`, 16-byte chunk c at physical chunk c ^ (row & 7)
+            uint8_t* prow = sP + half * kHalf + row * 128;
             float rs = 0.f;
 #pragma unroll
-            for (int c = 0; c < kBlock / 8; ++c) {
+            for (int c = 0; c < 8; ++c) {
                 float e[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
@@ -291,26 +308,32 @@ __global__ void __launch_bounds__(192, 1) attention_fwd_kernel(const __grid_cons
                 }
                 const uint4 packed = make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]),
                                                 pack_bf16x2(e[4], e[5]), pack_bf16x2(e[6], e[7]));
-                const int h = c >> 3, cc = c & 7;
-                *reinterpret_cast<uint4*>(prow + h * kHalf + ((cc ^ (row & 7)) << 4)) = packed;
+                *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = packed;
             }
             l += rs;
             fence_proxy_async_smem();  // generic-proxy writes of P -> visible to the tensor core
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[s]);
+            if (lane == 0) mbar_arrive(&p_full);
         }
-        // epilogue: O / l -> bf16
+        // epilogue: O / l -> bf16, each thread its 64 columns of the row
+        if (ok) {
+            xl[half][row] = l;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&l_bar);
+            ok = __all_sync(0xffffffffu, mbar_wait(&l_bar, 0, abort_flag, status, 37));
+            if (ok) l = xl[0][row] + xl[1][row];
+        }
         if (ok && nkv > 0) {
-            const int sl = (nkv - 1) & 1;
-            ok = mbar_wait(&o_done[sl], static_cast<uint32_t>(((nkv - 1) >> 1) & 1), abort_flag, status, 32);
+            ok = mbar_wait(&o_done, static_cast<uint32_t>((nkv - 1) & 1), abort_flag, status, 32);
             if (__all_sync(0xffffffffu, ok)) {
                 tc_fence_after();
                 const float inv = 1.0f / l;
-                uint16_t* orow = p.O + (static_cast<size_t>(head) * p.seq + static_cast<size_t>(qtile) * kBlock + row) * kHead;
+                uint16_t* orow =
+                    p.O + (static_cast<size_t>(head) * p.seq + static_cast<size_t>(qtile) * kBlock + row) * kHead + half * 64;
 #pragma unroll 1
-                for (int c = 0; c < kHead / 32; ++c) {
+                for (int c = 0; c < 2; ++c) {
                     uint32_t r[32];
-                    tmem_ld_32x32b_x32(tmem + 256u + static_cast<uint32_t>(c * 32) + lane_addr, r);
+                    tmem_ld_32x32b_x32(tmem + 256u + static_cast<uint32_t>(half * 64 + c * 32) + lane_addr, r);
                     tmem_ld_wait();
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
@@ -401,6 +424,6 @@ extern "C" int bee_b200_attention(int dt, const void* q, const void* k, const vo
         attr_set[dev] = true;
     }
     dim3 grid(static_cast<unsigned>(seq / kBlock), static_cast<unsigned>(heads));
-    attention_fwd_kernel<<<grid, 192, kSmem, as_stream(stream)>>>(tq, tk, tv, p);
+    attention_fwd_kernel<<<grid, kThreads, kSmem, as_stream(stream)>>>(tq, tk, tv, p);
     return launch_status("attention");
 }
