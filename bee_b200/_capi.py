@@ -59,9 +59,18 @@ SIGNATURES = {
     "bee_b200_matmul": [_i, _vp, _vp, _vp, _sz, _sz, _sz, _vp],
     "bee_b200_bmm": [_i, _i, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _i, _f, _vp],
     "bee_b200_attention": [_i, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _f, _vp],
+    "bee_b200_splitk_recv_bytes": [_sz, _sz, _i],
+    "bee_b200_gemm_splitk_scatter": [_vp, _sz, _vp, _sz, _sz, _sz, _c.POINTER(_vp), _i, _i, _vp],
+    "bee_b200_gemm_splitk_reduce": [_vp, _c.POINTER(_vp), _sz, _sz, _i, _i, _vp],
+    "bee_b200_ipc_alloc": [_c.POINTER(_vp), _sz],
+    "bee_b200_ipc_free": [_vp],
+    "bee_b200_ipc_handle": [_vp, _vp],
+    "bee_b200_ipc_open": [_vp, _c.POINTER(_vp)],
+    "bee_b200_ipc_close": [_vp],
     "bee_b200_device_status": [_c.POINTER(_i)],
 }
-_RESTYPES = {"bee_b200_last_error": _c.c_char_p, "bee_b200_status_string": _c.c_char_p}
+_RESTYPES = {"bee_b200_last_error": _c.c_char_p, "bee_b200_status_string": _c.c_char_p,
+             "bee_b200_splitk_recv_bytes": _sz}
 
 _lock = threading.Lock()
 _lib = None

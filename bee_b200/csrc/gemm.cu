@@ -37,6 +37,8 @@ using namespace sm100;
 // Device status word: code of the first bounded wait that gave up (0 = none).
 __device__ int g_gemm_status = 0;
 
+constexpr int kMaxPeers = 8;
+
 struct GemmParams {
     int M, N, K;
     int m_tiles, n_tiles, tiles_per_batch, total_tiles;
@@ -45,6 +47,10 @@ struct GemmParams {
     long long batch_stride_c;  // elements
     float alpha;
     void* C;
+    // split-K scatter mode: fp32 256x256 partial tiles go to the receive buffer of
+    // tile owner (tile % world), slot `rank`, over NVLink peer stores
+    float* peer_recv[kMaxPeers];
+    int world, rank, owned;  // owned = tiles per owner = ceil(total_tiles / world)
 };
 
 // 1-SM tiles: 128xBN.  BN = 128 streams K in 128-wide stages (every TMA box
@@ -64,16 +70,19 @@ template <int BN> struct TileCfg {
 
 constexpr int kGroupM = 16;
 
-__device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& b, int& mb, int& nb) {
-    b = tile / p.tiles_per_batch;
-    const int t = tile - b * p.tiles_per_batch;
-    const int per_group = kGroupM * p.n_tiles;
+__device__ __forceinline__ void grouped_tile(int t, int m_tiles, int n_tiles, int& mb, int& nb) {
+    const int per_group = kGroupM * n_tiles;
     const int group = t / per_group;
     const int first_m = group * kGroupM;
-    const int gsize = min(p.m_tiles - first_m, kGroupM);
+    const int gsize = min(m_tiles - first_m, kGroupM);
     const int r = t - group * per_group;
     mb = first_m + r % gsize;
     nb = r / gsize;
+}
+
+__device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& b, int& mb, int& nb) {
+    b = tile / p.tiles_per_batch;
+    grouped_tile(tile - b * p.tiles_per_batch, p.m_tiles, p.n_tiles, mb, nb);
 }
 
 // Stores one thread's 32 consecutive accumulator columns (row `row_off`,
@@ -328,7 +337,7 @@ struct Pair2Cfg {
     static constexpr uint32_t TMEM_COLS = 512;
 };
 
-template <bool B_KMAJOR, bool OUT_F32>
+template <bool B_KMAJOR, bool OUT_F32, bool SCATTER = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     gemm_bf16_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                  const GemmParams p) {
@@ -505,12 +514,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
                                        (static_cast<uint32_t>(q * 32) << 16),
                                    r);
                 tmem_ld_wait();
-                store_chunk32<OUT_F32>(p, r, row_ok, row_off, nb * Cfg::BN + c * 32);
+                if constexpr (SCATTER) {
+                    // fp32 partial straight into the owner's slot for this rank (peer stores over
+                    // NVLink).  Slot layout: float4 (row r, columns 4g..4g+3) at index g * 256 + r,
+                    // so the 32 lanes (32 consecutive rows) of each store cover 512 contiguous bytes.
+                    float4* dst = reinterpret_cast<float4*>(
+                                      p.peer_recv[tile % p.world] +
+                                      (static_cast<size_t>(p.rank) * p.owned + tile / p.world) * (Cfg::BM * Cfg::BN)) +
+                                  static_cast<int>(rank) * 128 + q * 32 + lane;
+#pragma unroll
+                    for (int v = 0; v < 8; ++v)
+                        dst[(c * 8 + v) * 256] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                                             __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+                } else {
+                    store_chunk32<OUT_F32>(p, r, row_ok, row_off, nb * Cfg::BN + c * 32);
+                }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
         }
+        // peer stores must be visible to the other GPUs before anything later in the stream
+        if constexpr (SCATTER) __threadfence_system();
     }
 
     tc_fence_before();
@@ -518,6 +543,71 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     cluster_sync();  // no CTA leaves while its peer may still touch its barriers or shared memory
     tc_fence_after();
     if (warp == 1) tmem_dealloc_pair<Cfg::TMEM_COLS>(tmem_base);
+}
+
+// ---------------------------------------------------------------- split-K reduce
+// Tiles are numbered in the GEMM's grouped raster order (grouped_tile).
+// Rank `rank` owns tiles t = rank + i * world.  Its receive buffer holds, per
+// source rank s, the fp32 partial of every owned tile: slot (s, i) at
+// (s * owned + i) * 65536 floats, float4 (row r, columns 4g..4g+3) at g * 256 + r.
+// One CTA reduces a 32-row band of one tile: it sums the world slots in fixed
+// order (slot 0, 1, ...) with coalesced reads, transposes the band through
+// shared memory and writes bf16 rows, 512 contiguous bytes per warp store, into
+// every rank's C (local and peer stores over NVLink).
+struct SplitKReduceParams {
+    int M, N, m_tiles, n_tiles, total_tiles, world, rank, owned;
+    long long ldc;
+    uint16_t* c_peer[kMaxPeers];
+};
+
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ recv, const SplitKReduceParams p) {
+    constexpr int BAND = 32, PITCH = 256 + 4;  // pitch: float4 stores of 8 consecutive rows hit distinct banks
+    __shared__ __align__(16) float band[BAND * PITCH];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int units = p.owned * (256 / BAND);
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        const int i = u / (256 / BAND), r0 = (u % (256 / BAND)) * BAND;
+        const int tile = p.rank + i * p.world;
+        if (tile >= p.total_tiles) break;  // owned tiles are visited in increasing order
+        int mb, nb;
+        grouped_tile(tile, p.m_tiles, p.n_tiles, mb, nb);  // the GEMM's tile order
+        // sum: thread (warp w, lane l) handles column groups g = k * 8 + w of row r0 + l
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int g = k * 8 + warp;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int s = 0; s < p.world; ++s) {
+                const float4* src = reinterpret_cast<const float4*>(recv + (static_cast<size_t>(s) * p.owned + i) * 65536);
+                const float4 v = __ldcs(src + g * 256 + r0 + lane);
+                acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+            }
+            *reinterpret_cast<float4*>(&band[lane * PITCH + g * 4]) = acc;
+        }
+        __syncthreads();
+        // write: 32 rows x 32 chunks of 8 columns; a warp covers one row
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int f = k * 256 + tid;
+            const int rr = f >> 5, c8 = f & 31;
+            const int row = mb * 256 + r0 + rr, col = nb * 256 + c8 * 8;
+            if (row < p.M && col < p.N) {
+                const float4 a = *reinterpret_cast<const float4*>(&band[rr * PITCH + c8 * 8]);
+                const float4 b = *reinterpret_cast<const float4*>(&band[rr * PITCH + c8 * 8 + 4]);
+                const uint4 o = make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y),
+                                           pack_bf16x2(b.z, b.w));
+                const size_t off = static_cast<size_t>(row) * p.ldc + col;
+                if (col + 8 <= p.N) {
+                    for (int r = 0; r < p.world; ++r) *reinterpret_cast<uint4*>(p.c_peer[r] + off) = o;
+                } else {
+                    const uint16_t* h = reinterpret_cast<const uint16_t*>(&o);
+                    for (int r = 0; r < p.world; ++r)
+                        for (int e = 0; e < 8 && col + e < p.N; ++e) p.c_peer[r][off + e] = h[e];
+                }
+            }
+        }
+        __syncthreads();
+    }
+    __threadfence_system();  // peer stores visible to the other GPUs before later stream work
 }
 
 // ---------------------------------------------------------------- SIMT GEMM
@@ -788,6 +878,91 @@ int bee_b200_device_status(int* out_code) {
     if (e != cudaSuccess) return fail(static_cast<int>(e), "device_status: %s", cudaGetErrorString(e));
     if (*out_code == 0) *out_code = attn;
     return ok();
+}
+
+
+size_t bee_b200_splitk_recv_bytes(size_t M, size_t N, int world) {
+    if (world < 1) return 0;
+    const size_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
+    const size_t owned = (tiles + world - 1) / world;
+    return static_cast<size_t>(world) * owned * 256 * 256 * sizeof(float);
+}
+
+int bee_b200_gemm_splitk_scatter(const void* A, size_t lda, const void* B, size_t M, size_t K, size_t N,
+                                 void* const* recv_peers, int world, int rank, bee_b200_stream_t stream) {
+    if (M == 0 || N == 0) return ok();
+    if (!A || !B || !recv_peers) return fail(cudaErrorInvalidValue, "splitk_scatter: null pointer");
+    if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+        return fail(cudaErrorInvalidValue, "splitk_scatter: rank %d / world %d out of range (world <= %d)", rank, world,
+                    kMaxPeers);
+    for (int r = 0; r < world; ++r)
+        if (!recv_peers[r] || !aligned16(recv_peers[r]))
+            return fail(cudaErrorInvalidValue, "splitk_scatter: receive buffer %d missing or misaligned", r);
+    if (K == 0 || K % 8 != 0 || N % 8 != 0 || lda % 8 != 0 || lda < K || !aligned16(A) || !aligned16(B))
+        return fail(cudaErrorInvalidValue, "splitk_scatter: needs K, N, lda multiples of 8 and 16-byte aligned A, B");
+    if (M > (1u << 30) || N > (1u << 30) || K > (1u << 30))
+        return fail(cudaErrorInvalidValue, "splitk_scatter: extent too large");
+    CUtensorMap ta, tb;
+    if (int rc = make_map(&ta, A, K, M, 1, lda, lda * M, 64, 128)) return rc;
+    if (int rc = make_map(&tb, B, N, K, 1, N, K * N, 64, Pair2Cfg::BK)) return rc;
+    GemmParams p{};
+    p.M = static_cast<int>(M);
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.m_tiles = static_cast<int>((M + 255) / 256);
+    p.n_tiles = static_cast<int>((N + 255) / 256);
+    p.tiles_per_batch = p.m_tiles * p.n_tiles;
+    p.total_tiles = p.tiles_per_batch;
+    p.num_kb = static_cast<int>((K + Pair2Cfg::BK - 1) / Pair2Cfg::BK);
+    p.ldc = static_cast<long long>(N);
+    p.batch_stride_c = 0;
+    p.alpha = 1.0f;
+    p.C = nullptr;
+    p.world = world;
+    p.rank = rank;
+    p.owned = (p.total_tiles + world - 1) / world;
+    for (int r = 0; r < world; ++r) p.peer_recv[r] = static_cast<float*>(recv_peers[r]);
+    auto kern = gemm_bf16_tcgen05_2sm_kernel<false, true, true>;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Pair2Cfg::SMEM);
+        if (e != cudaSuccess) return fail(static_cast<int>(e), "splitk_scatter: shared memory attribute: %s", cudaGetErrorString(e));
+        attr_set[dev] = true;
+    }
+    const int pairs = sm_count() / 2;
+    const int grid = 2 * (p.total_tiles < pairs ? p.total_tiles : pairs);
+    kern<<<grid, 192, Pair2Cfg::SMEM, as_stream(stream)>>>(ta, tb, p);
+    return launch_status("splitk_scatter");
+}
+
+int bee_b200_gemm_splitk_reduce(const void* recv_local, void* const* c_peers, size_t M, size_t N, int world, int rank,
+                                bee_b200_stream_t stream) {
+    if (M == 0 || N == 0) return ok();
+    if (!recv_local || !c_peers) return fail(cudaErrorInvalidValue, "splitk_reduce: null pointer");
+    if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+        return fail(cudaErrorInvalidValue, "splitk_reduce: rank %d / world %d out of range", rank, world);
+    if (N % 8 != 0) return fail(cudaErrorInvalidValue, "splitk_reduce: N must be a multiple of 8");
+    SplitKReduceParams p{};
+    p.M = static_cast<int>(M);
+    p.N = static_cast<int>(N);
+    p.m_tiles = static_cast<int>((M + 255) / 256);
+    p.n_tiles = static_cast<int>((N + 255) / 256);
+    p.total_tiles = p.m_tiles * p.n_tiles;
+    p.world = world;
+    p.rank = rank;
+    p.owned = (p.total_tiles + world - 1) / world;
+    p.ldc = static_cast<long long>(N);
+    for (int r = 0; r < world; ++r) {
+        if (!c_peers[r] || !aligned16(c_peers[r])) return fail(cudaErrorInvalidValue, "splitk_reduce: C %d missing or misaligned", r);
+        p.c_peer[r] = static_cast<uint16_t*>(c_peers[r]);
+    }
+    size_t grid = static_cast<size_t>(p.owned) * 8;  // 32-row bands
+    const size_t cap = static_cast<size_t>(sm_count()) * 6;
+    if (grid > cap) grid = cap;
+    splitk_reduce_kernel<<<static_cast<unsigned>(grid), 256, 0, as_stream(stream)>>>(static_cast<const float*>(recv_local), p);
+    return launch_status("splitk_reduce");
 }
 
 }  // extern "C"

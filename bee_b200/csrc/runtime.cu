@@ -6,6 +6,7 @@
 // synchronises implicitly; bee_b200_stream_synchronize is the explicit fence.
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -127,6 +128,49 @@ int bee_b200_memset(void* ptr, int value, size_t nbytes, bee_b200_stream_t strea
     if (!ptr) return fail(cudaErrorInvalidValue, "memset: null pointer");
     cudaError_t e = cudaMemsetAsync(ptr, value & 0xff, nbytes, as_stream(stream));
     if (e != cudaSuccess) return fail(static_cast<int>(e), "memset(%zu): %s", nbytes, cudaGetErrorString(e));
+    return ok();
+}
+
+
+int bee_b200_ipc_alloc(void** out_ptr, size_t nbytes) {
+    if (!out_ptr) return fail(cudaErrorInvalidValue, "ipc_alloc: out_ptr is null");
+    *out_ptr = nullptr;
+    if (nbytes == 0) return fail(cudaErrorInvalidValue, "ipc_alloc: zero bytes");
+    cudaError_t e = cudaMalloc(out_ptr, nbytes);
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "ipc_alloc(%zu): %s", nbytes, cudaGetErrorString(e));
+    return ok();
+}
+
+int bee_b200_ipc_free(void* ptr) {
+    if (!ptr) return ok();
+    cudaError_t e = cudaFree(ptr);
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "ipc_free: %s", cudaGetErrorString(e));
+    return ok();
+}
+
+int bee_b200_ipc_handle(const void* ptr, void* handle_out) {
+    if (!ptr || !handle_out) return fail(cudaErrorInvalidValue, "ipc_handle: null pointer");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "ipc_handle: %s", cudaGetErrorString(e));
+    static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t is 64 bytes");
+    memcpy(handle_out, &h, sizeof(h));
+    return ok();
+}
+
+int bee_b200_ipc_open(const void* handle, void** out_ptr) {
+    if (!handle || !out_ptr) return fail(cudaErrorInvalidValue, "ipc_open: null pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(out_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "ipc_open: %s", cudaGetErrorString(e));
+    return ok();
+}
+
+int bee_b200_ipc_close(void* ptr) {
+    if (!ptr) return ok();
+    cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "ipc_close: %s", cudaGetErrorString(e));
     return ok();
 }
 

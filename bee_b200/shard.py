@@ -7,8 +7,11 @@ NCCL (through torch.distributed) carries the only exchange steps:
   rows and need no collective;
 * the global integer sum all-reduces one partial per rank (integer addition
   wraps identically in any order, so the result is bit-exact);
-* GEMM shards by output columns (no collective) or by K (split-K: fp32 partial
-  products summed by an all-reduce, then cast);
+* GEMM shards by output columns (no collective) or by K (split-K, SplitKGemm:
+  the GEMM epilogue stores fp32 partial tiles straight into the owning GPU's
+  receive buffer over NVLink, the owner sums and casts its tiles and writes
+  them into every GPU's C; NCCL only supplies the two stream-ordered
+  cross-GPU barriers);
 * attention shards by heads (no collective).
 """
 from __future__ import annotations
@@ -43,3 +46,119 @@ def allgather_rows(local, group=None):
     parts = [torch.empty_like(local) for _ in range(dist.get_world_size(group))]
     dist.all_gather(parts, local.contiguous(), group=group)
     return torch.cat(parts, 0)
+
+
+class SplitKGemm:
+    """C = A . B with K sharded over the ranks of one box, fused with its
+    reduction over NVLink peer memory (one process per GPU, NCCL process group).
+
+    Rank r passes A[:, K_r] (a column block of the row-major [M, K] A: base
+    pointer and row stride `lda`) and B[K_r, :] ([K_r, N] row-major); every rank
+    receives the full bf16 C = sum_r A[:, K_r] . B[K_r, :] in its own `c`.
+
+    Set-up (once per shape): each rank allocates an IPC-shareable receive buffer
+    (bee_b200_splitk_recv_bytes) and its C, exports both handles, all-gathers
+    them and opens the peers' buffers.  Per call, on the caller's stream:
+    scatter GEMM -> barrier -> owner reduce + C broadcast -> barrier.  The
+    barriers are one-element NCCL all-reduces, ordered on the same stream.
+    """
+
+    def __init__(self, M: int, N: int, device, group=None):
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        from . import _capi
+        self._capi = _capi
+        self.M, self.N, self.group = M, N, group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world > 8:
+            raise ValueError("split-K GEMM supports at most 8 GPUs")
+        self.device = torch.device(device)
+        self._recv_bytes = int(_capi.lib().bee_b200_splitk_recv_bytes(M, N, self.world))
+        self._own = []    # (pointer) buffers this rank allocated
+        self._opened = []  # peer mappings opened in this process
+        recv = ctypes.c_void_p()
+        cbuf = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _capi.call("bee_b200_ipc_alloc", ctypes.byref(recv), self._recv_bytes)
+            self._own.append(recv.value)
+            _capi.call("bee_b200_ipc_alloc", ctypes.byref(cbuf), max(M * N * 2, 16))
+            self._own.append(cbuf.value)
+            handles = (ctypes.c_ubyte * 128)()
+            _capi.call("bee_b200_ipc_handle", ctypes.c_void_p(recv.value), ctypes.byref(handles, 0))
+            _capi.call("bee_b200_ipc_handle", ctypes.c_void_p(cbuf.value), ctypes.byref(handles, 64))
+            mine = torch.tensor(list(bytes(handles)), dtype=torch.uint8, device=self.device)
+            if self.world > 1:
+                allh = [torch.empty_like(mine) for _ in range(self.world)]
+                dist.all_gather(allh, mine, group=group)
+                allh = [bytes(h.cpu().tolist()) for h in allh]
+            else:
+                allh = [bytes(handles)]
+            self.recv_local = recv.value
+            self.c_local = cbuf.value
+            recv_peers, c_peers = [], []
+            for r, h in enumerate(allh):
+                if r == self.rank:
+                    recv_peers.append(recv.value)
+                    c_peers.append(cbuf.value)
+                    continue
+                ptrs = []
+                for off in (0, 64):
+                    hb = (ctypes.c_ubyte * 64).from_buffer_copy(h[off:off + 64])
+                    out = ctypes.c_void_p()
+                    _capi.call("bee_b200_ipc_open", ctypes.byref(hb), ctypes.byref(out))
+                    self._opened.append(out.value)
+                    ptrs.append(out.value)
+                recv_peers.append(ptrs[0])
+                c_peers.append(ptrs[1])
+            self._recv_peers = (ctypes.c_void_p * self.world)(*recv_peers)
+            self._c_peers = (ctypes.c_void_p * self.world)(*c_peers)
+            self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+            torch.cuda.synchronize(self.device)
+        # C as a tensor view of the IPC buffer (the library owns the memory)
+        self.c = _wrap_bf16(self.c_local, M, N, self.device)
+
+    def barrier(self):
+        """Stream-ordered cross-GPU barrier on the current stream."""
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(self._flag, group=self.group)
+
+    def __call__(self, a_ptr: int, lda: int, b_ptr: int, k_local: int, stream_ptr: int):
+        """Launches the scatter GEMM, the barrier, the owner reduce and the
+        closing barrier on the current torch stream (whose handle is stream_ptr)."""
+        _capi = self._capi
+        _capi.call("bee_b200_gemm_splitk_scatter", a_ptr, lda, b_ptr, self.M, k_local, self.N, self._recv_peers,
+                   self.world, self.rank, stream_ptr)
+        self.barrier()
+        _capi.call("bee_b200_gemm_splitk_reduce", self.recv_local, self._c_peers, self.M, self.N, self.world,
+                   self.rank, stream_ptr)
+        self.barrier()
+        return self.c
+
+    def close(self):
+        """Unmaps the peers' buffers and frees this rank's (after a device sync
+        and a barrier, so no rank still writes into them)."""
+        import torch
+        if not self._own:
+            return
+        torch.cuda.synchronize(self.device)
+        self.barrier()
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for ptr in self._opened:
+                self._capi.call("bee_b200_ipc_close", ptr)
+            for ptr in self._own:
+                self._capi.call("bee_b200_ipc_free", ptr)
+        self._opened, self._own = [], []
+
+
+def _wrap_bf16(ptr: int, M: int, N: int, device):
+    """A [M, N] bf16 torch view of device memory at `ptr` (not owned)."""
+    import torch
+
+    class _Iface:
+        __cuda_array_interface__ = {"shape": (M, N), "typestr": "<i2", "data": (ptr, False), "version": 3,
+                                    "strides": None}
+    return torch.as_tensor(_Iface(), device=device).view(torch.bfloat16)

@@ -343,8 +343,10 @@ def run_extras(args, d, dev, stream, peaks):
       B sharded by output columns (each GPU owns an [8192, 8192] column block of a
       [8192, 8192*N] B, weak scaling, no collective);
     * gemm_bf16_8192_splitk: the same single 8192^3 product with K sharded over the
-      GPUs (strong scaling), fp32 partials summed by an NCCL all-reduce, then cast
-      to bf16;
+      GPUs (strong scaling): the GEMM epilogue stores fp32 partial tiles into the
+      owning GPU over NVLink, the owner sums, casts and writes its tiles into every
+      GPU's C (SplitKGemm); the unfused chain (fp32 partial, NCCL all-reduce,
+      cast) is timed beside it;
     * rms_norm_rope_bf16: RMSNorm (eps 1e-6) + RoPE (theta 1e4, rotate-half) of X
       [16 x 2048, 4096] bf16 viewed [16, 2048, 32, 128], fused, per GPU (weak);
     * attention_bf16: S = Q.K^T/sqrt(128) (fp32), P = softmax(S) (bf16),
@@ -410,12 +412,30 @@ def run_extras(args, d, dev, stream, peaks):
                 import torch.distributed as dist
                 dist.all_reduce(part, op=dist.ReduceOp.SUM)
             call("bee_b200_ew_cast", _capi.F32, part.data_ptr(), _capi.BF16, c.data_ptr(), n * n, st)
-        ms = timed(splitk)
+        ms_nccl = timed(splitk)
+        del ak, bk, part
+
+        from bee_b200.shard import SplitKGemm
+        fused = SplitKGemm(n, n, dev, group=d.pg)
+        a_ptr = a.data_ptr() + 2 * klo
+        b_ptr = b[klo:khi].data_ptr()
+        ms = timed(lambda: fused(a_ptr, n, b_ptr, kr, st))
+        ok_fused = status_ok()
+        fused.close()
         tf = flop / (ms / 1e3) / 1e12
-        out["gemm_bf16_8192_splitk"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
-                                        "scaling": "strong (K sharded, NCCL all-reduce of fp32 partials)",
-                                        "allreduce_bytes_per_gpu": n * n * 4 if d.world > 1 else 0}
-        del a, b, c, ak, bk, part
+        tf_nccl = flop / (ms_nccl / 1e3) / 1e12
+        owned = -(-(n // 256) ** 2 // d.world)
+        out["gemm_bf16_8192_splitk"] = {
+            "ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
+            "scaling": "strong (K sharded)",
+            "kernels": "tcgen05 GEMM whose epilogue stores fp32 partial tiles into the owner GPU over NVLink, "
+                       "owner reduce writing bf16 C into every GPU; two one-element NCCL all-reduces as barriers",
+            "nvlink_bytes_out_per_gpu": (d.world - 1) * owned * 256 * 256 * (4 + 2) if d.world > 1 else 0,
+            "status_ok": ok_fused,
+            "nccl_allreduce_chain": {"ms": round(ms_nccl, 4), "TFLOP/s": round(tf_nccl, 1),
+                                     "kernels": "bmm fp32 out -> NCCL all-reduce (fp32) -> cast",
+                                     "allreduce_bytes_per_gpu": n * n * 4 if d.world > 1 else 0}}
+        del a, b, c
 
         rows, cols, seq, heads, hd = 16 * 2048, 4096, 2048, 32, 128
         x = torch.randn(rows, cols, device=dev, generator=g).to(torch.bfloat16)

@@ -193,6 +193,38 @@ BEE_B200_API int bee_b200_bmm(int dt_in, int dt_out, const void* A, const void* 
 BEE_B200_API int bee_b200_attention(int dt, const void* q, const void* k, const void* v, void* o, size_t heads,
                                     size_t seq, size_t head_dim, float scale, bee_b200_stream_t stream);
 
+/* ------------------------------------------------- multi-GPU (split-K GEMM)
+ * New: the reference has no multi-GPU code.  One process per GPU.  C = A . B
+ * with K sharded over `world` GPUs: rank r holds A[:, K_r] (a column block of
+ * the row-major A, row stride `lda`) and B[K_r, :].  The product tiles are
+ * 256x256; tile t is owned by rank t % world.
+ *
+ * 1. bee_b200_gemm_splitk_scatter: every rank computes its fp32 partial on the
+ *    tensor cores and the GEMM epilogue stores each partial tile straight into
+ *    the owner's receive buffer over NVLink (plain peer stores, slot = source
+ *    rank).  recv_peers[r] is rank r's receive buffer as mapped in this process
+ *    (bee_b200_ipc_open), each bee_b200_splitk_recv_bytes(M, N, world) bytes.
+ * 2. A cross-GPU barrier on the stream (e.g. an all-reduce of one element).
+ * 3. bee_b200_gemm_splitk_reduce: each rank sums the world partials of its
+ *    own tiles in fixed slot order, rounds to bf16 and writes the tile into
+ *    every rank's C (c_peers[r]: rank r's C mapped in this process, [M, N]).
+ * 4. Another barrier before C is read on another GPU.
+ * Requirements: world <= 8; K, N, lda multiples of 8; 16-byte aligned buffers. */
+BEE_B200_API size_t bee_b200_splitk_recv_bytes(size_t M, size_t N, int world);
+BEE_B200_API int bee_b200_gemm_splitk_scatter(const void* A, size_t lda, const void* B, size_t M, size_t K, size_t N,
+                                              void* const* recv_peers, int world, int rank, bee_b200_stream_t stream);
+BEE_B200_API int bee_b200_gemm_splitk_reduce(const void* recv_local, void* const* c_peers, size_t M, size_t N, int world,
+                                             int rank, bee_b200_stream_t stream);
+
+/* Device buffers shareable between the processes of one box (CUDA IPC):
+ * allocate (cudaMalloc, so the buffer can be exported), export a 64-byte
+ * handle, open a peer's handle into this process, close / free. */
+BEE_B200_API int bee_b200_ipc_alloc(void** out_ptr, size_t nbytes);
+BEE_B200_API int bee_b200_ipc_free(void* ptr);
+BEE_B200_API int bee_b200_ipc_handle(const void* ptr, void* handle_out);
+BEE_B200_API int bee_b200_ipc_open(const void* handle, void** out_ptr);
+BEE_B200_API int bee_b200_ipc_close(void* ptr);
+
 /* Reads and clears the device status word of the tensor-core kernels on the
  * current device: 0, or the code of the first bounded pipeline wait that gave
  * up (the kernel then abandons its remaining tiles instead of hanging).

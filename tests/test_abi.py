@@ -92,3 +92,31 @@ def test_binding_raises_with_message():
     with pytest.raises(_capi.BeeError) as e:
         _capi.call("bee_b200_reduce_global", 0, 2, None, None, 0, None)
     assert e.value.status == 1 and "empty" in str(e.value)
+
+
+def test_splitk_receive_buffer_size():
+    lib = _capi.lib()
+    # 8192 x 8192 -> 1024 tiles of 256 x 256; world 3 owns ceil(1024 / 3) = 342 per rank, 3 slots each
+    assert lib.bee_b200_splitk_recv_bytes(8192, 8192, 3) == 3 * 342 * 65536 * 4
+    assert lib.bee_b200_splitk_recv_bytes(1, 8, 1) == 65536 * 4
+    assert lib.bee_b200_splitk_recv_bytes(520, 776, 2) == 2 * 6 * 65536 * 4  # 3 x 4 tiles
+    assert lib.bee_b200_splitk_recv_bytes(8, 8, 0) == 0
+
+
+def test_splitk_argument_checks_on_host():
+    peers = (ctypes.c_void_p * 9)(*([16] * 9))
+    rc, msg = _rc("bee_b200_gemm_splitk_scatter", 16, 64, 16, 64, 64, 64, peers, 9, 0, None)
+    assert rc == 1 and "world" in msg
+    rc, msg = _rc("bee_b200_gemm_splitk_scatter", 16, 64, 16, 64, 64, 64, peers, 2, 2, None)
+    assert rc == 1 and "out of range" in msg
+    rc, msg = _rc("bee_b200_gemm_splitk_scatter", 16, 64, 16, 64, 60, 64, peers, 2, 0, None)
+    assert rc == 1 and "multiples of 8" in msg
+    rc, msg = _rc("bee_b200_gemm_splitk_scatter", 16, 64, 16, 64, 0, 64, peers, 2, 0, None)
+    assert rc == 1
+    rc, msg = _rc("bee_b200_gemm_splitk_scatter", None, 64, 16, 64, 64, 64, peers, 2, 0, None)
+    assert rc == 1 and "null" in msg
+    rc, msg = _rc("bee_b200_gemm_splitk_reduce", 16, peers, 64, 60, 2, 0, None)
+    assert rc == 1 and "multiple of 8" in msg
+    assert _rc("bee_b200_gemm_splitk_reduce", 16, peers, 0, 64, 2, 0, None)[0] == 0  # empty C: no-op
+    rc, msg = _rc("bee_b200_ipc_alloc", None, 16)
+    assert rc == 1 and "null" in msg
