@@ -45,6 +45,8 @@ SIGNATURES = {
     "bee_b200_memset": [_vp, _i, _sz, _vp],
     "bee_b200_stream_synchronize": [_vp],
     "bee_b200_ew_binary": [_i, _i, _vp, _vp, _vp, _sz, _vp],
+    "bee_b200_ew_binary_strided": [_i, _i, _i, _c.POINTER(_c.c_int64), _vp, _c.POINTER(_c.c_int64), _vp,
+                                   _c.POINTER(_c.c_int64), _vp, _vp],
     "bee_b200_ew_unary": [_i, _i, _vp, _vp, _sz, _vp],
     "bee_b200_ew_cast": [_i, _vp, _i, _vp, _sz, _vp],
     "bee_b200_scale_fp": [_i, _vp, _d, _sz, _vp],
@@ -59,6 +61,8 @@ SIGNATURES = {
     "bee_b200_matmul": [_i, _vp, _vp, _vp, _sz, _sz, _sz, _vp],
     "bee_b200_bmm": [_i, _i, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _i, _f, _vp],
     "bee_b200_attention": [_i, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _f, _vp],
+    "bee_b200_transpose_2d": [_i, _vp, _vp, _sz, _sz, _vp],
+    "bee_b200_strided_copy": [_i, _vp, _i, _c.POINTER(_c.c_int64), _c.POINTER(_c.c_int64), _vp, _vp],
     "bee_b200_splitk_recv_bytes": [_sz, _sz, _i],
     "bee_b200_gemm_splitk_scatter": [_vp, _sz, _vp, _sz, _sz, _sz, _c.POINTER(_vp), _i, _i, _vp],
     "bee_b200_gemm_splitk_reduce": [_vp, _c.POINTER(_vp), _sz, _sz, _i, _i, _vp],

@@ -109,6 +109,68 @@ __global__ void __launch_bounds__(kThreads) binary_scalar_kernel(const S* __rest
         out[i] = from_c<S>(bin<OP>(to_c(a[i]), to_c(b[i])));
 }
 
+// Broadcasting / strided binary op: out (contiguous, viewed [rows, L]) =
+// a op b where each operand is a strided view of out's shape (stride 0 on
+// broadcast dims).  Work item = one 16-byte chunk of an output row; an operand
+// whose innermost stride is 1 is read in 16-byte vectors when aligned, one with
+// innermost stride 0 is read once per chunk, any other stride element by element.
+constexpr int kMaxBcastDims = 8;
+struct BcastDims {
+    int nd;                                // outer dims (all but the innermost)
+    long long shape[kMaxBcastDims];
+    long long sa[kMaxBcastDims], sb[kMaxBcastDims];
+};
+
+template <typename S>
+__device__ __forceinline__ void load_chunk(const S* p, long long inner, bool vec, int cnt, Pack16<S>& v) {
+    constexpr int E = 16 / sizeof(S);
+    if (inner == 1 && vec && cnt == E) {
+        v.v = __ldcs(reinterpret_cast<const uint4*>(p));
+    } else if (inner == 0) {
+        const S x = p[0];
+#pragma unroll
+        for (int k = 0; k < E; ++k) v.s[k] = x;
+    } else {
+#pragma unroll
+        for (int k = 0; k < E; ++k) v.s[k] = k < cnt ? p[k * inner] : p[0];
+    }
+}
+
+template <typename S, int OP>
+__global__ void __launch_bounds__(kThreads) binary_strided_kernel(const S* __restrict__ a, const S* __restrict__ b,
+                                                                  S* __restrict__ out, long long rows, long long L,
+                                                                  BcastDims d, long long ia, long long ib, int a_vec,
+                                                                  int b_vec, int o_vec) {
+    constexpr int E = 16 / sizeof(S);
+    const long long per_row = (L + E - 1) / E;
+    const long long items = rows * per_row;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < items; i += stride) {
+        long long r = i / per_row;
+        const long long c = (i - r * per_row) * E;
+        const long long orow = r;
+        long long oa = 0, ob = 0;
+        for (int k = d.nd - 1; k >= 0; --k) {
+            const long long x = r % d.shape[k];
+            r /= d.shape[k];
+            oa += x * d.sa[k];
+            ob += x * d.sb[k];
+        }
+        const int cnt = static_cast<int>(L - c < E ? L - c : E);
+        Pack16<S> va, vb, vo;
+        load_chunk<S>(a + oa + c * ia, ia, a_vec, cnt, va);
+        load_chunk<S>(b + ob + c * ib, ib, b_vec, cnt, vb);
+#pragma unroll
+        for (int k = 0; k < E; ++k) vo.s[k] = from_c<S>(bin<OP>(to_c(va.s[k]), to_c(vb.s[k])));
+        S* o = out + orow * L + c;
+        if (o_vec && cnt == E) {
+            __stcs(reinterpret_cast<uint4*>(o), vo.v);
+        } else {
+            for (int k = 0; k < cnt; ++k) o[k] = vo.s[k];
+        }
+    }
+}
+
 template <typename S, int OP>
 __global__ void __launch_bounds__(kThreads) unary_kernel(const S* __restrict__ a, S* __restrict__ out, size_t n,
                                                          int vectorised) {
@@ -243,6 +305,50 @@ static int dispatch_binary_op(int op, const void* a, const void* b, void* out, s
     return launch_status("ew_binary");
 }
 
+struct StridedOperands {
+    int nd;  // simplified dims, innermost last
+    long long shape[kMaxBcastDims], sa[kMaxBcastDims], sb[kMaxBcastDims];
+};
+
+template <typename S, int OP>
+static void launch_binary_strided(const void* a, const void* b, void* out, const StridedOperands& v, cudaStream_t st) {
+    constexpr int E = 16 / sizeof(S);
+    const long long L = v.shape[v.nd - 1];
+    long long rows = 1;
+    BcastDims d{};
+    d.nd = v.nd - 1;
+    for (int k = 0; k < v.nd - 1; ++k) {
+        d.shape[k] = v.shape[k];
+        d.sa[k] = v.sa[k];
+        d.sb[k] = v.sb[k];
+        rows *= v.shape[k];
+    }
+    const long long ia = v.sa[v.nd - 1], ib = v.sb[v.nd - 1];
+    bool a_vec = aligned16(a), b_vec = aligned16(b);
+    for (int k = 0; k < v.nd - 1; ++k) {
+        a_vec = a_vec && (v.sa[k] * static_cast<long long>(sizeof(S))) % 16 == 0;
+        b_vec = b_vec && (v.sb[k] * static_cast<long long>(sizeof(S))) % 16 == 0;
+    }
+    const int o_vec = aligned16(out) && (L * static_cast<long long>(sizeof(S))) % 16 == 0;
+    const long long items = rows * ((L + E - 1) / E);
+    binary_strided_kernel<S, OP><<<grid_for(static_cast<size_t>(items)), kThreads, 0, st>>>(
+        static_cast<const S*>(a), static_cast<const S*>(b), static_cast<S*>(out), rows, L, d, ia, ib, a_vec ? 1 : 0,
+        b_vec ? 1 : 0, o_vec);
+}
+
+template <typename S>
+static int dispatch_binary_strided(int op, const void* a, const void* b, void* out, const StridedOperands& v,
+                                   cudaStream_t st) {
+    switch (op) {
+    case OP_ADD: launch_binary_strided<S, OP_ADD>(a, b, out, v, st); break;
+    case OP_SUB: launch_binary_strided<S, OP_SUB>(a, b, out, v, st); break;
+    case OP_MUL: launch_binary_strided<S, OP_MUL>(a, b, out, v, st); break;
+    case OP_DIV: launch_binary_strided<S, OP_DIV>(a, b, out, v, st); break;
+    default: return fail(cudaErrorInvalidValue, "ew_binary_strided: unknown op code %d", op);
+    }
+    return launch_status("ew_binary_strided");
+}
+
 template <typename S, int OP>
 static void launch_unary(const void* a, void* out, size_t n, cudaStream_t st) {
     int vec = aligned16(a) && aligned16(out);
@@ -305,6 +411,53 @@ int bee_b200_ew_binary(int op, int dt, const void* a, const void* b, void* out, 
     case DT_F64: return dispatch_binary_op<double>(op, a, b, out, n, st);
     case DT_BF16: return dispatch_binary_op<bf16_t>(op, a, b, out, n, st);
     default: return fail(cudaErrorInvalidValue, "ew_binary: unsupported dtype %d", dt);
+    }
+}
+
+int bee_b200_ew_binary_strided(int op, int dt, int ndim, const int64_t* shape, const void* a, const int64_t* a_strides,
+                               const void* b, const int64_t* b_strides, void* out, bee_b200_stream_t stream) {
+    if (ndim < 0 || ndim > kMaxBcastDims)
+        return fail(cudaErrorInvalidValue, "ew_binary_strided: ndim %d outside [0, %d]", ndim, kMaxBcastDims);
+    if (ndim > 0 && (!shape || !a_strides || !b_strides))
+        return fail(cudaErrorInvalidValue, "ew_binary_strided: null shape or strides");
+    long long n = 1;
+    for (int k = 0; k < ndim; ++k) {
+        if (shape[k] < 0) return fail(cudaErrorInvalidValue, "ew_binary_strided: negative extent in dim %d", k);
+        n *= shape[k];
+        if (n > (1LL << 46)) return fail(cudaErrorInvalidValue, "ew_binary_strided: too many elements");
+    }
+    if (n == 0) return ok();
+    if (!a || !b || !out) return fail(cudaErrorInvalidValue, "ew_binary_strided: null pointer");
+    // simplify: drop extent-1 dims, merge neighbours contiguous with each other in both operands
+    StridedOperands v{};
+    for (int k = 0; k < ndim; ++k) {
+        if (shape[k] == 1) continue;
+        if (v.nd > 0 && v.sa[v.nd - 1] == a_strides[k] * shape[k] && v.sb[v.nd - 1] == b_strides[k] * shape[k]) {
+            v.shape[v.nd - 1] *= shape[k];
+            v.sa[v.nd - 1] = a_strides[k];
+            v.sb[v.nd - 1] = b_strides[k];
+        } else {
+            v.shape[v.nd] = shape[k];
+            v.sa[v.nd] = a_strides[k];
+            v.sb[v.nd] = b_strides[k];
+            ++v.nd;
+        }
+    }
+    if (v.nd == 0) {
+        v.nd = 1;
+        v.shape[0] = 1;
+        v.sa[0] = v.sb[0] = 1;
+    }
+    if (v.nd == 1 && v.sa[0] == 1 && v.sb[0] == 1) return bee_b200_ew_binary(op, dt, a, b, out, static_cast<size_t>(n), stream);
+    cudaStream_t st = as_stream(stream);
+    switch (dt) {
+    case DT_U8: return dispatch_binary_strided<uint8_t>(op, a, b, out, v, st);
+    case DT_I32: return dispatch_binary_strided<int32_t>(op, a, b, out, v, st);
+    case DT_I64: return dispatch_binary_strided<int64_t>(op, a, b, out, v, st);
+    case DT_F32: return dispatch_binary_strided<float>(op, a, b, out, v, st);
+    case DT_F64: return dispatch_binary_strided<double>(op, a, b, out, v, st);
+    case DT_BF16: return dispatch_binary_strided<bf16_t>(op, a, b, out, v, st);
+    default: return fail(cudaErrorInvalidValue, "ew_binary_strided: unsupported dtype %d", dt);
     }
 }
 

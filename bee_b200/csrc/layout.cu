@@ -1,0 +1,294 @@
+// Layout kernels: 2-D transpose and strided-view materialisation.
+//
+// bee_b200_transpose_2d replaces ops_transpose_2d (Bee/CUDA/Ops/OpsBridge.hpp:37-38,
+// Bee/CUDA/Ops/Transpose.cu:110-145): dst[i, j] = src[j, i] for a contiguous
+// [rows, cols] src.  bee_b200_strided_copy is the device path for
+// Tensor::contiguous() of an arbitrary view, which the reference serves with a
+// 2-D transpose fast path and otherwise a device -> host -> device round trip
+// (Bee/Tensor/Core/Tensor.cpp:468-508).
+//
+// Both are pure data movement (HBM-bound: every byte read once, written once)
+// and move elements by their size only, so every dtype of one size shares a
+// kernel.  Three kernels:
+//   * transpose_tile_kernel: dst[b][p][q] = src[b*sb + q*ld + p] through a
+//     64 x 64 shared-memory tile, 16-byte global loads and stores on both
+//     sides when the rows allow it (batched: a transposed view of the two
+//     innermost dims, such as K^T of [heads, seq, d]);
+//   * rows_copy_kernel: views whose innermost dim is contiguous (slices such
+//     as the halves of a RoPE head) — 16-byte vectors along each row;
+//   * gather_kernel: any other view, one element at a time.
+// A view's dims are first simplified: size-1 dims dropped, neighbours merged
+// where the outer stride equals inner stride x inner extent.
+#include <algorithm>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace bee_b200 {
+
+namespace {
+
+constexpr int kMaxDims = 8;
+constexpr int kTile = 64;
+
+template <int ES> struct Word;
+template <> struct Word<1> { using T = uint8_t; };
+template <> struct Word<2> { using T = uint16_t; };
+template <> struct Word<4> { using T = uint32_t; };
+template <> struct Word<8> { using T = unsigned long long; };
+
+template <int ES>
+__global__ void __launch_bounds__(256) transpose_tile_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                                             long long batch, long long P, long long Q, long long ld,
+                                                             long long sb, int src_vec, int dst_vec) {
+    using T = typename Word<ES>::T;
+    constexpr int VEC = 16 / ES;            // elements per 16-byte vector
+    constexpr int VPR = kTile / VEC;        // vectors per tile row
+    __shared__ T tile[kTile][kTile + 1];    // [q][p]; the pad keeps column reads at most 2-way conflicted
+    const T* s = reinterpret_cast<const T*>(src);
+    T* d = reinterpret_cast<T*>(dst);
+    const long long tp = (P + kTile - 1) / kTile, tq = (Q + kTile - 1) / kTile;
+    const long long tiles = batch * tp * tq;
+    for (long long t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const long long b = t / (tp * tq);
+        const long long rem = t - b * tp * tq;
+        const long long q0 = (rem / tp) * kTile, p0 = (rem % tp) * kTile;
+        const T* sbase = s + b * sb;
+        for (int v = threadIdx.x; v < kTile * VPR; v += blockDim.x) {
+            const int qq = v / VPR, pv = v % VPR;
+            const long long q = q0 + qq, p = p0 + pv * VEC;
+            if (q >= Q) continue;
+            const T* g = sbase + q * ld + p;
+            if (src_vec && p + VEC <= P) {
+                const uint4 w = __ldcs(reinterpret_cast<const uint4*>(g));
+                T e[VEC];
+                memcpy(e, &w, 16);
+#pragma unroll
+                for (int j = 0; j < VEC; ++j) tile[qq][pv * VEC + j] = e[j];
+            } else {
+                for (int j = 0; j < VEC && p + j < P; ++j) tile[qq][pv * VEC + j] = g[j];
+            }
+        }
+        __syncthreads();
+        T* dbase = d + b * P * Q;
+        for (int v = threadIdx.x; v < kTile * VPR; v += blockDim.x) {
+            const int pp = v / VPR, qv = v % VPR;
+            const long long p = p0 + pp, q = q0 + qv * VEC;
+            if (p >= P) continue;
+            T* g = dbase + p * Q + q;
+            if (dst_vec && q + VEC <= Q) {
+                T e[VEC];
+#pragma unroll
+                for (int j = 0; j < VEC; ++j) e[j] = tile[qv * VEC + j][pp];
+                uint4 w;
+                memcpy(&w, e, 16);
+                __stcs(reinterpret_cast<uint4*>(g), w);
+            } else {
+                for (int j = 0; j < VEC && q + j < Q; ++j) g[j] = tile[qv * VEC + j][pp];
+            }
+        }
+        __syncthreads();
+    }
+}
+
+struct ViewDims {
+    int nd;                       // outer dims (all but the innermost)
+    long long shape[kMaxDims];    // outer extents
+    long long stride[kMaxDims];   // outer strides, elements
+};
+
+// Source offset (elements) of outer row `r` of the view.
+__device__ __forceinline__ long long row_offset(long long r, const ViewDims& v) {
+    long long off = 0;
+    for (int i = v.nd - 1; i >= 0; --i) {
+        const long long x = r % v.shape[i];
+        r /= v.shape[i];
+        off += x * v.stride[i];
+    }
+    return off;
+}
+
+// dst [rows, L] contiguous; row r of the view starts at src + row_offset(r); its
+// L elements are contiguous.  Work item = one 16-byte vector of a row.
+template <int ES>
+__global__ void __launch_bounds__(256) rows_copy_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                                        long long rows, long long L, ViewDims v, int vec_ok) {
+    using T = typename Word<ES>::T;
+    constexpr int VEC = 16 / ES;
+    const T* s = reinterpret_cast<const T*>(src);
+    T* d = reinterpret_cast<T*>(dst);
+    const long long per_row = (L + VEC - 1) / VEC;
+    const long long items = rows * per_row;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < items; i += stride) {
+        const long long r = i / per_row, c = (i - r * per_row) * VEC;
+        const T* g = s + row_offset(r, v) + c;
+        T* o = d + r * L + c;
+        if (vec_ok && c + VEC <= L) {
+            __stcs(reinterpret_cast<uint4*>(o), __ldcs(reinterpret_cast<const uint4*>(g)));
+        } else {
+            for (int j = 0; j < VEC && c + j < L; ++j) o[j] = g[j];
+        }
+    }
+}
+
+// Any view: one element per work item; the innermost dim has stride `inner_stride`.
+template <int ES>
+__global__ void __launch_bounds__(256) gather_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                                     long long n, long long L, long long inner_stride, ViewDims v) {
+    using T = typename Word<ES>::T;
+    const T* s = reinterpret_cast<const T*>(src);
+    T* d = reinterpret_cast<T*>(dst);
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const long long r = i / L, c = i - r * L;
+        d[i] = s[row_offset(r, v) + c * inner_stride];
+    }
+}
+
+int elem_size(int dt) {
+    switch (dt) {
+    case DT_BOOL: case DT_U8: case DT_I8: return 1;
+    case DT_F16: case DT_BF16: return 2;
+    case DT_I32: case DT_F32: return 4;
+    case DT_I64: case DT_F64: return 8;
+    default: return 0;
+    }
+}
+
+unsigned persistent_grid(long long work, int per_sm) {
+    const long long cap = static_cast<long long>(sm_count()) * per_sm;
+    return static_cast<unsigned>(std::max(1LL, std::min(work, cap)));
+}
+
+template <int ES>
+int launch_transpose(const void* src, void* dst, long long batch, long long P, long long Q, long long ld, long long sb,
+                     cudaStream_t st) {
+    const int src_vec = aligned16(src) && (ld * ES) % 16 == 0 && (sb * ES) % 16 == 0;
+    const int dst_vec = aligned16(dst) && (Q * ES) % 16 == 0;
+    const long long tiles = batch * ((P + kTile - 1) / kTile) * ((Q + kTile - 1) / kTile);
+    transpose_tile_kernel<ES><<<persistent_grid(tiles, 8), 256, 0, st>>>(
+        static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), batch, P, Q, ld, sb, src_vec, dst_vec);
+    return launch_status("transpose");
+}
+
+int transpose_by_size(int es, const void* src, void* dst, long long batch, long long P, long long Q, long long ld,
+                      long long sb, cudaStream_t st) {
+    switch (es) {
+    case 1: return launch_transpose<1>(src, dst, batch, P, Q, ld, sb, st);
+    case 2: return launch_transpose<2>(src, dst, batch, P, Q, ld, sb, st);
+    case 4: return launch_transpose<4>(src, dst, batch, P, Q, ld, sb, st);
+    default: return launch_transpose<8>(src, dst, batch, P, Q, ld, sb, st);
+    }
+}
+
+template <int ES>
+int launch_rows(const void* src, void* dst, long long rows, long long L, const ViewDims& v, cudaStream_t st) {
+    bool vec_ok = aligned16(src) && aligned16(dst) && (L * ES) % 16 == 0;
+    for (int i = 0; i < v.nd; ++i) vec_ok = vec_ok && (v.stride[i] * ES) % 16 == 0;
+    const long long items = rows * ((L + 16 / ES - 1) / (16 / ES));
+    rows_copy_kernel<ES><<<persistent_grid((items + 255) / 256, 8), 256, 0, st>>>(
+        static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, L, v, vec_ok ? 1 : 0);
+    return launch_status("strided_copy(rows)");
+}
+
+template <int ES>
+int launch_gather(const void* src, void* dst, long long n, long long L, long long inner_stride, const ViewDims& v,
+                  cudaStream_t st) {
+    gather_kernel<ES><<<persistent_grid((n + 255) / 256, 8), 256, 0, st>>>(
+        static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), n, L, inner_stride, v);
+    return launch_status("strided_copy(gather)");
+}
+
+}  // namespace
+}  // namespace bee_b200
+
+using namespace bee_b200;
+
+extern "C" {
+
+int bee_b200_transpose_2d(int dt, const void* src, void* dst, size_t rows, size_t cols, bee_b200_stream_t stream) {
+    const int es = elem_size(dt);
+    if (es == 0) return fail(cudaErrorInvalidValue, "transpose_2d: unsupported dtype %d", dt);
+    if (rows == 0 || cols == 0) return ok();
+    if (!src || !dst) return fail(cudaErrorInvalidValue, "transpose_2d: null pointer");
+    if (rows > (1ull << 40) || cols > (1ull << 40)) return fail(cudaErrorInvalidValue, "transpose_2d: extent too large");
+    // dst [cols, rows]: dst[p][q] = src[q * cols + p]
+    return transpose_by_size(es, src, dst, 1, static_cast<long long>(cols), static_cast<long long>(rows),
+                             static_cast<long long>(cols), 0, as_stream(stream));
+}
+
+int bee_b200_strided_copy(int dt, const void* src, int ndim, const int64_t* shape, const int64_t* strides, void* dst,
+                          bee_b200_stream_t stream) {
+    const int es = elem_size(dt);
+    if (es == 0) return fail(cudaErrorInvalidValue, "strided_copy: unsupported dtype %d", dt);
+    if (ndim < 0 || ndim > kMaxDims) return fail(cudaErrorInvalidValue, "strided_copy: ndim %d outside [0, %d]", ndim, kMaxDims);
+    if (ndim > 0 && (!shape || !strides)) return fail(cudaErrorInvalidValue, "strided_copy: null shape or strides");
+    long long n = 1;
+    for (int i = 0; i < ndim; ++i) {
+        if (shape[i] < 0) return fail(cudaErrorInvalidValue, "strided_copy: negative extent in dim %d", i);
+        n *= shape[i];
+        if (n > (1LL << 46)) return fail(cudaErrorInvalidValue, "strided_copy: too many elements");
+    }
+    if (n == 0) return ok();
+    if (!src || !dst) return fail(cudaErrorInvalidValue, "strided_copy: null pointer");
+    cudaStream_t st = as_stream(stream);
+
+    // simplify: drop size-1 dims, merge neighbours that are contiguous with each other
+    long long sh[kMaxDims], sd[kMaxDims];
+    int nd = 0;
+    for (int i = 0; i < ndim; ++i) {
+        if (shape[i] == 1) continue;
+        if (nd > 0 && sd[nd - 1] == strides[i] * shape[i]) {
+            sh[nd - 1] *= shape[i];
+            sd[nd - 1] = strides[i];
+        } else {
+            sh[nd] = shape[i];
+            sd[nd] = strides[i];
+            ++nd;
+        }
+    }
+    if (nd == 0) {  // a single element
+        sh[0] = 1;
+        sd[0] = 1;
+        nd = 1;
+    }
+    if (nd == 1 && sd[0] == 1) {
+        cudaError_t e = cudaMemcpyAsync(dst, src, static_cast<size_t>(n) * es, cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) return fail(static_cast<int>(e), "strided_copy: %s", cudaGetErrorString(e));
+        return ok();
+    }
+    // a transposed pair of innermost dims: [.., Q-dim stride 1 .., P-dim] -> batched tiles
+    if (nd >= 2 && sd[nd - 2] == 1 && sd[nd - 1] != 1 && (nd == 2 || nd == 3)) {
+        const long long P = sh[nd - 2], Q = sh[nd - 1];
+        const long long ld = sd[nd - 1];
+        const long long batch = nd == 3 ? sh[0] : 1;
+        const long long sb = nd == 3 ? sd[0] : 0;
+        // dst[b][p][q] = src[b*sb + q*ld + p] with dst [batch][P][Q]; the tile
+        // kernel names the dst rows p and the dst columns q.
+        return transpose_by_size(es, src, dst, batch, P, Q, ld, sb, st);
+    }
+    ViewDims v{};
+    v.nd = nd - 1;
+    for (int i = 0; i < nd - 1; ++i) {
+        v.shape[i] = sh[i];
+        v.stride[i] = sd[i];
+    }
+    const long long L = sh[nd - 1], rows = n / L;
+    if (sd[nd - 1] == 1) {
+        switch (es) {
+        case 1: return launch_rows<1>(src, dst, rows, L, v, st);
+        case 2: return launch_rows<2>(src, dst, rows, L, v, st);
+        case 4: return launch_rows<4>(src, dst, rows, L, v, st);
+        default: return launch_rows<8>(src, dst, rows, L, v, st);
+        }
+    }
+    switch (es) {
+    case 1: return launch_gather<1>(src, dst, n, L, sd[nd - 1], v, st);
+    case 2: return launch_gather<2>(src, dst, n, L, sd[nd - 1], v, st);
+    case 4: return launch_gather<4>(src, dst, n, L, sd[nd - 1], v, st);
+    default: return launch_gather<8>(src, dst, n, L, sd[nd - 1], v, st);
+    }
+}
+
+}  // extern "C"

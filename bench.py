@@ -489,6 +489,43 @@ def run_extras(args, d, dev, stream, peaks):
                                 1024, 1024, st))
         out["gemm_f32_1024"] = {"ms": round(ms, 4), "TFLOP/s": round(2.0 * 1024 ** 3 / (ms / 1e3) / 1e12, 2),
                                 "unit": "TFLOP/s (per GPU)", "path": "SIMT fp32 (parity config, rel tol 1e-4)"}
+        del a32, b32, c32
+
+        # layout and broadcast ops on the [8192, 8192] fp32 shard (HBM-bound, 2 x 256 MiB moved)
+        import ctypes
+        x = torch.randn(8192, 8192, device=dev, generator=g)
+        y = torch.empty_like(x)
+        ms = timed(lambda: call("bee_b200_transpose_2d", _capi.F32, x.data_ptr(), y.data_ptr(), 8192, 8192, st))
+        nbytes = 2 * 8192 * 8192 * 4
+        gbs = d.world * nbytes / (ms / 1e3) / 1e9
+        out["transpose_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                     "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                     "bytes_per_gpu": nbytes, "scaling": "weak"}
+        rmax = torch.empty(8192, device=dev)
+        call("bee_b200_reduce_axis", _capi.MAX, _capi.F32, x.data_ptr(), rmax.data_ptr(), 8192, 8192, 1, st)
+        shp = (ctypes.c_int64 * 2)(8192, 8192)
+        sa = (ctypes.c_int64 * 2)(8192, 1)
+        sb = (ctypes.c_int64 * 2)(1, 0)
+        ms = timed(lambda: call("bee_b200_ew_binary_strided", _capi.SUB, _capi.F32, 2, shp, x.data_ptr(), sa,
+                                rmax.data_ptr(), sb, y.data_ptr(), st))
+        nbytes = 2 * 8192 * 8192 * 4 + 8192 * 4
+        gbs = d.world * nbytes / (ms / 1e3) / 1e9
+        out["bcast_sub_rowmax_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                            "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                            "op": "x[8192, 8192] - rowmax[8192, 1] (broadcast, stride 0)",
+                                            "bytes_per_gpu": nbytes, "scaling": "weak"}
+        kq = torch.randn(256, 2048, 128, device=dev, generator=g).to(torch.bfloat16)
+        kt = torch.empty(256, 128, 2048, device=dev, dtype=torch.bfloat16)
+        vsh = (ctypes.c_int64 * 3)(256, 128, 2048)
+        vst = (ctypes.c_int64 * 3)(2048 * 128, 1, 128)
+        ms = timed(lambda: call("bee_b200_strided_copy", _capi.BF16, kq.data_ptr(), 3, vsh, vst, kt.data_ptr(), st))
+        nbytes = 2 * 256 * 2048 * 128 * 2
+        gbs = d.world * nbytes / (ms / 1e3) / 1e9
+        out["contiguous_kt_bf16"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                     "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                     "op": "contiguous() of K^T, K [256, 2048, 128] bf16 (128 MiB each way)",
+                                     "bytes_per_gpu": nbytes, "scaling": "weak"}
+        del x, y, rmax, kq, kt
     stream.synchronize()
     return out
 

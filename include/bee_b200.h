@@ -71,6 +71,17 @@ BEE_B200_API int bee_b200_stream_synchronize(bee_b200_stream_t stream);
  * tensor::cuda::ew_binary (Bee/Tensor/Cuda/Backend.hpp:51). */
 BEE_B200_API int bee_b200_ew_binary(int op, int dt, const void* a, const void* b, void* out, size_t n,
                        bee_b200_stream_t stream);
+/* New: the CUDA side of broadcasting binary ops, which the reference rejects
+ * on CUDA (Bee/Tensor/Ops/ElementWise.cpp:110-111) and runs on the CPU with
+ * numpy-style broadcasting (Bee/Tensor/Ops/Broadcast.cpp).  out is a
+ * contiguous tensor of `shape` (ndim <= 8); a and b are strided views of that
+ * shape (strides in elements; 0 on a broadcast dim), so the caller's broadcast
+ * (or any non-contiguous operand) needs no materialisation.  Same ops, dtypes
+ * and arithmetic as bee_b200_ew_binary. */
+BEE_B200_API int bee_b200_ew_binary_strided(int op, int dt, int ndim, const int64_t* shape, const void* a,
+                                            const int64_t* a_strides, const void* b, const int64_t* b_strides,
+                                            void* out, bee_b200_stream_t stream);
+
 
 /* dst[i] = op(src[i]).  Neg/Abs: I32, I64, F32, F64, BF16; Sqrt/Exp/Log: F32,
  * F64, BF16.  Replaces ops_unary (Bee/CUDA/Ops/OpsBridge.hpp:28) behind
@@ -192,6 +203,21 @@ BEE_B200_API int bee_b200_bmm(int dt_in, int dt_out, const void* A, const void* 
  * bee_b200_bmm).  New: the reference has no attention. */
 BEE_B200_API int bee_b200_attention(int dt, const void* q, const void* k, const void* v, void* o, size_t heads,
                                     size_t seq, size_t head_dim, float scale, bee_b200_stream_t stream);
+
+/* ------------------------------------------------- layout
+ * Replaces ops_transpose_2d (Bee/CUDA/Ops/OpsBridge.hpp:37-38): dst[i, j] =
+ * src[j, i] for a contiguous [rows, cols] src (dst is [cols, rows]).  Every
+ * dtype code (moved by element size); size 0 succeeds without work. */
+BEE_B200_API int bee_b200_transpose_2d(int dt, const void* src, void* dst, size_t rows, size_t cols,
+                                       bee_b200_stream_t stream);
+
+/* New: the device path of Tensor::contiguous() for any view, which the
+ * reference serves with a device -> host -> device round trip except for the
+ * 2-D transpose (Bee/Tensor/Core/Tensor.cpp:468-508).  `src` points at the
+ * view's first element (storage + offset); shape and strides (in elements,
+ * ndim <= 8) describe the view; dst receives the elements in row-major order. */
+BEE_B200_API int bee_b200_strided_copy(int dt, const void* src, int ndim, const int64_t* shape, const int64_t* strides,
+                                       void* dst, bee_b200_stream_t stream);
 
 /* ------------------------------------------------- multi-GPU (split-K GEMM)
  * New: the reference has no multi-GPU code.  One process per GPU.  C = A . B

@@ -161,6 +161,21 @@ class Oracle:
         self.lib.oracle_attention_f32(_p(q), _p(k), _p(v), _p(o), heads, seq, hd, scale, _p(work))
         return o
 
+    @staticmethod
+    def strided_gather(flat: np.ndarray, offset: int, shape, strides) -> np.ndarray:
+        """Row-major materialisation of the view (offset, shape, strides in
+        elements) of the 1-D buffer `flat`: out[i0, .., ik] = flat[offset +
+        sum_d i_d * strides[d]] — the stride loop of the reference's
+        contiguous_copy_into (Bee/Tensor/Core/Tensor.cpp:119-147), as numpy
+        index arithmetic."""
+        flat = np.asarray(flat).reshape(-1)
+        idx = np.full(tuple(shape), offset, dtype=np.int64)
+        for d, (n, st) in enumerate(zip(shape, strides)):
+            sh = [1] * len(shape)
+            sh[d] = n
+            idx = idx + (np.arange(n, dtype=np.int64) * st).reshape(sh)
+        return flat[idx]
+
 
 class Reference:
     """The reference's own CPU path (oracle/_ref/libbee_ref.so, built from its sources)."""
@@ -181,6 +196,8 @@ class Reference:
             "bref_rms_norm_f32": [_vp, _vp, _vp, _i64, _i64, _f, _i],
             "bref_rope_f32": [_vp, _vp, _i64, _i64, _i64, _i64, _d, _i64, _i],
             "bref_attention_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _f, _i],
+            "bref_view_copy_f32": [_vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i],
+            "bref_binary_bcast_f32": [_i, _vp, _vp, _vp, _vp, _i, _vp, _i],
         }.items():
             fn = getattr(L, name)
             fn.argtypes = args
@@ -254,6 +271,39 @@ class Reference:
         heads, seq, hd = q.shape
         t = self._chk(self.lib.bref_attention_f32(_p(q), _p(k), _p(v), _p(o), heads, seq, hd, scale, reps), "attention")
         return o, t
+
+
+    def binary_bcast_f32(self, op, a, b, reps=1):
+        """a op b with broadcasting (equal ranks), on the reference's CPU path."""
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        out = np.empty(np.broadcast_shapes(a.shape, b.shape), np.float32)
+        ash = np.array(a.shape, np.int64)
+        bsh = np.array(b.shape, np.int64)
+        t = self._chk(self.lib.bref_binary_bcast_f32(op, _p(a), _p(ash), _p(b), _p(bsh), a.ndim, _p(out), reps),
+                      "binary broadcast")
+        return out, t
+
+    def view_copy_f32(self, x, perm, slices=None, reps=1):
+        """permute(perm), then slice(d, start, end, step) per dim of `slices`
+        (None = whole dim), then contiguous(), on the reference's CPU path."""
+        x = np.ascontiguousarray(x, np.float32)
+        nd = x.ndim
+        shape = np.array(x.shape, np.int64)
+        permv = np.array(perm, np.int32)
+        st = np.zeros(nd, np.int64)
+        en = np.zeros(nd, np.int64)
+        sp = np.zeros(nd, np.int64)
+        out_shape = [x.shape[p] for p in perm]
+        for d, sl in enumerate(slices or [None] * nd):
+            if sl is None:
+                continue
+            st[d], en[d], sp[d] = sl
+            out_shape[d] = len(range(sl[0], sl[1], sl[2]))
+        out = np.empty(out_shape, np.float32)
+        t = self._chk(self.lib.bref_view_copy_f32(_p(x), nd, _p(shape), _p(permv), _p(st), _p(en), _p(sp), _p(out),
+                                                  reps), "view_copy")
+        return out, t
 
 
 def reference_available() -> bool:

@@ -263,4 +263,51 @@ double bref_attention_f32(const float* q, const float* k, const float* v, float*
     return t;
 }
 
+
+// permute(perm) then, for each dim d with step[d] > 0, slice(d, start[d],
+// end[d], step[d]), then contiguous() — the reference's CPU view
+// materialisation (Bee/Tensor/Core/Tensor.cpp:468-546) of an fp32 tensor.
+double bref_view_copy_f32(const float* x, int ndim, const int64_t* shape, const int* perm, const int64_t* start,
+                          const int64_t* end, const int64_t* step, float* out, int reps) {
+    Shape s(shape, shape + ndim);
+    Tensor t = make(s, DType::F32, x);
+    Tensor res;
+    double sec = timed(reps, [&] {
+        auto v = t.permute(std::span<const int>(perm, static_cast<size_t>(ndim)));
+        if (!okr(v, "permute")) return false;
+        Tensor cur = *v;
+        for (int d = 0; d < ndim; ++d) {
+            if (step[d] <= 0) continue;
+            auto sl = cur.slice(d, start[d], end[d], step[d]);
+            if (!okr(sl, "slice")) return false;
+            cur = *sl;
+        }
+        auto c = cur.contiguous();
+        if (!okr(c, "contiguous")) return false;
+        res = *c;
+        return true;
+    });
+    if (sec >= 0) std::memcpy(out, res.data_ptr(), static_cast<size_t>(res.numel()) * sizeof(float));
+    return sec;
+}
+
+
+// Broadcasting binary op on the reference's CPU path (Bee/Tensor/Ops/ElementWise.cpp,
+// shapes aligned from the right as in Bee/Tensor/Ops/Broadcast.cpp); the
+// output shape is the broadcast of a_shape and b_shape (both of rank ndim).
+double bref_binary_bcast_f32(int op, const float* a, const int64_t* a_shape, const float* b, const int64_t* b_shape,
+                             int ndim, float* out, int reps) {
+    Tensor A = make(Shape(a_shape, a_shape + ndim), DType::F32, a);
+    Tensor B = make(Shape(b_shape, b_shape + ndim), DType::F32, b);
+    Tensor C;
+    double t = timed(reps, [&] {
+        auto r = op == 0 ? add(A, B) : op == 1 ? sub(A, B) : op == 2 ? mul(A, B) : div(A, B);
+        if (!okr(r, "binary broadcast")) return false;
+        C = *r;
+        return true;
+    });
+    if (t >= 0) copy_out(C, out);
+    return t;
+}
+
 }  // extern "C"
