@@ -53,6 +53,7 @@ SIGNATURES = {
     "bee_b200_reduce_global": [_i, _i, _vp, _vp, _sz, _vp],
     "bee_b200_reduce_global_noalloc": [_i, _i, _vp, _vp, _sz, _vp],
     "bee_b200_reduce_axis": [_i, _i, _vp, _vp, _sz, _sz, _sz, _vp],
+    "bee_b200_reduce_mean_int": [_i, _vp, _vp, _sz, _sz, _sz, _vp],
     "bee_b200_softmax_rows": [_i, _vp, _vp, _sz, _sz, _vp],
     "bee_b200_softmax_rows_to": [_i, _vp, _i, _vp, _sz, _sz, _vp],
     "bee_b200_rms_norm_rows": [_i, _vp, _vp, _vp, _sz, _sz, _f, _vp],

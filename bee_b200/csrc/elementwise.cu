@@ -137,36 +137,87 @@ __device__ __forceinline__ void load_chunk(const S* p, long long inner, bool vec
 }
 
 template <typename S, int OP>
+__device__ __forceinline__ void strided_chunk(const S* __restrict__ a, const S* __restrict__ b, S* __restrict__ o,
+                                              long long c, long long L, long long ia, long long ib, int a_vec,
+                                              int b_vec, int o_vec) {
+    constexpr int E = 16 / sizeof(S);
+    const int cnt = static_cast<int>(L - c < E ? L - c : E);
+    Pack16<S> va, vb, vo;
+    load_chunk<S>(a + c * ia, ia, a_vec, cnt, va);
+    load_chunk<S>(b + c * ib, ib, b_vec, cnt, vb);
+#pragma unroll
+    for (int k = 0; k < E; ++k) vo.s[k] = from_c<S>(bin<OP>(to_c(va.s[k]), to_c(vb.s[k])));
+    if (o_vec && cnt == E) {
+        __stcs(reinterpret_cast<uint4*>(o + c), vo.v);
+    } else {
+#pragma unroll
+        for (int k = 0; k < E; ++k)
+            if (k < cnt) o[c + k] = vo.s[k];
+    }
+}
+
+// ROW_MODE (rows of at least 4 KiB): one CTA per output row at a time, the two
+// operand row offsets computed once per row, UNROLL chunks per thread with
+// their loads issued first.  Otherwise a work item is one chunk of a row.
+template <typename S, int OP, bool ROW_MODE>
 __global__ void __launch_bounds__(kThreads) binary_strided_kernel(const S* __restrict__ a, const S* __restrict__ b,
                                                                   S* __restrict__ out, long long rows, long long L,
                                                                   BcastDims d, long long ia, long long ib, int a_vec,
                                                                   int b_vec, int o_vec) {
     constexpr int E = 16 / sizeof(S);
     const long long per_row = (L + E - 1) / E;
-    const long long items = rows * per_row;
-    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < items; i += stride) {
-        long long r = i / per_row;
-        const long long c = (i - r * per_row) * E;
-        const long long orow = r;
-        long long oa = 0, ob = 0;
-        for (int k = d.nd - 1; k >= 0; --k) {
-            const long long x = r % d.shape[k];
-            r /= d.shape[k];
-            oa += x * d.sa[k];
-            ob += x * d.sb[k];
-        }
-        const int cnt = static_cast<int>(L - c < E ? L - c : E);
-        Pack16<S> va, vb, vo;
-        load_chunk<S>(a + oa + c * ia, ia, a_vec, cnt, va);
-        load_chunk<S>(b + ob + c * ib, ib, b_vec, cnt, vb);
+    if constexpr (ROW_MODE) {
+        for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
+            long long r = row, oa = 0, ob = 0;
+            for (int k = d.nd - 1; k >= 0; --k) {
+                const long long x = r % d.shape[k];
+                r /= d.shape[k];
+                oa += x * d.sa[k];
+                ob += x * d.sb[k];
+            }
+            const S* ar = a + oa;
+            const S* br = b + ob;
+            S* orow = out + row * L;
+            long long j = threadIdx.x;
+            for (; j + (kUnroll - 1) * kThreads < per_row; j += kUnroll * kThreads) {
+                Pack16<S> va[kUnroll], vb[kUnroll];
 #pragma unroll
-        for (int k = 0; k < E; ++k) vo.s[k] = from_c<S>(bin<OP>(to_c(va.s[k]), to_c(vb.s[k])));
-        S* o = out + orow * L + c;
-        if (o_vec && cnt == E) {
-            __stcs(reinterpret_cast<uint4*>(o), vo.v);
-        } else {
-            for (int k = 0; k < cnt; ++k) o[k] = vo.s[k];
+                for (int u = 0; u < kUnroll; ++u) {
+                    const long long c = (j + u * kThreads) * E;
+                    load_chunk<S>(ar + c * ia, ia, a_vec, E, va[u]);
+                    load_chunk<S>(br + c * ib, ib, b_vec, E, vb[u]);
+                }
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u) {
+                    Pack16<S> vo;
+#pragma unroll
+                    for (int k = 0; k < E; ++k) vo.s[k] = from_c<S>(bin<OP>(to_c(va[u].s[k]), to_c(vb[u].s[k])));
+                    const long long c = (j + u * kThreads) * E;
+                    if (o_vec) {
+                        __stcs(reinterpret_cast<uint4*>(orow + c), vo.v);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < E; ++k) orow[c + k] = vo.s[k];
+                    }
+                }
+            }
+            for (; j < per_row; j += kThreads) strided_chunk<S, OP>(ar, br, orow, j * E, L, ia, ib, a_vec, b_vec, o_vec);
+        }
+    } else {
+        const long long items = rows * per_row;
+        const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+        for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < items; i += stride) {
+            long long r = i / per_row;
+            const long long c = (i - r * per_row) * E;
+            const long long orow = r;
+            long long oa = 0, ob = 0;
+            for (int k = d.nd - 1; k >= 0; --k) {
+                const long long x = r % d.shape[k];
+                r /= d.shape[k];
+                oa += x * d.sa[k];
+                ob += x * d.sb[k];
+            }
+            strided_chunk<S, OP>(a + oa, b + ob, out + orow * L, c, L, ia, ib, a_vec, b_vec, o_vec);
         }
     }
 }
@@ -330,10 +381,17 @@ static void launch_binary_strided(const void* a, const void* b, void* out, const
         b_vec = b_vec && (v.sb[k] * static_cast<long long>(sizeof(S))) % 16 == 0;
     }
     const int o_vec = aligned16(out) && (L * static_cast<long long>(sizeof(S))) % 16 == 0;
-    const long long items = rows * ((L + E - 1) / E);
-    binary_strided_kernel<S, OP><<<grid_for(static_cast<size_t>(items)), kThreads, 0, st>>>(
-        static_cast<const S*>(a), static_cast<const S*>(b), static_cast<S*>(out), rows, L, d, ia, ib, a_vec ? 1 : 0,
-        b_vec ? 1 : 0, o_vec);
+    const long long per_row = (L + E - 1) / E;
+    if (per_row >= 256) {
+        const long long cap = static_cast<long long>(sm_count()) * 8;
+        binary_strided_kernel<S, OP, true><<<static_cast<unsigned>(rows < cap ? rows : cap), kThreads, 0, st>>>(
+            static_cast<const S*>(a), static_cast<const S*>(b), static_cast<S*>(out), rows, L, d, ia, ib,
+            a_vec ? 1 : 0, b_vec ? 1 : 0, o_vec);
+    } else {
+        binary_strided_kernel<S, OP, false><<<grid_for(static_cast<size_t>(rows * per_row)), kThreads, 0, st>>>(
+            static_cast<const S*>(a), static_cast<const S*>(b), static_cast<S*>(out), rows, L, d, ia, ib,
+            a_vec ? 1 : 0, b_vec ? 1 : 0, o_vec);
+    }
 }
 
 template <typename S>

@@ -11,7 +11,7 @@
 // and move elements by their size only, so every dtype of one size shares a
 // kernel.  Three kernels:
 //   * transpose_tile_kernel: dst[b][p][q] = src[b*sb + q*ld + p] through a
-//     64 x 64 shared-memory tile, 16-byte global loads and stores on both
+//     16 KiB shared-memory tile, 16-byte global loads and stores on both
 //     sides when the rows allow it (batched: a transposed view of the two
 //     innermost dims, such as K^T of [heads, seq, d]);
 //   * rows_copy_kernel: views whose innermost dim is contiguous (slices such
@@ -29,7 +29,6 @@ namespace bee_b200 {
 namespace {
 
 constexpr int kMaxDims = 8;
-constexpr int kTile = 64;
 
 template <int ES> struct Word;
 template <> struct Word<1> { using T = uint8_t; };
@@ -37,42 +36,71 @@ template <> struct Word<2> { using T = uint16_t; };
 template <> struct Word<4> { using T = uint32_t; };
 template <> struct Word<8> { using T = unsigned long long; };
 
+// Tile shape per element size: 16 KiB of data, TQ source rows of TP elements.
+// Both sides move 1024 16-byte vectors per tile, four per thread, all loads of a
+// thread issued before its shared-memory writes.  A warp instruction covers 4
+// rows x 8 vectors (128 contiguous bytes per row) on both sides, which with a
+// one-element row pad keeps the scalar shared-memory accesses at most 2-way
+// conflicted (4-way for 1-byte elements).
+template <int ES> struct TileShape;
+template <> struct TileShape<1> { static constexpr int TP = 128, TQ = 128, PAD = 4; };
+template <> struct TileShape<2> { static constexpr int TP = 64, TQ = 128, PAD = 2; };
+template <> struct TileShape<4> { static constexpr int TP = 64, TQ = 64, PAD = 1; };
+template <> struct TileShape<8> { static constexpr int TP = 32, TQ = 64, PAD = 1; };
+
 template <int ES>
 __global__ void __launch_bounds__(256) transpose_tile_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
                                                              long long batch, long long P, long long Q, long long ld,
                                                              long long sb, int src_vec, int dst_vec) {
     using T = typename Word<ES>::T;
-    constexpr int VEC = 16 / ES;            // elements per 16-byte vector
-    constexpr int VPR = kTile / VEC;        // vectors per tile row
-    __shared__ T tile[kTile][kTile + 1];    // [q][p]; the pad keeps column reads at most 2-way conflicted
+    using Sh = TileShape<ES>;
+    constexpr int TP = Sh::TP, TQ = Sh::TQ, PITCH = TP + Sh::PAD;
+    constexpr int VEC = 16 / ES;
+    constexpr int VPRL = TP / VEC, VPRS = TQ / VEC;  // vectors per source row / per destination row
+    constexpr int SEGL = VPRL / 8, SEGS = VPRS / 8;  // 8-vector segments per row
+    constexpr int ITERS = (TQ * VPRL) / 256;         // = (TP * VPRS) / 256 = 4
+    static_assert(TQ * VPRL == 1024 && TP * VPRS == 1024, "16 KiB tiles");
+    __shared__ T tile[TQ][PITCH];  // [q][p]
     const T* s = reinterpret_cast<const T*>(src);
     T* d = reinterpret_cast<T*>(dst);
-    const long long tp = (P + kTile - 1) / kTile, tq = (Q + kTile - 1) / kTile;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const long long tp = (P + TP - 1) / TP, tq = (Q + TQ - 1) / TQ;
     const long long tiles = batch * tp * tq;
     for (long long t = blockIdx.x; t < tiles; t += gridDim.x) {
         const long long b = t / (tp * tq);
         const long long rem = t - b * tp * tq;
-        const long long q0 = (rem / tp) * kTile, p0 = (rem % tp) * kTile;
+        const long long q0 = (rem / tp) * TQ, p0 = (rem % tp) * TP;
         const T* sbase = s + b * sb;
-        for (int v = threadIdx.x; v < kTile * VPR; v += blockDim.x) {
-            const int qq = v / VPR, pv = v % VPR;
+        uint4 w[ITERS];
+#pragma unroll
+        for (int it = 0; it < ITERS; ++it) {
+            const int slot = it * 8 + warp;  // 4 rows x 8 vectors
+            const int qq = (slot / SEGL) * 4 + (lane >> 3), pv = (slot % SEGL) * 8 + (lane & 7);
+            const long long q = q0 + qq, p = p0 + pv * VEC;
+            if (q < Q && src_vec && p + VEC <= P) w[it] = __ldcs(reinterpret_cast<const uint4*>(sbase + q * ld + p));
+        }
+#pragma unroll
+        for (int it = 0; it < ITERS; ++it) {
+            const int slot = it * 8 + warp;
+            const int qq = (slot / SEGL) * 4 + (lane >> 3), pv = (slot % SEGL) * 8 + (lane & 7);
             const long long q = q0 + qq, p = p0 + pv * VEC;
             if (q >= Q) continue;
-            const T* g = sbase + q * ld + p;
             if (src_vec && p + VEC <= P) {
-                const uint4 w = __ldcs(reinterpret_cast<const uint4*>(g));
                 T e[VEC];
-                memcpy(e, &w, 16);
+                memcpy(e, &w[it], 16);
 #pragma unroll
                 for (int j = 0; j < VEC; ++j) tile[qq][pv * VEC + j] = e[j];
             } else {
+                const T* g = sbase + q * ld + p;
                 for (int j = 0; j < VEC && p + j < P; ++j) tile[qq][pv * VEC + j] = g[j];
             }
         }
         __syncthreads();
         T* dbase = d + b * P * Q;
-        for (int v = threadIdx.x; v < kTile * VPR; v += blockDim.x) {
-            const int pp = v / VPR, qv = v % VPR;
+#pragma unroll
+        for (int it = 0; it < ITERS; ++it) {
+            const int slot = it * 8 + warp;
+            const int pp = (slot / SEGS) * 4 + (lane >> 3), qv = (slot % SEGS) * 8 + (lane & 7);
             const long long p = p0 + pp, q = q0 + qv * VEC;
             if (p >= P) continue;
             T* g = dbase + p * Q + q;
@@ -80,9 +108,9 @@ __global__ void __launch_bounds__(256) transpose_tile_kernel(const uint8_t* __re
                 T e[VEC];
 #pragma unroll
                 for (int j = 0; j < VEC; ++j) e[j] = tile[qv * VEC + j][pp];
-                uint4 w;
-                memcpy(&w, e, 16);
-                __stcs(reinterpret_cast<uint4*>(g), w);
+                uint4 o;
+                memcpy(&o, e, 16);
+                __stcs(reinterpret_cast<uint4*>(g), o);
             } else {
                 for (int j = 0; j < VEC && q + j < Q; ++j) g[j] = tile[qv * VEC + j][pp];
             }
@@ -109,8 +137,10 @@ __device__ __forceinline__ long long row_offset(long long r, const ViewDims& v) 
 }
 
 // dst [rows, L] contiguous; row r of the view starts at src + row_offset(r); its
-// L elements are contiguous.  Work item = one 16-byte vector of a row.
-template <int ES>
+// L elements are contiguous.  Long rows (ROW_MODE): one CTA per row at a time,
+// the row offset computed once, four 16-byte vectors in flight per thread.
+// Short rows: work item = one 16-byte vector of a row.
+template <int ES, bool ROW_MODE>
 __global__ void __launch_bounds__(256) rows_copy_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
                                                         long long rows, long long L, ViewDims v, int vec_ok) {
     using T = typename Word<ES>::T;
@@ -118,16 +148,39 @@ __global__ void __launch_bounds__(256) rows_copy_kernel(const uint8_t* __restric
     const T* s = reinterpret_cast<const T*>(src);
     T* d = reinterpret_cast<T*>(dst);
     const long long per_row = (L + VEC - 1) / VEC;
-    const long long items = rows * per_row;
-    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < items; i += stride) {
-        const long long r = i / per_row, c = (i - r * per_row) * VEC;
-        const T* g = s + row_offset(r, v) + c;
-        T* o = d + r * L + c;
-        if (vec_ok && c + VEC <= L) {
-            __stcs(reinterpret_cast<uint4*>(o), __ldcs(reinterpret_cast<const uint4*>(g)));
-        } else {
-            for (int j = 0; j < VEC && c + j < L; ++j) o[j] = g[j];
+    if constexpr (ROW_MODE) {
+        for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+            const T* g = s + row_offset(r, v);
+            T* o = d + r * L;
+            long long c = threadIdx.x;
+            if (vec_ok) {
+                const long long full = L / VEC;
+                for (; c + 3 * 256 < full; c += 4 * 256) {
+                    uint4 x[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) x[u] = __ldcs(reinterpret_cast<const uint4*>(g + (c + u * 256) * VEC));
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) __stcs(reinterpret_cast<uint4*>(o + (c + u * 256) * VEC), x[u]);
+                }
+                for (; c < full; c += 256)
+                    __stcs(reinterpret_cast<uint4*>(o + c * VEC), __ldcs(reinterpret_cast<const uint4*>(g + c * VEC)));
+                for (long long e = full * VEC + threadIdx.x; e < L; e += 256) o[e] = g[e];
+            } else {
+                for (long long e = threadIdx.x; e < L; e += 256) o[e] = g[e];
+            }
+        }
+    } else {
+        const long long items = rows * per_row;
+        const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+        for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < items; i += stride) {
+            const long long r = i / per_row, c = (i - r * per_row) * VEC;
+            const T* g = s + row_offset(r, v) + c;
+            T* o = d + r * L + c;
+            if (vec_ok && c + VEC <= L) {
+                __stcs(reinterpret_cast<uint4*>(o), __ldcs(reinterpret_cast<const uint4*>(g)));
+            } else {
+                for (int j = 0; j < VEC && c + j < L; ++j) o[j] = g[j];
+            }
         }
     }
 }
@@ -166,7 +219,8 @@ int launch_transpose(const void* src, void* dst, long long batch, long long P, l
                      cudaStream_t st) {
     const int src_vec = aligned16(src) && (ld * ES) % 16 == 0 && (sb * ES) % 16 == 0;
     const int dst_vec = aligned16(dst) && (Q * ES) % 16 == 0;
-    const long long tiles = batch * ((P + kTile - 1) / kTile) * ((Q + kTile - 1) / kTile);
+    using Sh = TileShape<ES>;
+    const long long tiles = batch * ((P + Sh::TP - 1) / Sh::TP) * ((Q + Sh::TQ - 1) / Sh::TQ);
     transpose_tile_kernel<ES><<<persistent_grid(tiles, 8), 256, 0, st>>>(
         static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), batch, P, Q, ld, sb, src_vec, dst_vec);
     return launch_status("transpose");
@@ -186,9 +240,14 @@ template <int ES>
 int launch_rows(const void* src, void* dst, long long rows, long long L, const ViewDims& v, cudaStream_t st) {
     bool vec_ok = aligned16(src) && aligned16(dst) && (L * ES) % 16 == 0;
     for (int i = 0; i < v.nd; ++i) vec_ok = vec_ok && (v.stride[i] * ES) % 16 == 0;
-    const long long items = rows * ((L + 16 / ES - 1) / (16 / ES));
-    rows_copy_kernel<ES><<<persistent_grid((items + 255) / 256, 8), 256, 0, st>>>(
-        static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, L, v, vec_ok ? 1 : 0);
+    const long long per_row = (L + 16 / ES - 1) / (16 / ES);
+    if (per_row >= 256) {  // rows of 4 KiB or more: a CTA per row
+        rows_copy_kernel<ES, true><<<persistent_grid(rows, 8), 256, 0, st>>>(
+            static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, L, v, vec_ok ? 1 : 0);
+    } else {
+        rows_copy_kernel<ES, false><<<persistent_grid((rows * per_row + 255) / 256, 8), 256, 0, st>>>(
+            static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, L, v, vec_ok ? 1 : 0);
+    }
     return launch_status("strided_copy(rows)");
 }
 

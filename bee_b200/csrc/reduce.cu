@@ -25,43 +25,199 @@ namespace bee_b200 {
 // One 256-thread CTA per row of length `axis` (inner == 1), launched one CTA
 // per row so that the rows in flight on the GPU form a contiguous window of
 // memory (better DRAM locality than a grid-stride over rows).
-template <int OP, typename T>
-__global__ void __launch_bounds__(256) reduce_rows_cta_kernel(const T* __restrict__ src, T* __restrict__ dst,
-                                                              size_t rows, size_t axis) {
-    __shared__ T smem[32];
+template <typename P>
+__global__ void __launch_bounds__(256) reduce_rows_cta_kernel(const typename P::In* __restrict__ src,
+                                                              typename P::Out* __restrict__ dst, size_t rows,
+                                                              size_t axis) {
+    __shared__ typename P::Acc smem[32];
     for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
-        T v = strided_reduce<OP, T, 8>(src + r * axis, 0, axis, threadIdx.x, blockDim.x);
-        v = block_reduce<OP>(v, smem);
-        if (threadIdx.x == 0) dst[r] = v;
+        typename P::Acc v = strided_reduce<P, 8>(src + r * axis, 0, axis, threadIdx.x, blockDim.x);
+        v = block_reduce<P>(v, smem);
+        if (threadIdx.x == 0) dst[r] = P::finish(v, axis);
     }
 }
 
 // One warp per row (short rows, inner == 1).
-template <int OP, typename T>
-__global__ void __launch_bounds__(256) reduce_rows_warp_kernel(const T* __restrict__ src, T* __restrict__ dst,
-                                                               size_t rows, size_t axis) {
+template <typename P>
+__global__ void __launch_bounds__(256) reduce_rows_warp_kernel(const typename P::In* __restrict__ src,
+                                                               typename P::Out* __restrict__ dst, size_t rows,
+                                                               size_t axis) {
     const size_t warps = static_cast<size_t>(gridDim.x) * (blockDim.x >> 5);
     const int lane = threadIdx.x & 31;
     for (size_t r = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
-        T v = strided_reduce<OP>(src + r * axis, 0, axis, lane, 32);
-        v = warp_reduce<OP>(v);
-        if (lane == 0) dst[r] = v;
+        typename P::Acc v = strided_reduce<P>(src + r * axis, 0, axis, lane, 32);
+        v = warp_reduce<P>(v);
+        if (lane == 0) dst[r] = P::finish(v, axis);
     }
 }
 
-// [outer, axis, inner] with inner > 1: one thread per output, neighbouring
-// threads read neighbouring inner elements (coalesced), walking the axis.
-template <int OP, typename T>
-__global__ void __launch_bounds__(256) reduce_inner_kernel(const T* __restrict__ src, T* __restrict__ dst,
-                                                           size_t outer, size_t axis, size_t inner) {
-    const size_t total = outer * inner;
-    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
-    for (size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total; idx += stride) {
-        const size_t o = idx / inner, i = idx - o * inner;
-        const T* p = src + o * axis * inner + i;
-        T acc = Red<OP, T>::identity();
-        for (size_t k = 0; k < axis; ++k) acc = Red<OP, T>::apply(acc, p[k * inner]);
-        dst[idx] = acc;
+// Cross-CTA combine of a split reduction: `count` CTAs publish partials of one
+// output group; the last to take the group's ticket folds them in index order
+// and re-arms the ticket.
+struct SplitScratch {
+    unsigned int* tickets;  // one per output group, zero on entry
+    void* partials;         // Acc[count][group width]
+};
+
+// Few long rows (inner == 1): S CTAs per row, each folding an interleaved
+// share of the row's 32 KiB units, partials combined by the row's last CTA in
+// index order (deterministic for a given S).
+template <typename P>
+__global__ void __launch_bounds__(256) reduce_rows_split_kernel(const typename P::In* __restrict__ src,
+                                                                typename P::Out* __restrict__ dst, size_t rows,
+                                                                size_t axis, unsigned S, SplitScratch sc) {
+    using Acc = typename P::Acc;
+    using In = typename P::In;
+    constexpr size_t E = 16 / sizeof(In);
+    constexpr size_t UNIT = 256 * 8;  // vectors per unit
+    __shared__ Acc smem[32];
+    __shared__ bool last;
+    Acc* partials = static_cast<Acc*>(sc.partials);
+    for (size_t b = blockIdx.x; b < rows * S; b += gridDim.x) {
+        const size_t row = b / S;
+        const unsigned part = static_cast<unsigned>(b % S);
+        const In* base = src + row * axis;
+        Acc acc = P::identity();
+        if ((reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
+            const uint4* v = reinterpret_cast<const uint4*>(base);
+            const size_t nvec = axis / E;
+            for (size_t u = static_cast<size_t>(part) * UNIT; u < nvec; u += static_cast<size_t>(S) * UNIT) {
+                uint4 r[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const size_t idx = u + k * 256 + threadIdx.x;
+                    r[k] = idx < nvec ? ld_stream_u4(v + idx) : make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (u + k * 256 + threadIdx.x < nvec) acc = fold<P>(acc, r[k]);
+            }
+            if (part == 0)
+                for (size_t j = nvec * E + threadIdx.x; j < axis; j += 256) acc = P::add(acc, base[j]);
+        } else {
+            for (size_t j = static_cast<size_t>(part) * 256 + threadIdx.x; j < axis; j += static_cast<size_t>(S) * 256)
+                acc = P::add(acc, base[j]);
+        }
+        acc = block_reduce<P>(acc, smem);
+        if (threadIdx.x == 0) {
+            partials[row * S + part] = acc;
+            __threadfence();
+            last = atomicAdd(&sc.tickets[row], 1u) == S - 1;
+        }
+        __syncthreads();
+        if (last) {
+            __threadfence();
+            Acc r = P::identity();
+            for (unsigned i = threadIdx.x; i < S; i += 256)
+                r = P::combine(r, *reinterpret_cast<volatile Acc*>(partials + row * S + i));
+            r = block_reduce<P>(r, smem);
+            if (threadIdx.x == 0) {
+                dst[row] = P::finish(r, axis);
+                sc.tickets[row] = 0;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// [outer, axis, inner] with inner > 1 (reduce over a non-innermost dim).  A
+// work item is (o, column tile, axis segment): the 32 lanes of a warp cover a
+// tile of 32 x E contiguous columns (E = 16 / sizeof(In) when inner allows
+// 16-byte vectors, else 1), so every row access is one coalesced 512-byte (or
+// 32-element) segment; the 8 warps take rows k = k0 + w, k0 + w + 8, ... of
+// the segment, four rows in flight each; warp partials are combined in warp
+// order through shared memory.  With G > 1 segments, tile partials go to
+// scratch and the segment that arrives last folds them in segment order.
+template <typename P, int E>
+__global__ void __launch_bounds__(256) reduce_cols_kernel(const typename P::In* __restrict__ src,
+                                                          typename P::Out* __restrict__ dst, size_t outer, size_t axis,
+                                                          size_t inner, size_t ctiles, unsigned G, size_t seg,
+                                                          SplitScratch sc) {
+    using Acc = typename P::Acc;
+    using In = typename P::In;
+    constexpr int TW = 32 * E;  // columns per tile
+    __shared__ Acc red[8][TW];
+    __shared__ bool last;
+    Acc* partials = static_cast<Acc*>(sc.partials);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const size_t items = outer * ctiles * G;
+    for (size_t w = blockIdx.x; w < items; w += gridDim.x) {
+        const unsigned g = static_cast<unsigned>(w % G);
+        const size_t rest = w / G;
+        const size_t ct = rest % ctiles, o = rest / ctiles;
+        const size_t col0 = ct * TW;
+        const size_t col = col0 + static_cast<size_t>(lane) * E;
+        const size_t k0 = static_cast<size_t>(g) * seg;
+        const size_t k1 = k0 + seg < axis ? k0 + seg : axis;
+        Acc acc[E];
+#pragma unroll
+        for (int j = 0; j < E; ++j) acc[j] = P::identity();
+        const In* base = src + o * axis * inner + col;
+        if constexpr (E > 1) {
+            if (col < inner) {  // inner % E == 0: the whole vector is in range
+                size_t k = k0 + warp;
+                for (; k + 24 < k1; k += 32) {
+                    uint4 r[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) r[u] = ld_stream_u4(reinterpret_cast<const uint4*>(base + (k + 8 * u) * inner));
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        V16<In> x;
+                        x.v = r[u];
+#pragma unroll
+                        for (int j = 0; j < E; ++j) acc[j] = P::add(acc[j], x.s[j]);
+                    }
+                }
+                for (; k < k1; k += 8) {
+                    V16<In> x;
+                    x.v = ld_stream_u4(reinterpret_cast<const uint4*>(base + k * inner));
+#pragma unroll
+                    for (int j = 0; j < E; ++j) acc[j] = P::add(acc[j], x.s[j]);
+                }
+            }
+        } else {
+            if (col < inner) {
+                size_t k = k0 + warp;
+                for (; k + 24 < k1; k += 32) {
+                    In r[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) r[u] = base[(k + 8 * u) * inner];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) acc[0] = P::add(acc[0], r[u]);
+                }
+                for (; k < k1; k += 8) acc[0] = P::add(acc[0], base[k * inner]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < E; ++j) red[warp][lane * E + j] = acc[j];
+        __syncthreads();
+        for (int c = threadIdx.x; c < TW; c += 256) {
+            Acc r = red[0][c];
+#pragma unroll
+            for (int v = 1; v < 8; ++v) r = P::combine(r, red[v][c]);
+            if (col0 + c < inner) {
+                if (G == 1) dst[o * inner + col0 + c] = P::finish(r, axis);
+                else partials[(static_cast<size_t>(g) * outer + o) * inner + col0 + c] = r;
+            }
+        }
+        if (G > 1) {
+            __threadfence();
+            __syncthreads();
+            if (threadIdx.x == 0) last = atomicAdd(&sc.tickets[o * ctiles + ct], 1u) == G - 1;
+            __syncthreads();
+            if (last) {
+                __threadfence();
+                for (int c = threadIdx.x; c < TW; c += 256) {
+                    if (col0 + c >= inner) continue;
+                    Acc r = P::identity();
+                    for (unsigned gg = 0; gg < G; ++gg)
+                        r = P::combine(r, *reinterpret_cast<volatile Acc*>(partials + (static_cast<size_t>(gg) * outer + o) * inner + col0 + c));
+                    dst[o * inner + col0 + c] = P::finish(r, axis);
+                }
+                if (threadIdx.x == 0) sc.tickets[o * ctiles + ct] = 0;
+            }
+        }
+        __syncthreads();
     }
 }
 
@@ -106,15 +262,17 @@ static int stream_scratch(cudaStream_t st, void** out) {
     return 0;
 }
 
-template <int OP, typename T>
+template <typename P>
 static int run_global(const void* src, void* dst, size_t n, cudaStream_t st) {
-    const unsigned grid = global_grid<T>(n, sm_count());
-    const size_t bytes = sizeof(GlobalScratch) + static_cast<size_t>(grid) * sizeof(T);
+    using In = typename P::In;
+    using Out = typename P::Out;
+    const unsigned grid = global_grid<In>(n, sm_count());
+    const size_t bytes = sizeof(GlobalScratch) + static_cast<size_t>(grid) * sizeof(typename P::Acc);
     void* scratch = nullptr;
     if (bytes <= kStreamScratchBytes && stream_scratch(st, &scratch) == 0) {
         cudaGetLastError();  // a failed probe above must not be reported as a launch error
-        reduce_global_kernel<OP, T><<<grid, kGlobalThreads, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst),
-                                                                     n, static_cast<GlobalScratch*>(scratch));
+        reduce_global_kernel<P><<<grid, kGlobalThreads, 0, st>>>(static_cast<const In*>(src), static_cast<Out*>(dst), n,
+                                                                 static_cast<GlobalScratch*>(scratch));
         return launch_status("reduce_global");
     }
     cudaGetLastError();
@@ -122,8 +280,8 @@ static int run_global(const void* src, void* dst, size_t n, cudaStream_t st) {
     if (e != cudaSuccess) return fail(static_cast<int>(e), "reduce_global: scratch allocation: %s", cudaGetErrorString(e));
     e = cudaMemsetAsync(scratch, 0, sizeof(GlobalScratch), st);
     if (e == cudaSuccess) {
-        reduce_global_kernel<OP, T><<<grid, kGlobalThreads, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst),
-                                                                     n, static_cast<GlobalScratch*>(scratch));
+        reduce_global_kernel<P><<<grid, kGlobalThreads, 0, st>>>(static_cast<const In*>(src), static_cast<Out*>(dst), n,
+                                                                 static_cast<GlobalScratch*>(scratch));
         e = cudaGetLastError();
     }
     cudaError_t e2 = cudaFreeAsync(scratch, st);
@@ -132,35 +290,96 @@ static int run_global(const void* src, void* dst, size_t n, cudaStream_t st) {
     return ok();
 }
 
-template <int OP, typename T>
+// Stream-ordered scratch for a split reduction: `groups` tickets (zeroed) and
+// `partial_bytes` of partials, released on the stream after the launch.
+template <typename Launch>
+static int with_split_scratch(size_t groups, size_t partial_bytes, cudaStream_t st, const char* what, Launch&& launch) {
+    const size_t tbytes = (groups * sizeof(unsigned int) + 255) / 256 * 256;
+    void* mem = nullptr;
+    cudaError_t e = pool_malloc(&mem, tbytes + partial_bytes, st);
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "%s: scratch allocation: %s", what, cudaGetErrorString(e));
+    e = cudaMemsetAsync(mem, 0, tbytes, st);
+    if (e == cudaSuccess) {
+        SplitScratch sc{static_cast<unsigned int*>(mem), static_cast<uint8_t*>(mem) + tbytes};
+        launch(sc);
+        e = cudaGetLastError();
+    }
+    cudaError_t e2 = cudaFreeAsync(mem, st);
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "%s: %s", what, cudaGetErrorString(e));
+    if (e2 != cudaSuccess) return fail(static_cast<int>(e2), "%s: scratch release: %s", what, cudaGetErrorString(e2));
+    return ok();
+}
+
+template <typename P>
 static int run_axis(const void* src, void* dst, size_t outer, size_t axis, size_t inner, cudaStream_t st) {
-    const T* s = static_cast<const T*>(src);
-    T* d = static_cast<T*>(dst);
-    const size_t cap = static_cast<size_t>(sm_count()) * 16;
+    using In = typename P::In;
+    using Out = typename P::Out;
+    using Acc = typename P::Acc;
+    const In* s = static_cast<const In*>(src);
+    Out* d = static_cast<Out*>(dst);
+    const size_t sms = static_cast<size_t>(sm_count());
+    const size_t cap = sms * 16;
+    const size_t target = sms * 8;  // resident 256-thread CTAs
     if (inner == 1) {
+        if (outer == 1) return run_global<P>(src, dst, axis, st);
+        if (outer < sms && axis >= (size_t(1) << 16)) {
+            // few long rows: split every row over S CTAs
+            size_t S = (target + outer - 1) / outer;
+            const size_t max_s = (axis + 256 * 8 * 4 - 1) / (256 * 8 * 4);  // at least four 32 KiB-ish units each
+            if (S > max_s) S = max_s;
+            if (S > 1) {
+                return with_split_scratch(outer, outer * S * sizeof(Acc), st, "reduce_axis", [&](SplitScratch sc) {
+                    const size_t grid = outer * S < target ? outer * S : target;
+                    reduce_rows_split_kernel<P><<<static_cast<unsigned>(grid), 256, 0, st>>>(
+                        s, d, outer, axis, static_cast<unsigned>(S), sc);
+                });
+            }
+        }
         if (axis >= 2048) {
             const size_t grid = outer < (size_t(1) << 30) ? outer : (size_t(1) << 30);
-            reduce_rows_cta_kernel<OP, T><<<static_cast<unsigned>(grid), 256, 0, st>>>(s, d, outer, axis);
+            reduce_rows_cta_kernel<P><<<static_cast<unsigned>(grid), 256, 0, st>>>(s, d, outer, axis);
         } else {
             size_t grid = (outer + 7) / 8;
             if (grid > cap) grid = cap;
-            reduce_rows_warp_kernel<OP, T><<<static_cast<unsigned>(grid), 256, 0, st>>>(s, d, outer, axis);
+            reduce_rows_warp_kernel<P><<<static_cast<unsigned>(grid), 256, 0, st>>>(s, d, outer, axis);
         }
-    } else {
-        size_t grid = (outer * inner + 255) / 256;
-        if (grid > cap) grid = cap;
-        reduce_inner_kernel<OP, T><<<static_cast<unsigned>(grid), 256, 0, st>>>(s, d, outer, axis, inner);
+        return launch_status("reduce_axis");
     }
-    return launch_status("reduce_axis");
+    constexpr int EV = 16 / sizeof(In);
+    const bool vec = inner % EV == 0 && aligned16(src);
+    const size_t tw = vec ? 32 * EV : 32;
+    const size_t ctiles = (inner + tw - 1) / tw;
+    const size_t tiles = outer * ctiles;
+    size_t G = (target + tiles - 1) / tiles;
+    const size_t max_g = (axis + 63) / 64;  // segments of at least 64 rows (8 per warp)
+    if (G > max_g) G = max_g;
+    if (G < 1) G = 1;
+    const size_t seg = (axis + G - 1) / G;
+    G = (axis + seg - 1) / seg;
+    auto launch = [&](SplitScratch sc) {
+        const size_t items = tiles * G;
+        const size_t grid = items < cap ? items : cap;
+        if (vec)
+            reduce_cols_kernel<P, EV><<<static_cast<unsigned>(grid), 256, 0, st>>>(
+                s, d, outer, axis, inner, ctiles, static_cast<unsigned>(G), seg, sc);
+        else
+            reduce_cols_kernel<P, 1><<<static_cast<unsigned>(grid), 256, 0, st>>>(
+                s, d, outer, axis, inner, ctiles, static_cast<unsigned>(G), seg, sc);
+    };
+    if (G == 1) {
+        launch(SplitScratch{nullptr, nullptr});
+        return launch_status("reduce_axis");
+    }
+    return with_split_scratch(tiles, G * outer * inner * sizeof(Acc), st, "reduce_axis", launch);
 }
 
 template <typename T>
 static int dispatch_global(int op, const void* src, void* dst, size_t n, cudaStream_t st) {
     switch (op) {
-    case RED_SUM: if constexpr (!std::is_same_v<T, uint8_t>) return run_global<RED_SUM, T>(src, dst, n, st); break;
-    case RED_PROD: if constexpr (!std::is_same_v<T, uint8_t>) return run_global<RED_PROD, T>(src, dst, n, st); break;
-    case RED_MIN: return run_global<RED_MIN, T>(src, dst, n, st);
-    case RED_MAX: return run_global<RED_MAX, T>(src, dst, n, st);
+    case RED_SUM: if constexpr (!std::is_same_v<T, uint8_t>) return run_global<ElemRed<RED_SUM, T>>(src, dst, n, st); break;
+    case RED_PROD: if constexpr (!std::is_same_v<T, uint8_t>) return run_global<ElemRed<RED_PROD, T>>(src, dst, n, st); break;
+    case RED_MIN: return run_global<ElemRed<RED_MIN, T>>(src, dst, n, st);
+    case RED_MAX: return run_global<ElemRed<RED_MAX, T>>(src, dst, n, st);
     default: return fail(cudaErrorInvalidValue, "reduce_global: unknown op code %d", op);
     }
     return fail(cudaErrorInvalidValue, "reduce_global: op %d does not support U8", op);
@@ -169,10 +388,10 @@ static int dispatch_global(int op, const void* src, void* dst, size_t n, cudaStr
 template <typename T>
 static int dispatch_axis(int op, const void* src, void* dst, size_t outer, size_t axis, size_t inner, cudaStream_t st) {
     switch (op) {
-    case RED_SUM: if constexpr (!std::is_same_v<T, uint8_t>) return run_axis<RED_SUM, T>(src, dst, outer, axis, inner, st); break;
-    case RED_PROD: if constexpr (!std::is_same_v<T, uint8_t>) return run_axis<RED_PROD, T>(src, dst, outer, axis, inner, st); break;
-    case RED_MIN: return run_axis<RED_MIN, T>(src, dst, outer, axis, inner, st);
-    case RED_MAX: return run_axis<RED_MAX, T>(src, dst, outer, axis, inner, st);
+    case RED_SUM: if constexpr (!std::is_same_v<T, uint8_t>) return run_axis<ElemRed<RED_SUM, T>>(src, dst, outer, axis, inner, st); break;
+    case RED_PROD: if constexpr (!std::is_same_v<T, uint8_t>) return run_axis<ElemRed<RED_PROD, T>>(src, dst, outer, axis, inner, st); break;
+    case RED_MIN: return run_axis<ElemRed<RED_MIN, T>>(src, dst, outer, axis, inner, st);
+    case RED_MAX: return run_axis<ElemRed<RED_MAX, T>>(src, dst, outer, axis, inner, st);
     default: return fail(cudaErrorInvalidValue, "reduce_axis: unknown op code %d", op);
     }
     return fail(cudaErrorInvalidValue, "reduce_axis: op %d does not support U8", op);
@@ -210,6 +429,18 @@ int bee_b200_reduce_axis(int op, int dt, const void* src, void* dst, size_t oute
     case DT_F32: return dispatch_axis<float>(op, src, dst, outer, axis, inner, st);
     case DT_F64: return dispatch_axis<double>(op, src, dst, outer, axis, inner, st);
     default: return fail(cudaErrorInvalidValue, "reduce_axis: unsupported dtype %d", dt);
+    }
+}
+
+int bee_b200_reduce_mean_int(int dt, const void* src, double* dst, size_t outer, size_t axis, size_t inner,
+                             bee_b200_stream_t stream) {
+    if (outer == 0 || axis == 0 || inner == 0) return fail(cudaErrorInvalidValue, "reduce_mean_int: empty extent");
+    if (!src || !dst) return fail(cudaErrorInvalidValue, "reduce_mean_int: null pointer");
+    cudaStream_t st = as_stream(stream);
+    switch (dt) {
+    case DT_I32: return run_axis<MeanInt<int32_t>>(src, dst, outer, axis, inner, st);
+    case DT_I64: return run_axis<MeanInt<int64_t>>(src, dst, outer, axis, inner, st);
+    default: return fail(cudaErrorInvalidValue, "reduce_mean_int: dtype %d is not I32 or I64", dt);
     }
 }
 

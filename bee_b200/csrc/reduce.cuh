@@ -39,22 +39,54 @@ template <int OP, typename T> struct Red {
     }
 };
 
-template <int OP, typename T> __device__ __forceinline__ T warp_reduce(T v) {
+// Reduction policies: input element In, accumulator Acc, output Out.
+//   ElemRed<OP, T>: the reference's reduce semantics, accumulating in T.
+//   MeanInt<T>: integer mean (Bee/Tensor/Cpu/ReduceCpu.hpp:431-466, 551-610):
+//     the exact integer sum in int64 (two's complement, no overflow while
+//     |sum| < 2^63), then double(sum) / double(count).  The reference
+//     accumulates in double, which is exact while every partial sum stays
+//     below 2^53 in magnitude; in that range both give the same bits.
+template <int OP, typename T> struct ElemRed {
+    using In = T;
+    using Acc = T;
+    using Out = T;
+    static __device__ __forceinline__ Acc identity() { return Red<OP, T>::identity(); }
+    static __device__ __forceinline__ Acc add(Acc a, In x) { return Red<OP, T>::apply(a, x); }
+    static __device__ __forceinline__ Acc combine(Acc a, Acc b) { return Red<OP, T>::apply(a, b); }
+    static __device__ __forceinline__ Out finish(Acc a, size_t) { return a; }
+};
+
+template <typename T> struct MeanInt {
+    using In = T;
+    using Acc = long long;
+    using Out = double;
+    static __device__ __forceinline__ Acc identity() { return 0; }
+    static __device__ __forceinline__ Acc combine(Acc a, Acc b) {
+        return static_cast<Acc>(static_cast<unsigned long long>(a) + static_cast<unsigned long long>(b));
+    }
+    static __device__ __forceinline__ Acc add(Acc a, In x) { return combine(a, static_cast<Acc>(x)); }
+    static __device__ __forceinline__ Out finish(Acc a, size_t n) {
+        return static_cast<double>(a) / static_cast<double>(n);
+    }
+};
+
+template <typename P> __device__ __forceinline__ typename P::Acc warp_reduce(typename P::Acc v) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = Red<OP, T>::apply(v, __shfl_xor_sync(0xffffffffu, v, o));
+    for (int o = 16; o > 0; o >>= 1) v = P::combine(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
 
 // Block-wide reduce; the result is valid in every thread.  `smem` holds
 // blockDim.x / 32 entries.
-template <int OP, typename T> __device__ __forceinline__ T block_reduce(T v, T* smem) {
+template <typename P> __device__ __forceinline__ typename P::Acc block_reduce(typename P::Acc v, typename P::Acc* smem) {
+    using Acc = typename P::Acc;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    v = warp_reduce<OP>(v);
+    v = warp_reduce<P>(v);
     __syncthreads();
     if (lane == 0) smem[warp] = v;
     __syncthreads();
-    T r = Red<OP, T>::identity();
-    for (int w = 0; w < nwarps; ++w) r = Red<OP, T>::apply(r, smem[w]);
+    Acc r = P::identity();
+    for (int w = 0; w < nwarps; ++w) r = P::combine(r, smem[w]);
     return r;
 }
 
@@ -63,22 +95,25 @@ template <typename T> union V16 {
     T s[16 / sizeof(T)];
 };
 
-// Folds a 16-byte vector into `acc` lane by lane (fixed order).
-template <int OP, typename T> __device__ __forceinline__ T fold(T acc, uint4 raw) {
-    V16<T> x;
+// Folds a 16-byte vector of In into `acc` lane by lane (fixed order).
+template <typename P> __device__ __forceinline__ typename P::Acc fold(typename P::Acc acc, uint4 raw) {
+    using In = typename P::In;
+    V16<In> x;
     x.v = raw;
 #pragma unroll
-    for (int k = 0; k < int(16 / sizeof(T)); ++k) acc = Red<OP, T>::apply(acc, x.s[k]);
+    for (int k = 0; k < int(16 / sizeof(In)); ++k) acc = P::add(acc, x.s[k]);
     return acc;
 }
 
 // Reduces src[lo, hi) cooperatively by `nthr` threads (index `tid`); the
 // 16-byte vector path is used when src+lo is 16-byte aligned.
-template <int OP, typename T, int U = 4>
-__device__ __forceinline__ T strided_reduce(const T* __restrict__ src, size_t lo, size_t hi, size_t tid, size_t nthr) {
-    constexpr size_t E = 16 / sizeof(T);
-    T acc = Red<OP, T>::identity();
-    const T* base = src + lo;
+template <typename P, int U = 4>
+__device__ __forceinline__ typename P::Acc strided_reduce(const typename P::In* __restrict__ src, size_t lo, size_t hi,
+                                                          size_t tid, size_t nthr) {
+    using In = typename P::In;
+    constexpr size_t E = 16 / sizeof(In);
+    typename P::Acc acc = P::identity();
+    const In* base = src + lo;
     const size_t len = hi - lo;
     size_t head = 0;
     if ((reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
@@ -90,12 +125,12 @@ __device__ __forceinline__ T strided_reduce(const T* __restrict__ src, size_t lo
 #pragma unroll
             for (int u = 0; u < U; ++u) r[u] = ld_stream_u4(v + i + u * nthr);
 #pragma unroll
-            for (int u = 0; u < U; ++u) acc = fold<OP>(acc, r[u]);
+            for (int u = 0; u < U; ++u) acc = fold<P>(acc, r[u]);
         }
-        for (; i < nvec; i += nthr) acc = fold<OP>(acc, ld_stream_u4(v + i));
+        for (; i < nvec; i += nthr) acc = fold<P>(acc, ld_stream_u4(v + i));
         head = nvec * E;
     }
-    for (size_t j = head + tid; j < len; j += nthr) acc = Red<OP, T>::apply(acc, base[j]);
+    for (size_t j = head + tid; j < len; j += nthr) acc = P::add(acc, base[j]);
     return acc;
 }
 
@@ -104,7 +139,7 @@ __device__ __forceinline__ T strided_reduce(const T* __restrict__ src, size_t lo
 struct GlobalScratch {
     unsigned int ticket;  // number of CTAs that have published their partial
     unsigned int pad[63];
-    // followed by gridDim.x partials of sizeof(T), 256-byte aligned
+    // followed by gridDim.x partials of sizeof(Acc), 256-byte aligned
 };
 
 // Global reduce, one launch.  The input is cut into units of 256 threads x 8
@@ -126,16 +161,19 @@ template <typename T> inline unsigned global_grid(size_t n, int sms) {
     return static_cast<unsigned>(need < 1 ? 1 : (need < cap ? need : cap));
 }
 
-template <int OP, typename T>
-__global__ void __launch_bounds__(kGlobalThreads) reduce_global_kernel(const T* __restrict__ src, T* __restrict__ dst,
-                                                                       size_t n, GlobalScratch* scratch) {
-    constexpr size_t E = 16 / sizeof(T);
+template <typename P>
+__global__ void __launch_bounds__(kGlobalThreads) reduce_global_kernel(const typename P::In* __restrict__ src,
+                                                                       typename P::Out* __restrict__ dst, size_t n,
+                                                                       GlobalScratch* scratch) {
+    using In = typename P::In;
+    using Acc = typename P::Acc;
+    constexpr size_t E = 16 / sizeof(In);
     constexpr size_t UNIT = static_cast<size_t>(kGlobalThreads) * kGlobalUnroll;  // vectors per unit
-    __shared__ T smem[32];
+    __shared__ Acc smem[32];
     __shared__ bool last;
-    T* partials = reinterpret_cast<T*>(scratch + 1);
+    Acc* partials = reinterpret_cast<Acc*>(scratch + 1);
     const unsigned tid = threadIdx.x;
-    T acc = Red<OP, T>::identity();
+    Acc acc = P::identity();
     if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
         const uint4* v = reinterpret_cast<const uint4*>(src);
         const size_t nvec = n / E;
@@ -145,22 +183,22 @@ __global__ void __launch_bounds__(kGlobalThreads) reduce_global_kernel(const T* 
 #pragma unroll
                 for (int k = 0; k < kGlobalUnroll; ++k) r[k] = ld_stream_u4(v + base + k * kGlobalThreads + tid);
 #pragma unroll
-                for (int k = 0; k < kGlobalUnroll; ++k) acc = fold<OP>(acc, r[k]);
+                for (int k = 0; k < kGlobalUnroll; ++k) acc = fold<P>(acc, r[k]);
             } else {
                 for (int k = 0; k < kGlobalUnroll; ++k) {
                     const size_t idx = base + k * kGlobalThreads + tid;
-                    if (idx < nvec) acc = fold<OP>(acc, ld_stream_u4(v + idx));
+                    if (idx < nvec) acc = fold<P>(acc, ld_stream_u4(v + idx));
                 }
             }
         }
         if (blockIdx.x == 0)
-            for (size_t j = nvec * E + tid; j < n; j += kGlobalThreads) acc = Red<OP, T>::apply(acc, src[j]);
+            for (size_t j = nvec * E + tid; j < n; j += kGlobalThreads) acc = P::add(acc, src[j]);
     } else {
         const size_t stride = static_cast<size_t>(gridDim.x) * kGlobalThreads;
         for (size_t j = static_cast<size_t>(blockIdx.x) * kGlobalThreads + tid; j < n; j += stride)
-            acc = Red<OP, T>::apply(acc, src[j]);
+            acc = P::add(acc, src[j]);
     }
-    acc = block_reduce<OP>(acc, smem);
+    acc = block_reduce<P>(acc, smem);
     if (tid == 0) {
         partials[blockIdx.x] = acc;
         __threadfence();
@@ -172,12 +210,12 @@ __global__ void __launch_bounds__(kGlobalThreads) reduce_global_kernel(const T* 
     __threadfence();
     // Last CTA: fold the partials in index order (thread-strided, then the
     // block reduce), then re-arm the ticket for the next call.
-    T r = Red<OP, T>::identity();
+    Acc r = P::identity();
     for (unsigned i = tid; i < gridDim.x; i += kGlobalThreads)
-        r = Red<OP, T>::apply(r, *reinterpret_cast<volatile T*>(partials + i));
-    r = block_reduce<OP>(r, smem);
+        r = P::combine(r, *reinterpret_cast<volatile Acc*>(partials + i));
+    r = block_reduce<P>(r, smem);
     if (tid == 0) {
-        *dst = r;
+        *dst = P::finish(r, n);
         scratch->ticket = 0;
     }
 }

@@ -67,7 +67,7 @@ int run_noalloc(const void* src, void* dst, size_t n, cudaStream_t st) {
     if (int rc = scratch_address(&scratch)) return rc;
     cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(GlobalScratch), st);
     if (e != cudaSuccess) return fail(static_cast<int>(e), "reduce_global_noalloc: clearing the ticket: %s", cudaGetErrorString(e));
-    reduce_global_kernel<OP, T><<<grid, kGlobalThreads, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst), n,
+    reduce_global_kernel<ElemRed<OP, T>><<<grid, kGlobalThreads, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst), n,
                                                                  static_cast<GlobalScratch*>(scratch));
     return launch_status("reduce_global_noalloc");
 }

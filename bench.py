@@ -514,6 +514,16 @@ def run_extras(args, d, dev, stream, peaks):
                                             "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
                                             "op": "x[8192, 8192] - rowmax[8192, 1] (broadcast, stride 0)",
                                             "bytes_per_gpu": nbytes, "scaling": "weak"}
+        colsum = torch.empty(8192, device=dev)
+        ms = timed(lambda: call("bee_b200_reduce_axis", _capi.SUM, _capi.F32, x.data_ptr(), colsum.data_ptr(), 1, 8192,
+                                8192, st))
+        nbytes = 8192 * 8192 * 4 + 8192 * 4
+        gbs = d.world * nbytes / (ms / 1e3) / 1e9
+        out["sum_dim0_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                    "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                    "op": "sum(x, 0) of [8192, 8192] fp32 (column reduce, axis split over CTAs)",
+                                    "bytes_per_gpu": nbytes, "scaling": "weak"}
+        del colsum
         kq = torch.randn(256, 2048, 128, device=dev, generator=g).to(torch.bfloat16)
         kt = torch.empty(256, 128, 2048, device=dev, dtype=torch.bfloat16)
         vsh = (ctypes.c_int64 * 3)(256, 128, 2048)

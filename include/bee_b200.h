@@ -141,6 +141,16 @@ BEE_B200_API int bee_b200_reduce_global_noalloc(int op, int dt, const void* src,
 BEE_B200_API int bee_b200_reduce_axis(int op, int dt, const void* src, void* dst, size_t outer, size_t axis,
                          size_t inner, bee_b200_stream_t stream);
 
+/* New: integer mean on the device, which the reference's CUDA path rejects
+ * (Bee/Tensor/Ops/Reduce.cpp:155-160) and its CPU path computes by double
+ * accumulation (Bee/Tensor/Cpu/ReduceCpu.hpp:431-466, 551-610).  Mean over the
+ * `axis` dim of a contiguous [outer, axis, inner] I32 or I64 tensor into F64
+ * dst [outer, inner] (outer = inner = 1: the global mean).  The sum is exact
+ * (int64), then double(sum) / axis: the reference's result whenever its double
+ * accumulation is exact (partial sums below 2^53 in magnitude). */
+BEE_B200_API int bee_b200_reduce_mean_int(int dt, const void* src, double* dst, size_t outer, size_t axis, size_t inner,
+                                          bee_b200_stream_t stream);
+
 /* ----------------------------------------------------- row-wise operators
  * New operators (the reference has none; its CPU oracle composes them from
  * public ops: max/sub/exp/sum/div for softmax, mul/mean/add/sqrt/div/mul for

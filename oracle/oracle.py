@@ -162,6 +162,23 @@ class Oracle:
         return o
 
     @staticmethod
+    def mean_int(x: np.ndarray, axis=None) -> np.ndarray:
+        """Integer mean as the reference computes it (Bee/Tensor/Cpu/ReduceCpu.hpp:431-466,
+        551-610): accumulate in double, divide by the count, F64 out.  The
+        accumulation is done exactly (int64, or Python integers where int64
+        could overflow) and rounded once, which equals the reference's
+        sequential double sum whenever that sum is exact (every partial sum
+        below 2^53 in magnitude)."""
+        x = np.asarray(x)
+        n = x.size if axis is None else x.shape[axis]
+        bound = int(np.abs(x.astype(np.float64)).max(initial=0.0)) * max(n, 1)
+        if bound < 2 ** 62:
+            s = x.astype(np.int64).sum(axis=axis, dtype=np.int64)
+            return np.asarray(s, np.int64).astype(np.float64) / np.float64(n)
+        s = x.astype(object).sum(axis=axis)
+        return np.vectorize(lambda v: float(int(v)) / n, otypes=[np.float64])(s)
+
+    @staticmethod
     def strided_gather(flat: np.ndarray, offset: int, shape, strides) -> np.ndarray:
         """Row-major materialisation of the view (offset, shape, strides in
         elements) of the 1-D buffer `flat`: out[i0, .., ik] = flat[offset +
@@ -198,6 +215,7 @@ class Reference:
             "bref_attention_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _f, _i],
             "bref_view_copy_f32": [_vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i],
             "bref_binary_bcast_f32": [_i, _vp, _vp, _vp, _vp, _i, _vp, _i],
+            "bref_mean_int": [_i, _vp, _i64, _i64, _i64, _i, _vp, _i],
         }.items():
             fn = getattr(L, name)
             fn.argtypes = args
@@ -283,6 +301,16 @@ class Reference:
         t = self._chk(self.lib.bref_binary_bcast_f32(op, _p(a), _p(ash), _p(b), _p(bsh), a.ndim, _p(out), reps),
                       "binary broadcast")
         return out, t
+
+    def mean_int(self, x, global_mean=False, reps=1):
+        """Mean over dim 1 of the [outer, axis, inner] integer tensor x (or of
+        all elements), F64 result, on the reference's CPU path."""
+        dt = 2 if x.dtype == np.int32 else 3
+        x = np.ascontiguousarray(x)
+        o, a, i = x.shape
+        out = np.empty(1 if global_mean else o * i, np.float64)
+        t = self._chk(self.lib.bref_mean_int(dt, _p(x), o, a, i, int(global_mean), _p(out), reps), "mean")
+        return (out[0] if global_mean else out.reshape(o, i)), t
 
     def view_copy_f32(self, x, perm, slices=None, reps=1):
         """permute(perm), then slice(d, start, end, step) per dim of `slices`

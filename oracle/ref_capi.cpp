@@ -310,4 +310,21 @@ double bref_binary_bcast_f32(int op, const float* a, const int64_t* a_shape, con
     return t;
 }
 
+
+// Integer mean over dim 1 of [outer, axis, inner] (axis < 0: global mean of
+// all elements) on the reference's CPU path; out is F64.  dt: 2 I32, 3 I64.
+double bref_mean_int(int dt, const void* x, int64_t outer, int64_t axis, int64_t inner, int global, double* out,
+                     int reps) {
+    Tensor X = make({outer, axis, inner}, dt == 2 ? DType::I32 : DType::I64, x);
+    Tensor R;
+    double t = timed(reps, [&] {
+        auto r = global ? mean(X) : mean(X, 1);
+        if (!okr(r, "mean")) return false;
+        R = *r;
+        return true;
+    });
+    if (t >= 0) copy_out(R, out);
+    return t;
+}
+
 }  // extern "C"
