@@ -3,26 +3,26 @@
 //
 // The reference has no attention (its user composes per-head matmul, scale,
 // softmax and matmul, each round-tripping through memory).  Here one CTA owns
-// one head's block of 128 queries and streams the keys/values past it in
-// blocks of 128, so S and P never leave the SM:
-//   * warp 0 — TMA: Q once, then K_j / V_j into two-deep rings (the same
+// two 128-query tiles (A and B) of one head and streams the keys/values past
+// them in blocks of 128, so S and P never leave the SM:
+//   * warp 0 — TMA: Q_A, Q_B once, then K_j / V_j into two-deep rings (one
 //     64x128 box shape serves all three; K is read as the K-major operand of
 //     Q.K^T, V as the MN-major operand of P.V);
-//   * warp 1 — MMA: S_j = Q.K_j^T into one of two TMEM score buffers
-//     (tcgen05.mma M=128 N=128, K=128 head dims), issued one block ahead so
-//     the tensor core computes S_{j+1} while the softmax warps work on S_j;
-//     then O += P_j.V_j into a TMEM accumulator;
-//   * warps 2-9 — softmax: two threads share each query row, one per half of
-//     the 128 keys of a block (warps 2-5 and 6-9 cover the same TMEM lanes);
-//     each reads its 64 scores from TMEM, the pair combines row maxima through
-//     shared memory, keeps a running max m (log2 units) and a partial sum l,
-//     writes its half of P_j = 2^(s - m) as bf16 into shared memory (once
-//     P.V_{j-1} has consumed P_{j-1}) in the swizzled K-major layout the MMA
-//     reads, and at the end divides its half of the O row by the pair's l.
-//     The running max is only raised when a block's max exceeds it by more
-//     than 8 (a factor 2^8): until then P <= 256, which bf16 and fp32 hold
-//     exactly enough, and the result O / l is unchanged; when it is raised,
-//     the row of O in TMEM (and l) is rescaled after the previous P.V is done.
+//   * warp 1 — MMA, ping-pong between the tiles: O_A += P_A(j).V_j,
+//     S_A(j+1) = Q_A.K_{j+1}^T, O_B += P_B(j).V_j, S_B(j+1) = Q_B.K_{j+1}^T,
+//     so the tensor core works on one tile while the other tile's softmax runs;
+//   * warps 2-5 / 6-9 — softmax of tile A / B, one thread per query row: the
+//     thread reads its 128 scores from TMEM, keeps a running max m (log2 units)
+//     and sum l, and writes P = 2^(s*c - m) as bf16 back into TMEM over the
+//     first 64 columns of its own scores; P.V then reads P straight from TMEM
+//     (tcgen05.mma with the A operand in tensor memory).  The running max is
+//     only raised when a block's max exceeds it by more than 8 (a factor 2^8):
+//     until then P <= 256, which bf16 and fp32 hold exactly enough, and O / l
+//     is unchanged; when it is raised the thread rescales its row of O in TMEM
+//     (the previous P.V is complete by then: the MMA that produced the current
+//     scores was issued after it).  At the end each thread divides its O row
+//     by l and stores it.
+// TMEM (512 columns): S_A 0-127, S_B 128-255, O_A 256-383, O_B 384-511.
 // Every wait is bounded; a wait that gives up records a code in the status
 // word read by bee_b200_device_status and the CTA abandons its work.
 #include <cuda.h>
@@ -39,11 +39,11 @@ __device__ int g_attn_status = 0;
 
 namespace {
 
-constexpr int kBlock = 128;                       // queries per CTA, keys per step
+constexpr int kBlock = 128;                       // queries per tile, keys per step
 constexpr int kHead = 128;                        // head dim
 constexpr int kHalf = 128 * 64 * 2;               // one 128-row x 64-col bf16 swizzled block
 constexpr int kTile = 2 * kHalf;                  // 128 x 128 bf16
-constexpr int kSmem = kTile /*Q*/ + 2 * kTile /*K*/ + 2 * kTile /*V*/ + kTile /*P*/ + 1024;
+constexpr int kSmem = 2 * kTile /*Q_A, Q_B*/ + 2 * kTile /*K*/ + 2 * kTile /*V*/ + 1024;
 constexpr float kRescaleThreshold = 8.0f;         // log2 units
 
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -58,7 +58,6 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
         : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
@@ -73,7 +72,7 @@ struct AttnParams {
     uint16_t* O;      // [heads, seq, 128] bf16
 };
 
-constexpr int kThreads = 320;  // TMA warp, MMA warp, 8 softmax warps
+constexpr int kThreads = 320;  // TMA warp, MMA warp, 2 x 4 softmax warps
 
 __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                                const __grid_constant__ CUtensorMap tmK,
@@ -82,25 +81,22 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t q_full;
     __shared__ __align__(8) uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-    __shared__ __align__(8) uint64_t s_full[2], s_empty[2];
-    __shared__ __align__(8) uint64_t p_full, o_done;
+    __shared__ __align__(8) uint64_t s_full[2], p_full[2];  // [tile]
     __shared__ __align__(8) uint64_t done_bar;
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
-    __shared__ float xch[2][2][kBlock];  // [step parity][half][row]: partial row maxima
-    __shared__ float xl[2][kBlock];      // [half][row]: partial row sums, exchanged at the end
-    __shared__ __align__(8) uint64_t x_bar[2], l_bar;  // the exchanges' mbarriers (bounded waits)
 
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem;
-    uint8_t* sK = sQ + kTile;      // [2]
-    uint8_t* sV = sK + 2 * kTile;  // [2]
-    uint8_t* sP = sV + 2 * kTile;
+    uint8_t* sQ = smem;            // [2] tiles A, B
+    uint8_t* sK = sQ + 2 * kTile;  // [2] ring
+    uint8_t* sV = sK + 2 * kTile;  // [2] ring
     volatile int* abort_flag = &abort_sh;
     int* status = &g_attn_status;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qtile = blockIdx.x, head = blockIdx.y;
+    const int pair = blockIdx.x, head = blockIdx.y;
     const int nkv = p.nkv;
+    const int q0 = pair * 2 * kBlock;
+    const int ntiles = q0 + kBlock < p.seq ? 2 : 1;  // the last pair of an odd tile count has only tile A
 
     if (threadIdx.x == 0) {
         mbar_init(&q_full, 1);
@@ -110,14 +106,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_empty[i], 8);  // one arrive per softmax warp
+            mbar_init(&p_full[i], 4);  // one arrive per softmax warp of the tile
         }
-        mbar_init(&p_full, 8);
-        mbar_init(&o_done, 1);
         mbar_init(&done_bar, 1);
-        mbar_init(&x_bar[0], 8);
-        mbar_init(&x_bar[1], 8);
-        mbar_init(&l_bar, 8);
         abort_sh = 0;
         fence_mbar_init();
     }
@@ -130,14 +121,16 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = tmem_base_sh;  // S0: cols 0-127, S1: 128-255, O: 256-383
+    const uint32_t tmem = tmem_base_sh;
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
-            mbar_arrive_expect_tx(&q_full, kTile);
-            tma_load_3d(sQ, &tmQ, &q_full, 0, qtile * kBlock, head);
-            tma_load_3d(sQ + kHalf, &tmQ, &q_full, 64, qtile * kBlock, head);
+            mbar_arrive_expect_tx(&q_full, ntiles * kTile);
+            for (int t = 0; t < ntiles; ++t) {
+                tma_load_3d(sQ + t * kTile, &tmQ, &q_full, 0, q0 + t * kBlock, head);
+                tma_load_3d(sQ + t * kTile + kHalf, &tmQ, &q_full, 64, q0 + t * kBlock, head);
+            }
             int k_issued = 0, v_issued = 0;
             for (int j = 0; j < nkv; ++j) {
                 const int s = j & 1;
@@ -167,52 +160,59 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
         if (lane == 0) {
             constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false);  // B = K rows, K-major
             constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, true);   // B = V, MN-major
-            const uint32_t q_base = smem_u32(sQ);
             bool ok = mbar_wait(&q_full, 0, abort_flag, status, 23);
             bool issued = false;
-            // S_j = Q . K_j^T into score buffer j & 1
-            auto issue_s = [&](int j) -> bool {
-                const int s = j & 1;
-                const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
-                if (!mbar_wait(&k_full[s], ph, abort_flag, status, 24)) return false;
-                if (!mbar_wait(&s_empty[s], ph ^ 1u, abort_flag, status, 25)) return false;
-                tc_fence_after();
-                const uint32_t k_base = smem_u32(sK + s * kTile);
+            // S_t = Q_t . K_j^T into TMEM columns t * 128
+            auto issue_s = [&](int t, int j) {
+                const uint32_t q_base = smem_u32(sQ + t * kTile);
+                const uint32_t k_base = smem_u32(sK + (j & 1) * kTile);
 #pragma unroll
                 for (int k = 0; k < kHead / 16; ++k) {
                     const uint32_t off = (k / 4) * kHalf + (k % 4) * 32;
-                    mma_f16_ss(tmem + static_cast<uint32_t>(s * 128), sdesc_sw128(q_base + off, 16, 1024),
+                    mma_f16_ss(tmem + static_cast<uint32_t>(t * 128), sdesc_sw128(q_base + off, 16, 1024),
                                sdesc_sw128(k_base + off, 16, 1024), idesc_s, k != 0 ? 1u : 0u);
                 }
-                mma_commit(&k_empty[s]);
-                mma_commit(&s_full[s]);
+                mma_commit(&s_full[t]);
                 issued = true;
-                return true;
             };
-            // O += P_j . V_j
-            auto issue_o = [&](int j) -> bool {
+            // O_t += P_t . V_j, P_t in TMEM columns t * 128 .. + 63 (bf16 pairs)
+            auto issue_o = [&](int t, int j) {
+                const uint32_t v_base = smem_u32(sV + (j & 1) * kTile);
+#pragma unroll
+                for (int k = 0; k < kBlock / 16; ++k)
+                    mma_f16_ts(tmem + 256u + static_cast<uint32_t>(t * 128), tmem + static_cast<uint32_t>(t * 128 + k * 8),
+                               sdesc_sw128(v_base + k * 16 * 128, kHalf, 1024), idesc_o, (j | k) != 0 ? 1u : 0u);
+                issued = true;
+            };
+            if (ok && nkv > 0) {
+                ok = mbar_wait(&k_full[0], 0, abort_flag, status, 24);
+                if (ok) {
+                    tc_fence_after();
+                    for (int t = 0; t < ntiles; ++t) issue_s(t, 0);
+                    mma_commit(&k_empty[0]);
+                }
+            }
+            for (int j = 0; ok && j < nkv; ++j) {
                 const int s = j & 1;
                 const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
-                if (!mbar_wait(&p_full, static_cast<uint32_t>(j & 1), abort_flag, status, 26)) return false;
-                if (!mbar_wait(&v_full[s], ph, abort_flag, status, 27)) return false;
-                tc_fence_after();
-                const uint32_t p_base = smem_u32(sP);
-                const uint32_t v_base = smem_u32(sV + s * kTile);
-#pragma unroll
-                for (int k = 0; k < kBlock / 16; ++k) {
-                    const uint32_t a_off = (k / 4) * kHalf + (k % 4) * 32;
-                    mma_f16_ss(tmem + 256u, sdesc_sw128(p_base + a_off, 16, 1024),
-                               sdesc_sw128(v_base + k * 16 * 128, kHalf, 1024), idesc_o, (j | k) != 0 ? 1u : 0u);
+                const bool next = j + 1 < nkv;
+                const int s1 = (j + 1) & 1;
+                const uint32_t ph1 = static_cast<uint32_t>(((j + 1) >> 1) & 1);
+                for (int t = 0; ok && t < ntiles; ++t) {
+                    ok = mbar_wait(&p_full[t], static_cast<uint32_t>(j & 1), abort_flag, status, 26);
+                    if (ok && t == 0) ok = mbar_wait(&v_full[s], ph, abort_flag, status, 27);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_o(t, j);
+                    if (t == ntiles - 1) mma_commit(&v_empty[s]);
+                    if (next) {
+                        if (t == 0) ok = mbar_wait(&k_full[s1], ph1, abort_flag, status, 24);
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue_s(t, j + 1);
+                        if (t == ntiles - 1) mma_commit(&k_empty[s1]);
+                    }
                 }
-                mma_commit(&v_empty[s]);
-                mma_commit(&o_done);
-                issued = true;
-                return true;
-            };
-            if (ok && nkv > 0) ok = issue_s(0);
-            for (int j = 0; ok && j < nkv; ++j) {
-                if (j + 1 < nkv) ok = issue_s(j + 1);
-                if (ok) ok = issue_o(j);
             }
             if (issued) {
                 mma_commit(&done_bar);
@@ -222,118 +222,85 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
         __syncwarp();
     } else {
         // ------------------------------------------------ softmax / epilogue (warps 2-9)
+        const int t = (warp - 2) >> 2;          // tile A (warps 2-5) or B (warps 6-9)
         const int q = warp & 3;                 // TMEM lane quarter
-        const int half = (warp - 2) >> 2;       // which 64 keys of a block (and 64 O columns) this thread owns
         const int row = q * 32 + lane;          // query row within the tile
         const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+        const uint32_t s_col = tmem + static_cast<uint32_t>(t * 128) + lane_addr;
+        const uint32_t o_col = tmem + 256u + static_cast<uint32_t>(t * 128) + lane_addr;
+        const float c = p.scale_log2;
         float m = -INFINITY, l = 0.f;
-        bool ok = true;
-        for (int j = 0; j < nkv; ++j) {
-            const int s = j & 1;
-            const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
-            ok = mbar_wait(&s_full[s], ph, abort_flag, status, 29);
+        bool ok = t < ntiles;
+        for (int j = 0; ok && j < nkv; ++j) {
+            ok = mbar_wait(&s_full[t], static_cast<uint32_t>(j & 1), abort_flag, status, 29);
             if (!__all_sync(0xffffffffu, ok)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            float t[64];
+            float sc[128];
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
+            for (int cc = 0; cc < 4; ++cc) {
                 uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem + static_cast<uint32_t>(s * 128 + half * 64 + c * 32) + lane_addr, r);
+                tmem_ld_32x32b_x32(s_col + static_cast<uint32_t>(cc * 32), r);
                 tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) t[c * 32 + i] = __uint_as_float(r[i]) * p.scale_log2;
+                for (int i = 0; i < 32; ++i) sc[cc * 32 + i] = __uint_as_float(r[i]);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[s]);
-            float pm = t[0];
+            float mx = sc[0];
 #pragma unroll
-            for (int i = 1; i < 64; ++i) pm = fmaxf(pm, t[i]);
-            // Exchange partial maxima with the partner warp.  Buffer s is rewritten
-            // two steps later, only after every warp has arrived on x_bar for the
-            // step in between, i.e. after every warp has read it.
-            xch[s][half][row] = pm;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&x_bar[s]);
-            ok = mbar_wait(&x_bar[s], ph, abort_flag, status, 36);
-            if (!__all_sync(0xffffffffu, ok)) {
-                ok = false;
-                break;
-            }
-            const float mx = fmaxf(xch[s][0][row], xch[s][1][row]);
-            // P_j overwrites P_{j-1} and may rescale O: both need P.V_{j-1} done
-            if (j >= 1) {
-                ok = mbar_wait(&o_done, static_cast<uint32_t>((j - 1) & 1), abort_flag, status, 30);
-                if (!__all_sync(0xffffffffu, ok)) {
-                    ok = false;
-                    break;
-                }
-            }
+            for (int i = 1; i < 128; ++i) mx = fmaxf(mx, sc[i]);
+            mx *= c;  // scale > 0: the max of the scaled scores
             if (j == 0) {
                 m = mx;
             } else if (__any_sync(0xffffffffu, mx > m + kRescaleThreshold)) {
-                // raise the running max of the rows that need it
-                tc_fence_after();
+                // raise the running max of the rows that need it; O_t (after the
+                // previous P.V, complete before these scores were produced) and l
                 const float m_new = mx > m + kRescaleThreshold ? mx : m;
                 const float alpha = ex2(m - m_new);
 #pragma unroll 1
-                for (int c = 0; c < 2; ++c) {
+                for (int cc = 0; cc < 4; ++cc) {
                     uint32_t r[32];
-                    const uint32_t addr = tmem + 256u + static_cast<uint32_t>(half * 64 + c * 32) + lane_addr;
-                    tmem_ld_32x32b_x32(addr, r);
+                    tmem_ld_32x32b_x32(o_col + static_cast<uint32_t>(cc * 32), r);
                     tmem_ld_wait();
 #pragma unroll
                     for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-                    tmem_st_32x32b_x32(addr, r);
+                    tmem_st_32x32b_x32(o_col + static_cast<uint32_t>(cc * 32), r);
                 }
-                tmem_st_wait();
-                tc_fence_before();
                 l *= alpha;
                 m = m_new;
             }
-            // this thread's half of P = 2^(t - m) as bf16: K-half `half` of the
-            // swizzled tile, row `row`, 16-byte chunk c at physical chunk c ^ (row & 7)
-            uint8_t* prow = sP + half * kHalf + row * 128;
+            // P = 2^(s*c - m) as bf16 pairs over the first 64 score columns
             float rs = 0.f;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                float e[8];
+            for (int h = 0; h < 2; ++h) {
+                uint32_t w[32];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    e[i] = ex2(t[c * 8 + i] - m);
-                    rs += e[i];
+                for (int i = 0; i < 32; ++i) {
+                    const float e0 = ex2(fmaf(sc[h * 64 + 2 * i], c, -m));
+                    const float e1 = ex2(fmaf(sc[h * 64 + 2 * i + 1], c, -m));
+                    rs += e0 + e1;
+                    w[i] = pack_bf16x2(e0, e1);
                 }
-                const uint4 packed = make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]),
-                                                pack_bf16x2(e[4], e[5]), pack_bf16x2(e[6], e[7]));
-                *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = packed;
+                tmem_st_32x32b_x32(s_col + static_cast<uint32_t>(h * 32), w);
             }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[t]);
             l += rs;
-            fence_proxy_async_smem();  // generic-proxy writes of P -> visible to the tensor core
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full);
         }
-        // epilogue: O / l -> bf16, each thread its 64 columns of the row
-        if (ok) {
-            xl[half][row] = l;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&l_bar);
-            ok = __all_sync(0xffffffffu, mbar_wait(&l_bar, 0, abort_flag, status, 37));
-            if (ok) l = xl[0][row] + xl[1][row];
-        }
+        // epilogue: O / l -> bf16, the thread's whole row
         if (ok && nkv > 0) {
-            ok = mbar_wait(&o_done, static_cast<uint32_t>((nkv - 1) & 1), abort_flag, status, 32);
+            ok = mbar_wait(&done_bar, 0, abort_flag, status, 32);
             if (__all_sync(0xffffffffu, ok)) {
                 tc_fence_after();
                 const float inv = 1.0f / l;
-                uint16_t* orow =
-                    p.O + (static_cast<size_t>(head) * p.seq + static_cast<size_t>(qtile) * kBlock + row) * kHead + half * 64;
+                uint16_t* orow = p.O + (static_cast<size_t>(head) * p.seq + static_cast<size_t>(q0 + t * kBlock + row)) * kHead;
 #pragma unroll 1
-                for (int c = 0; c < 2; ++c) {
+                for (int cc = 0; cc < 4; ++cc) {
                     uint32_t r[32];
-                    tmem_ld_32x32b_x32(tmem + 256u + static_cast<uint32_t>(half * 64 + c * 32) + lane_addr, r);
+                    tmem_ld_32x32b_x32(o_col + static_cast<uint32_t>(cc * 32), r);
                     tmem_ld_wait();
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
@@ -342,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
                         o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
                         o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
                         o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
-                        reinterpret_cast<uint4*>(orow + c * 32)[v] = o;
+                        reinterpret_cast<uint4*>(orow + cc * 32)[v] = o;
                     }
                 }
             }
@@ -404,6 +371,8 @@ extern "C" int bee_b200_attention(int dt, const void* q, const void* k, const vo
         return fail(cudaErrorInvalidValue, "attention: head_dim %zu unsupported (128 only)", head_dim);
     if (seq % kBlock != 0 || seq > (1u << 30) || heads > 65535)
         return fail(cudaErrorInvalidValue, "attention: seq %zu must be a multiple of %d", seq, kBlock);
+    if (!(scale > 0.0f) || !(scale < 3.0e38f))
+        return fail(cudaErrorInvalidValue, "attention: scale must be positive and finite");
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
         return fail(cudaErrorInvalidValue, "attention: buffers must be 16-byte aligned");
     CUtensorMap tq, tk, tv;
@@ -423,7 +392,7 @@ extern "C" int bee_b200_attention(int dt, const void* q, const void* k, const vo
         if (e != cudaSuccess) return fail(static_cast<int>(e), "attention: shared memory attribute: %s", cudaGetErrorString(e));
         attr_set[dev] = true;
     }
-    dim3 grid(static_cast<unsigned>(seq / kBlock), static_cast<unsigned>(heads));
+    dim3 grid(static_cast<unsigned>((seq / kBlock + 1) / 2), static_cast<unsigned>(heads));
     attention_fwd_kernel<<<grid, kThreads, kSmem, as_stream(stream)>>>(tq, tk, tv, p);
     return launch_status("attention");
 }

@@ -208,8 +208,8 @@ BEE_B200_API int bee_b200_bmm(int dt_in, int dt_out, const void* A, const void* 
 /* Fused attention forward, per head: O = softmax(Q.K^T * scale) . V with
  * fp32 scores, softmax and accumulation; Q, K, V, O are [heads, seq, head_dim]
  * bf16, contiguous, 16-byte aligned.  One pass: scores and probabilities stay
- * in tensor memory / shared memory.  head_dim must be 128 and seq a multiple
- * of 128 (other shapes: compose bee_b200_bmm, bee_b200_softmax_rows_to and
+ * in tensor memory.  head_dim must be 128, seq a multiple of 128 and scale
+ * positive (other shapes: compose bee_b200_bmm, bee_b200_softmax_rows_to and
  * bee_b200_bmm).  New: the reference has no attention. */
 BEE_B200_API int bee_b200_attention(int dt, const void* q, const void* k, const void* v, void* o, size_t heads,
                                     size_t seq, size_t head_dim, float scale, bee_b200_stream_t stream);
