@@ -15,6 +15,11 @@ ranks per second (GB/s, 1e9).
 ``--impl reference`` times the reference's own CPU implementation of the same
 ops (the Bee::Tensor CPU path compiled from the reference sources into
 oracle/_ref, else the oracle port) on the host cores, rank 0 only.
+
+``--only NAME`` (profiling) skips the sweep and runs one of the extra configs
+alone (gemm_bf16_8192, rms_norm_rope_bf16, attention_bf16, gemm_f32_1024,
+transpose_f32_8192, ...), printing {"only": NAME, "extra": {...}}; the ncu
+captures of those kernels use it so that they run this file and nothing else.
 """
 from __future__ import annotations
 
@@ -360,6 +365,10 @@ def run_extras(args, d, dev, stream, peaks):
     st = stream.cuda_stream
     steps = max(3, min(args.steps, 20))
     warm = 3
+    only = getattr(args, "only", None)
+
+    def want(*names):
+        return only is None or only in names
     g = torch.Generator(device=dev).manual_seed(4321 + d.rank)
     out = {}
 
@@ -383,159 +392,160 @@ def run_extras(args, d, dev, stream, peaks):
         return c.value == 0
 
     with torch.cuda.stream(stream):
-        n = 8192
-        std = (1.0 / np.sqrt(n)) ** 0.5  # N(0, variance 1/sqrt(8192))
-        a = (torch.randn(n, n, device=dev, generator=g) * std).to(torch.bfloat16)
-        b = (torch.randn(n, n, device=dev, generator=g) * std).to(torch.bfloat16)
-        c = torch.empty(n, n, device=dev, dtype=torch.bfloat16)
-        flop = 2.0 * n ** 3
-        ms = timed(lambda: call("bee_b200_bmm", _capi.BF16, _capi.BF16, a.data_ptr(), b.data_ptr(), c.data_ptr(),
-                                1, n, n, n, 0, 1.0, st))
-        tf = d.world * flop / (ms / 1e3) / 1e12
-        out["gemm_bf16_8192"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
-                                 "frac_of_measured_bf16_burst": round(tf / d.world / peaks["bf16_tflops"], 3),
-                                 "frac_of_measured_bf16_sustained": round(tf / d.world / peaks["bf16_tflops_sustained"], 3),
-                                 "frac_of_spec_2250": round(tf / d.world / 2250.0, 3),
-                                 "scaling": "weak (column shards)", "status_ok": status_ok()}
+        if want("gemm_bf16_8192", "gemm_bf16_8192_splitk"):
+            n = 8192
+            std = (1.0 / np.sqrt(n)) ** 0.5  # N(0, variance 1/sqrt(8192))
+            a = (torch.randn(n, n, device=dev, generator=g) * std).to(torch.bfloat16)
+            b = (torch.randn(n, n, device=dev, generator=g) * std).to(torch.bfloat16)
+            c = torch.empty(n, n, device=dev, dtype=torch.bfloat16)
+            flop = 2.0 * n ** 3
+            ms = timed(lambda: call("bee_b200_bmm", _capi.BF16, _capi.BF16, a.data_ptr(), b.data_ptr(), c.data_ptr(),
+                                    1, n, n, n, 0, 1.0, st))
+            tf = d.world * flop / (ms / 1e3) / 1e12
+            out["gemm_bf16_8192"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
+                                     "frac_of_measured_bf16_burst": round(tf / d.world / peaks["bf16_tflops"], 3),
+                                     "frac_of_measured_bf16_sustained": round(tf / d.world / peaks["bf16_tflops_sustained"], 3),
+                                     "frac_of_spec_2250": round(tf / d.world / 2250.0, 3),
+                                     "scaling": "weak (column shards)", "status_ok": status_ok()}
 
-        # split-K: rank r multiplies A[:, K_r] by B[K_r, :]
-        klo, khi = shard_range(n, d.world, d.rank)
-        kr = khi - klo
-        ak = a[:, klo:khi].contiguous()
-        bk = b[klo:khi].contiguous()
-        part = torch.empty(n, n, device=dev, dtype=torch.float32)
+            # split-K: rank r multiplies A[:, K_r] by B[K_r, :]
+            klo, khi = shard_range(n, d.world, d.rank)
+            kr = khi - klo
+            ak = a[:, klo:khi].contiguous()
+            bk = b[klo:khi].contiguous()
+            part = torch.empty(n, n, device=dev, dtype=torch.float32)
 
-        def splitk():
-            call("bee_b200_bmm", _capi.BF16, _capi.F32, ak.data_ptr(), bk.data_ptr(), part.data_ptr(), 1, n, kr, n,
-                 0, 1.0, st)
-            if d.pg is not None:
-                import torch.distributed as dist
-                dist.all_reduce(part, op=dist.ReduceOp.SUM)
-            call("bee_b200_ew_cast", _capi.F32, part.data_ptr(), _capi.BF16, c.data_ptr(), n * n, st)
-        ms_nccl = timed(splitk)
-        del ak, bk, part
+            def splitk():
+                call("bee_b200_bmm", _capi.BF16, _capi.F32, ak.data_ptr(), bk.data_ptr(), part.data_ptr(), 1, n, kr, n,
+                     0, 1.0, st)
+                if d.pg is not None:
+                    import torch.distributed as dist
+                    dist.all_reduce(part, op=dist.ReduceOp.SUM)
+                call("bee_b200_ew_cast", _capi.F32, part.data_ptr(), _capi.BF16, c.data_ptr(), n * n, st)
+            ms_nccl = timed(splitk)
+            del ak, bk, part
 
-        from bee_b200.shard import SplitKGemm
-        fused = SplitKGemm(n, n, dev, group=d.pg)
-        a_ptr = a.data_ptr() + 2 * klo
-        b_ptr = b[klo:khi].data_ptr()
-        ms = timed(lambda: fused(a_ptr, n, b_ptr, kr, st))
-        ok_fused = status_ok()
-        fused.close()
-        tf = flop / (ms / 1e3) / 1e12
-        tf_nccl = flop / (ms_nccl / 1e3) / 1e12
-        owned = -(-(n // 256) ** 2 // d.world)
-        out["gemm_bf16_8192_splitk"] = {
-            "ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
-            "scaling": "strong (K sharded)",
-            "kernels": "tcgen05 GEMM whose epilogue stores fp32 partial tiles into the owner GPU over NVLink, "
-                       "owner reduce writing bf16 C into every GPU; two one-element NCCL all-reduces as barriers",
-            "nvlink_bytes_out_per_gpu": (d.world - 1) * owned * 256 * 256 * (4 + 2) if d.world > 1 else 0,
-            "status_ok": ok_fused,
-            "nccl_allreduce_chain": {"ms": round(ms_nccl, 4), "TFLOP/s": round(tf_nccl, 1),
-                                     "kernels": "bmm fp32 out -> NCCL all-reduce (fp32) -> cast",
-                                     "allreduce_bytes_per_gpu": n * n * 4 if d.world > 1 else 0}}
-        del a, b, c
+            from bee_b200.shard import SplitKGemm
+            fused = SplitKGemm(n, n, dev, group=d.pg)
+            a_ptr = a.data_ptr() + 2 * klo
+            b_ptr = b[klo:khi].data_ptr()
+            ms = timed(lambda: fused(a_ptr, n, b_ptr, kr, st))
+            ok_fused = status_ok()
+            fused.close()
+            tf = flop / (ms / 1e3) / 1e12
+            tf_nccl = flop / (ms_nccl / 1e3) / 1e12
+            owned = -(-(n // 256) ** 2 // d.world)
+            out["gemm_bf16_8192_splitk"] = {
+                "ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
+                "scaling": "strong (K sharded)",
+                "kernels": "tcgen05 GEMM whose epilogue stores fp32 partial tiles into the owner GPU over NVLink, "
+                           "owner reduce writing bf16 C into every GPU; two one-element NCCL all-reduces as barriers",
+                "nvlink_bytes_out_per_gpu": (d.world - 1) * owned * 256 * 256 * (4 + 2) if d.world > 1 else 0,
+                "status_ok": ok_fused,
+                "nccl_allreduce_chain": {"ms": round(ms_nccl, 4), "TFLOP/s": round(tf_nccl, 1),
+                                         "kernels": "bmm fp32 out -> NCCL all-reduce (fp32) -> cast",
+                                         "allreduce_bytes_per_gpu": n * n * 4 if d.world > 1 else 0}}
+            del a, b, c
+        if want("rms_norm_rope_bf16"):
+            rows, cols, seq, heads, hd = 16 * 2048, 4096, 2048, 32, 128
+            x = torch.randn(rows, cols, device=dev, generator=g).to(torch.bfloat16)
+            w = (1 + 0.02 * torch.randn(cols, device=dev, generator=g)).to(torch.bfloat16)
+            y = torch.empty_like(x)
+            ms = timed(lambda: call("bee_b200_rms_norm_rope", _capi.BF16, x.data_ptr(), w.data_ptr(), y.data_ptr(), rows,
+                                    seq, heads, hd, 1e-6, 10000.0, 0, st))
+            nbytes = 2 * rows * cols * 2 + cols * 2
+            gbs = d.world * nbytes / (ms / 1e3) / 1e9
+            out["rms_norm_rope_bf16"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                         "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                         "bytes_per_gpu": nbytes, "scaling": "weak (rows sharded)"}
+            del x, w, y
+        if want("attention_bf16"):
+            h, s_, dh = 32, 2048, 128
+            q = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
+            k = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
+            v = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
+            S = torch.empty(h, s_, s_, device=dev, dtype=torch.float32)
+            P = torch.empty(h, s_, s_, device=dev, dtype=torch.bfloat16)
+            o = torch.empty(h, s_, dh, device=dev, dtype=torch.bfloat16)
+            scale = 1.0 / np.sqrt(dh)
 
-        rows, cols, seq, heads, hd = 16 * 2048, 4096, 2048, 32, 128
-        x = torch.randn(rows, cols, device=dev, generator=g).to(torch.bfloat16)
-        w = (1 + 0.02 * torch.randn(cols, device=dev, generator=g)).to(torch.bfloat16)
-        y = torch.empty_like(x)
-        ms = timed(lambda: call("bee_b200_rms_norm_rope", _capi.BF16, x.data_ptr(), w.data_ptr(), y.data_ptr(), rows,
-                                seq, heads, hd, 1e-6, 10000.0, 0, st))
-        nbytes = 2 * rows * cols * 2 + cols * 2
-        gbs = d.world * nbytes / (ms / 1e3) / 1e9
-        out["rms_norm_rope_bf16"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
-                                     "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
-                                     "bytes_per_gpu": nbytes, "scaling": "weak (rows sharded)"}
-        del x, w, y
+            def attention_chain():
+                call("bee_b200_bmm", _capi.BF16, _capi.F32, q.data_ptr(), k.data_ptr(), S.data_ptr(), h, s_, dh, s_, 1,
+                     scale, st)
+                call("bee_b200_softmax_rows_to", _capi.F32, S.data_ptr(), _capi.BF16, P.data_ptr(), h * s_, s_, st)
+                call("bee_b200_bmm", _capi.BF16, _capi.BF16, P.data_ptr(), v.data_ptr(), o.data_ptr(), h, s_, s_, dh, 0,
+                     1.0, st)
 
-        h, s_, dh = 32, 2048, 128
-        q = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
-        k = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
-        v = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
-        S = torch.empty(h, s_, s_, device=dev, dtype=torch.float32)
-        P = torch.empty(h, s_, s_, device=dev, dtype=torch.bfloat16)
-        o = torch.empty(h, s_, dh, device=dev, dtype=torch.bfloat16)
-        scale = 1.0 / np.sqrt(dh)
-
-        def attention_chain():
-            call("bee_b200_bmm", _capi.BF16, _capi.F32, q.data_ptr(), k.data_ptr(), S.data_ptr(), h, s_, dh, s_, 1,
-                 scale, st)
-            call("bee_b200_softmax_rows_to", _capi.F32, S.data_ptr(), _capi.BF16, P.data_ptr(), h * s_, s_, st)
-            call("bee_b200_bmm", _capi.BF16, _capi.BF16, P.data_ptr(), v.data_ptr(), o.data_ptr(), h, s_, s_, dh, 0,
-                 1.0, st)
-
-        def attention_fused():
-            call("bee_b200_attention", _capi.BF16, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), h, s_, dh,
-                 scale, st)
-        aflop = 2.0 * 2 * h * s_ * s_ * dh
-        ms = timed(attention_fused)
-        tf = d.world * aflop / (ms / 1e3) / 1e12
-        ms_c = timed(attention_chain)
-        tf_c = d.world * aflop / (ms_c / 1e3) / 1e12
-        out["attention_bf16"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
-                                 "frac_of_measured_bf16_burst": round(tf / d.world / peaks["bf16_tflops"], 3),
-                                 "kernels": "fused (scores and probabilities stay on chip)",
-                                 "unfused_chain": {"ms": round(ms_c, 4), "TFLOP/s": round(tf_c, 1),
-                                                   "kernels": "bmm (QK^T, fp32 out) -> softmax fp32->bf16 -> bmm (PV)"},
-                                 "scaling": "weak (heads sharded)", "status_ok": status_ok()}
-        del q, k, v, S, P, o
-
-        a32 = torch.rand(1024, 1024, device=dev, generator=g) * 2 - 1
-        b32 = torch.rand(1024, 1024, device=dev, generator=g) * 2 - 1
-        c32 = torch.empty_like(a32)
-        ms = timed(lambda: call("bee_b200_matmul", _capi.F32, a32.data_ptr(), b32.data_ptr(), c32.data_ptr(), 1024,
-                                1024, 1024, st))
-        out["gemm_f32_1024"] = {"ms": round(ms, 4), "TFLOP/s": round(2.0 * 1024 ** 3 / (ms / 1e3) / 1e12, 2),
-                                "unit": "TFLOP/s (per GPU)", "path": "SIMT fp32 (parity config, rel tol 1e-4)"}
-        del a32, b32, c32
-
-        # layout and broadcast ops on the [8192, 8192] fp32 shard (HBM-bound, 2 x 256 MiB moved)
-        import ctypes
-        x = torch.randn(8192, 8192, device=dev, generator=g)
-        y = torch.empty_like(x)
-        ms = timed(lambda: call("bee_b200_transpose_2d", _capi.F32, x.data_ptr(), y.data_ptr(), 8192, 8192, st))
-        nbytes = 2 * 8192 * 8192 * 4
-        gbs = d.world * nbytes / (ms / 1e3) / 1e9
-        out["transpose_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
-                                     "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
-                                     "bytes_per_gpu": nbytes, "scaling": "weak"}
-        rmax = torch.empty(8192, device=dev)
-        call("bee_b200_reduce_axis", _capi.MAX, _capi.F32, x.data_ptr(), rmax.data_ptr(), 8192, 8192, 1, st)
-        shp = (ctypes.c_int64 * 2)(8192, 8192)
-        sa = (ctypes.c_int64 * 2)(8192, 1)
-        sb = (ctypes.c_int64 * 2)(1, 0)
-        ms = timed(lambda: call("bee_b200_ew_binary_strided", _capi.SUB, _capi.F32, 2, shp, x.data_ptr(), sa,
-                                rmax.data_ptr(), sb, y.data_ptr(), st))
-        nbytes = 2 * 8192 * 8192 * 4 + 8192 * 4
-        gbs = d.world * nbytes / (ms / 1e3) / 1e9
-        out["bcast_sub_rowmax_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
-                                            "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
-                                            "op": "x[8192, 8192] - rowmax[8192, 1] (broadcast, stride 0)",
-                                            "bytes_per_gpu": nbytes, "scaling": "weak"}
-        colsum = torch.empty(8192, device=dev)
-        ms = timed(lambda: call("bee_b200_reduce_axis", _capi.SUM, _capi.F32, x.data_ptr(), colsum.data_ptr(), 1, 8192,
-                                8192, st))
-        nbytes = 8192 * 8192 * 4 + 8192 * 4
-        gbs = d.world * nbytes / (ms / 1e3) / 1e9
-        out["sum_dim0_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
-                                    "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
-                                    "op": "sum(x, 0) of [8192, 8192] fp32 (column reduce, axis split over CTAs)",
-                                    "bytes_per_gpu": nbytes, "scaling": "weak"}
-        del colsum
-        kq = torch.randn(256, 2048, 128, device=dev, generator=g).to(torch.bfloat16)
-        kt = torch.empty(256, 128, 2048, device=dev, dtype=torch.bfloat16)
-        vsh = (ctypes.c_int64 * 3)(256, 128, 2048)
-        vst = (ctypes.c_int64 * 3)(2048 * 128, 1, 128)
-        ms = timed(lambda: call("bee_b200_strided_copy", _capi.BF16, kq.data_ptr(), 3, vsh, vst, kt.data_ptr(), st))
-        nbytes = 2 * 256 * 2048 * 128 * 2
-        gbs = d.world * nbytes / (ms / 1e3) / 1e9
-        out["contiguous_kt_bf16"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
-                                     "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
-                                     "op": "contiguous() of K^T, K [256, 2048, 128] bf16 (128 MiB each way)",
-                                     "bytes_per_gpu": nbytes, "scaling": "weak"}
-        del x, y, rmax, kq, kt
+            def attention_fused():
+                call("bee_b200_attention", _capi.BF16, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), h, s_, dh,
+                     scale, st)
+            aflop = 2.0 * 2 * h * s_ * s_ * dh
+            ms = timed(attention_fused)
+            tf = d.world * aflop / (ms / 1e3) / 1e12
+            ms_c = timed(attention_chain)
+            tf_c = d.world * aflop / (ms_c / 1e3) / 1e12
+            out["attention_bf16"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
+                                     "frac_of_measured_bf16_burst": round(tf / d.world / peaks["bf16_tflops"], 3),
+                                     "kernels": "fused (scores and probabilities stay on chip)",
+                                     "unfused_chain": {"ms": round(ms_c, 4), "TFLOP/s": round(tf_c, 1),
+                                                       "kernels": "bmm (QK^T, fp32 out) -> softmax fp32->bf16 -> bmm (PV)"},
+                                     "scaling": "weak (heads sharded)", "status_ok": status_ok()}
+            del q, k, v, S, P, o
+        if want("gemm_f32_1024"):
+            a32 = torch.rand(1024, 1024, device=dev, generator=g) * 2 - 1
+            b32 = torch.rand(1024, 1024, device=dev, generator=g) * 2 - 1
+            c32 = torch.empty_like(a32)
+            ms = timed(lambda: call("bee_b200_matmul", _capi.F32, a32.data_ptr(), b32.data_ptr(), c32.data_ptr(), 1024,
+                                    1024, 1024, st))
+            out["gemm_f32_1024"] = {"ms": round(ms, 4), "TFLOP/s": round(2.0 * 1024 ** 3 / (ms / 1e3) / 1e12, 2),
+                                    "unit": "TFLOP/s (per GPU)", "path": "SIMT fp32 (parity config, rel tol 1e-4)"}
+            del a32, b32, c32
+        if want("transpose_f32_8192", "bcast_sub_rowmax_f32_8192", "sum_dim0_f32_8192", "contiguous_kt_bf16"):
+            # layout and broadcast ops on the [8192, 8192] fp32 shard (HBM-bound, 2 x 256 MiB moved)
+            import ctypes
+            x = torch.randn(8192, 8192, device=dev, generator=g)
+            y = torch.empty_like(x)
+            ms = timed(lambda: call("bee_b200_transpose_2d", _capi.F32, x.data_ptr(), y.data_ptr(), 8192, 8192, st))
+            nbytes = 2 * 8192 * 8192 * 4
+            gbs = d.world * nbytes / (ms / 1e3) / 1e9
+            out["transpose_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                         "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                         "bytes_per_gpu": nbytes, "scaling": "weak"}
+            rmax = torch.empty(8192, device=dev)
+            call("bee_b200_reduce_axis", _capi.MAX, _capi.F32, x.data_ptr(), rmax.data_ptr(), 8192, 8192, 1, st)
+            shp = (ctypes.c_int64 * 2)(8192, 8192)
+            sa = (ctypes.c_int64 * 2)(8192, 1)
+            sb = (ctypes.c_int64 * 2)(1, 0)
+            ms = timed(lambda: call("bee_b200_ew_binary_strided", _capi.SUB, _capi.F32, 2, shp, x.data_ptr(), sa,
+                                    rmax.data_ptr(), sb, y.data_ptr(), st))
+            nbytes = 2 * 8192 * 8192 * 4 + 8192 * 4
+            gbs = d.world * nbytes / (ms / 1e3) / 1e9
+            out["bcast_sub_rowmax_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                                "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                                "op": "x[8192, 8192] - rowmax[8192, 1] (broadcast, stride 0)",
+                                                "bytes_per_gpu": nbytes, "scaling": "weak"}
+            colsum = torch.empty(8192, device=dev)
+            ms = timed(lambda: call("bee_b200_reduce_axis", _capi.SUM, _capi.F32, x.data_ptr(), colsum.data_ptr(), 1, 8192,
+                                    8192, st))
+            nbytes = 8192 * 8192 * 4 + 8192 * 4
+            gbs = d.world * nbytes / (ms / 1e3) / 1e9
+            out["sum_dim0_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                        "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                        "op": "sum(x, 0) of [8192, 8192] fp32 (column reduce, axis split over CTAs)",
+                                        "bytes_per_gpu": nbytes, "scaling": "weak"}
+            del colsum
+            kq = torch.randn(256, 2048, 128, device=dev, generator=g).to(torch.bfloat16)
+            kt = torch.empty(256, 128, 2048, device=dev, dtype=torch.bfloat16)
+            vsh = (ctypes.c_int64 * 3)(256, 128, 2048)
+            vst = (ctypes.c_int64 * 3)(2048 * 128, 1, 128)
+            ms = timed(lambda: call("bee_b200_strided_copy", _capi.BF16, kq.data_ptr(), 3, vsh, vst, kt.data_ptr(), st))
+            nbytes = 2 * 256 * 2048 * 128 * 2
+            gbs = d.world * nbytes / (ms / 1e3) / 1e9
+            out["contiguous_kt_bf16"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                         "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                         "op": "contiguous() of K^T, K [256, 2048, 128] bf16 (128 MiB each way)",
+                                         "bytes_per_gpu": nbytes, "scaling": "weak"}
+            del x, y, rmax, kq, kt
     stream.synchronize()
     return out
 
@@ -669,6 +679,8 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the GEMM / RMSNorm+RoPE / attention configs")
     ap.add_argument("--no-clocks", action="store_true", help="do not sample SM clocks during the timed region")
+    ap.add_argument("--only", default=None,
+                    help="profiling mode: run only the named extra config (e.g. attention_bf16) and print its timing")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
@@ -677,6 +689,16 @@ def main(argv=None):
         out = run_reference(args, d)
         if out is not None:
             print(json.dumps(out), flush=True)
+        return
+    if args.only:
+        import torch
+        d.init()
+        dev = torch.device("cuda", d.local)
+        stream = torch.cuda.Stream(device=dev)
+        extra = run_extras(args, d, dev, stream, load_peaks())
+        if d.rank == 0:
+            print(json.dumps({"only": args.only, "extra": extra}), flush=True)
+        d.close()
         return
     try:
         out = run_ours(args, d)
