@@ -61,6 +61,8 @@ SIGNATURES = {
     "bee_b200_rms_norm_rope": [_i, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _f, _d, _sz, _vp],
     "bee_b200_matmul": [_i, _vp, _vp, _vp, _sz, _sz, _sz, _vp],
     "bee_b200_bmm": [_i, _i, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _i, _f, _vp],
+    "bee_b200_bmm_strided": [_i, _i, _vp, _c.c_int64, _c.c_int64, _vp, _c.c_int64, _c.c_int64, _vp, _c.c_int64,
+                             _c.c_int64, _sz, _sz, _sz, _sz, _i, _f, _vp],
     "bee_b200_attention": [_i, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _f, _vp],
     "bee_b200_transpose_2d": [_i, _vp, _vp, _sz, _sz, _vp],
     "bee_b200_strided_copy": [_i, _vp, _i, _c.POINTER(_c.c_int64), _c.POINTER(_c.c_int64), _vp, _vp],

@@ -47,6 +47,7 @@ struct GemmParams {
     long long batch_stride_c;  // elements
     float alpha;
     void* C;
+    int c_vec;                 // C, ldc and batch_stride_c allow 16-byte stores
     // split-K scatter mode: fp32 256x256 partial tiles go to the receive buffer of
     // tile owner (tile % world), slot `rank`, over NVLink peer stores
     float* peer_recv[kMaxPeers];
@@ -94,7 +95,7 @@ __device__ __forceinline__ void store_chunk32(const GemmParams& p, const uint32_
     if (!row_ok || col0 >= p.N) return;
     if constexpr (OUT_F32) {
         float* dst = static_cast<float*>(p.C) + row_off + col0;
-        if (col0 + 32 <= p.N && (p.ldc & 3) == 0) {
+        if (col0 + 32 <= p.N && p.c_vec) {
 #pragma unroll
             for (int v = 0; v < 8; ++v)
                 reinterpret_cast<float4*>(dst)[v] =
@@ -107,7 +108,7 @@ __device__ __forceinline__ void store_chunk32(const GemmParams& p, const uint32_
         }
     } else {
         uint16_t* dst = static_cast<uint16_t*>(p.C) + row_off + col0;
-        if (col0 + 32 <= p.N && (p.ldc & 7) == 0) {
+        if (col0 + 32 <= p.N && p.c_vec) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
                 uint4 o;
@@ -646,8 +647,9 @@ template <typename T> __device__ __forceinline__ typename Acc<T>::type fma_acc(t
 // so shared-memory reads are broadcasts / conflict-free), BK = 16.
 template <typename T, typename TO>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A, const T* __restrict__ B,
-                                                        TO* __restrict__ C, int M, int N, int K, long long sA,
-                                                        long long sB, long long sC, int b_trans, float alpha) {
+                                                        TO* __restrict__ C, int M, int N, int K, long long lda,
+                                                        long long ldb, long long ldc, long long sA, long long sB,
+                                                        long long sC, int b_trans, float alpha) {
     using AT = typename Acc<T>::type;
     constexpr int BM = 64, BN = 64, BK = 16;
     __shared__ AT As[BK][BM + 1];
@@ -669,15 +671,15 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
             const int idx = threadIdx.x + l * 256;
             const int r = idx / BK, k = idx % BK;  // A: row r, col k
             const int gm = m0 + r, gk = k0 + k;
-            As[k][r] = (gm < M && gk < K) ? ld_as_acc(A + static_cast<long long>(gm) * K + gk) : AT(0);
+            As[k][r] = (gm < M && gk < K) ? ld_as_acc(A + static_cast<long long>(gm) * lda + gk) : AT(0);
             if (!b_trans) {
                 const int kk = idx / BN, n = idx % BN;  // B [K, N]
                 const int gk2 = k0 + kk, gn = n0 + n;
-                Bs[kk][n] = (gk2 < K && gn < N) ? ld_as_acc(B + static_cast<long long>(gk2) * N + gn) : AT(0);
+                Bs[kk][n] = (gk2 < K && gn < N) ? ld_as_acc(B + static_cast<long long>(gk2) * ldb + gn) : AT(0);
             } else {
                 const int n = idx / BK, kk = idx % BK;  // B stored [N, K]
                 const int gk2 = k0 + kk, gn = n0 + n;
-                Bs[kk][n] = (gk2 < K && gn < N) ? ld_as_acc(B + static_cast<long long>(gn) * K + gk2) : AT(0);
+                Bs[kk][n] = (gk2 < K && gn < N) ? ld_as_acc(B + static_cast<long long>(gn) * ldb + gk2) : AT(0);
             }
         }
         __syncthreads();
@@ -700,7 +702,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int gm = m0 + ty + 16 * i, gn = n0 + tx + 16 * j;
-            if (gm < M && gn < N) st_from_acc<T, TO>(C + static_cast<long long>(gm) * N + gn, acc[i][j], alpha);
+            if (gm < M && gn < N) st_from_acc<T, TO>(C + static_cast<long long>(gm) * ldc + gn, acc[i][j], alpha);
         }
 }
 
@@ -774,23 +776,43 @@ static int launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
     return launch_status("bmm(tcgen05 2-SM)");
 }
 
+// Element strides of a batched product: A[b][m][k] at A + b*sa + m*lda + k,
+// B[b][k][n] at B + b*sb + k*ldb + n (B^T: B[b][n][k] at B + b*sb + n*ldb + k),
+// C[b][m][n] at C + b*sc + m*ldc + n.
+struct BmmStrides {
+    long long lda, ldb, ldc, sa, sb, sc;
+};
+
+static BmmStrides contiguous_strides(size_t M, size_t K, size_t N, int b_trans) {
+    return BmmStrides{static_cast<long long>(K), static_cast<long long>(b_trans ? K : N), static_cast<long long>(N),
+                      static_cast<long long>(M * K), static_cast<long long>(K * N), static_cast<long long>(M * N)};
+}
+
 // bf16 x bf16 -> (bf16 | fp32) on the tensor cores.  Returns 0, an error, or
-// -1 when the shape cannot be expressed with TMA (caller falls back).
+// -1 when the shape or the strides cannot be expressed with TMA (the caller
+// falls back to the SIMT kernel).
 // M > 128 and N > 128 use 256x256 tiles on CTA pairs (cta_group::2); smaller
 // problems use 128xBN tiles on single CTAs.
 static int bmm_bf16_tc(int dt_out, const void* A, const void* B, void* C, size_t batch, size_t M, size_t K, size_t N,
-                       int b_trans, float alpha, cudaStream_t st) {
-    if (K % 8 != 0 || (!b_trans && N % 8 != 0) || !aligned16(A) || !aligned16(B)) return -1;
+                       int b_trans, float alpha, const BmmStrides& sd, cudaStream_t st) {
+    // TMA: 16-byte aligned bases, row and batch strides multiples of 16 bytes (8 bf16), positive
+    auto ok16 = [](long long v) { return v > 0 && v % 8 == 0 && v < (1ll << 36); };
+    if (!ok16(sd.lda) || !ok16(sd.ldb) || !aligned16(A) || !aligned16(B)) return -1;
+    if (batch > 1 && (!ok16(sd.sa) || !ok16(sd.sb))) return -1;
     if (M > (1u << 31) || N > (1u << 31) || K > (1u << 31) || batch > 65535) return -1;
+    const uint64_t sa = batch > 1 ? static_cast<uint64_t>(sd.sa) : static_cast<uint64_t>(sd.lda) * M;
+    const uint64_t sb = batch > 1 ? static_cast<uint64_t>(sd.sb) : static_cast<uint64_t>(sd.ldb) * (b_trans ? N : K);
     const int bn = N > 128 ? 256 : 128;
     const bool pair = N > 128 && M > 128;
     CUtensorMap ta, tb;
-    if (int rc = make_map(&ta, A, K, M, batch, K, M * K, 64, 128)) return rc;
+    if (make_map(&ta, A, K, M, batch, static_cast<uint64_t>(sd.lda), sa, 64, 128)) return -1;
     if (b_trans) {
-        if (int rc = make_map(&tb, B, K, N, batch, K, N * K, 64, pair ? 128u : static_cast<uint32_t>(bn))) return rc;
+        if (make_map(&tb, B, K, N, batch, static_cast<uint64_t>(sd.ldb), sb, 64,
+                     pair ? 128u : static_cast<uint32_t>(bn)))
+            return -1;
     } else {
         const uint32_t kbox = pair ? Pair2Cfg::BK : (bn == 256 ? TileCfg<256>::BK : TileCfg<128>::BK);
-        if (int rc = make_map(&tb, B, N, K, batch, N, K * N, 64, kbox)) return rc;
+        if (make_map(&tb, B, N, K, batch, static_cast<uint64_t>(sd.ldb), sb, 64, kbox)) return -1;
     }
     GemmParams p;
     p.M = static_cast<int>(M);
@@ -804,11 +826,13 @@ static int bmm_bf16_tc(int dt_out, const void* A, const void* B, void* C, size_t
     p.total_tiles = static_cast<int>(total);
     const size_t bk = pair ? Pair2Cfg::BK : (bn == 256 ? TileCfg<256>::BK : TileCfg<128>::BK);
     p.num_kb = static_cast<int>((K + bk - 1) / bk);
-    p.ldc = static_cast<long long>(N);
-    p.batch_stride_c = static_cast<long long>(M) * static_cast<long long>(N);
+    p.ldc = sd.ldc;
+    p.batch_stride_c = sd.sc;
     p.alpha = alpha;
     p.C = C;
     const bool f32 = dt_out == DT_F32;
+    const long long vq = f32 ? 4 : 8;  // elements per 16 bytes
+    p.c_vec = aligned16(C) && sd.ldc % vq == 0 && sd.sc % vq == 0 ? 1 : 0;
     if (pair) {
         if (b_trans) return f32 ? launch_tc_pair<true, true>(ta, tb, p, st) : launch_tc_pair<true, false>(ta, tb, p, st);
         return f32 ? launch_tc_pair<false, true>(ta, tb, p, st) : launch_tc_pair<false, false>(ta, tb, p, st);
@@ -819,21 +843,40 @@ static int bmm_bf16_tc(int dt_out, const void* A, const void* B, void* C, size_t
 
 template <typename T, typename TO>
 static int launch_simt(const void* A, const void* B, void* C, size_t batch, size_t M, size_t K, size_t N, int b_trans,
-                       float alpha, cudaStream_t st) {
+                       float alpha, const BmmStrides& sd, cudaStream_t st) {
     if (M > (1u << 30) || N > (1u << 30) || K > (1u << 30) || batch > 65535)
         return fail(cudaErrorInvalidValue, "matmul: extent too large for the SIMT path");
     dim3 grid(static_cast<unsigned>((N + 63) / 64), static_cast<unsigned>((M + 63) / 64), static_cast<unsigned>(batch));
     if (grid.y > 65535) return fail(cudaErrorInvalidValue, "matmul: M too large for the SIMT path");
     gemm_simt_kernel<T, TO><<<grid, 256, 0, st>>>(static_cast<const T*>(A), static_cast<const T*>(B), static_cast<TO*>(C),
-                                                  static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
-                                                  static_cast<long long>(M * K), static_cast<long long>(K * N),
-                                                  static_cast<long long>(M * N), b_trans, alpha);
+                                                  static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), sd.lda,
+                                                  sd.ldb, sd.ldc, sd.sa, sd.sb, sd.sc, b_trans, alpha);
     return launch_status("matmul(simt)");
 }
 
 }  // namespace bee_b200
 
 using namespace bee_b200;
+
+static int bmm_impl(int dt_in, int dt_out, const void* A, const void* B, void* C, size_t batch, size_t M, size_t K,
+                    size_t N, int b_trans, float alpha, const BmmStrides& sd, cudaStream_t st) {
+    if (dt_in == DT_BF16) {
+        if (dt_out != DT_BF16 && dt_out != DT_F32)
+            return fail(cudaErrorInvalidValue, "bmm: bf16 input needs a BF16 or F32 output, got %d", dt_out);
+        int rc = K == 0 ? -1 : bmm_bf16_tc(dt_out, A, B, C, batch, M, K, N, b_trans, alpha, sd, st);
+        if (rc != -1) return rc;
+        return dt_out == DT_F32 ? launch_simt<uint16_t, float>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st)
+                                : launch_simt<uint16_t, uint16_t>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st);
+    }
+    if (dt_out != dt_in) return fail(cudaErrorInvalidValue, "bmm: output dtype must equal input dtype for %d", dt_in);
+    switch (dt_in) {
+    case DT_F32: return launch_simt<float, float>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st);
+    case DT_F64: return launch_simt<double, double>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st);
+    case DT_I32: return launch_simt<int32_t, int32_t>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st);
+    case DT_I64: return launch_simt<int64_t, int64_t>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st);
+    default: return fail(cudaErrorInvalidValue, "bmm: unsupported dtype %d", dt_in);
+    }
+}
 
 extern "C" {
 
@@ -842,26 +885,36 @@ int bee_b200_bmm(int dt_in, int dt_out, const void* A, const void* B, void* C, s
     if (batch == 0 || M == 0 || N == 0) return ok();
     if (!A || !B || !C) return fail(cudaErrorInvalidValue, "bmm: null pointer");
     cudaStream_t st = as_stream(stream);
-    if (dt_in == DT_BF16) {
-        if (dt_out != DT_BF16 && dt_out != DT_F32)
-            return fail(cudaErrorInvalidValue, "bmm: bf16 input needs a BF16 or F32 output, got %d", dt_out);
-        if (K == 0) {
-            cudaError_t e = cudaMemsetAsync(C, 0, batch * M * N * (dt_out == DT_F32 ? 4 : 2), st);
-            return e == cudaSuccess ? ok() : fail(static_cast<int>(e), "bmm: %s", cudaGetErrorString(e));
-        }
-        int rc = bmm_bf16_tc(dt_out, A, B, C, batch, M, K, N, b_trans, alpha, st);
-        if (rc != -1) return rc;
-        return dt_out == DT_F32 ? launch_simt<uint16_t, float>(A, B, C, batch, M, K, N, b_trans, alpha, st)
-                                : launch_simt<uint16_t, uint16_t>(A, B, C, batch, M, K, N, b_trans, alpha, st);
+    if (dt_in == DT_BF16 && K == 0 && (dt_out == DT_BF16 || dt_out == DT_F32)) {
+        cudaError_t e = cudaMemsetAsync(C, 0, batch * M * N * (dt_out == DT_F32 ? 4 : 2), st);
+        return e == cudaSuccess ? ok() : fail(static_cast<int>(e), "bmm: %s", cudaGetErrorString(e));
     }
-    if (dt_out != dt_in) return fail(cudaErrorInvalidValue, "bmm: output dtype must equal input dtype for %d", dt_in);
-    switch (dt_in) {
-    case DT_F32: return launch_simt<float, float>(A, B, C, batch, M, K, N, b_trans, alpha, st);
-    case DT_F64: return launch_simt<double, double>(A, B, C, batch, M, K, N, b_trans, alpha, st);
-    case DT_I32: return launch_simt<int32_t, int32_t>(A, B, C, batch, M, K, N, b_trans, alpha, st);
-    case DT_I64: return launch_simt<int64_t, int64_t>(A, B, C, batch, M, K, N, b_trans, alpha, st);
-    default: return fail(cudaErrorInvalidValue, "bmm: unsupported dtype %d", dt_in);
+    return bmm_impl(dt_in, dt_out, A, B, C, batch, M, K, N, b_trans, alpha, contiguous_strides(M, K, N, b_trans), st);
+}
+
+int bee_b200_bmm_strided(int dt_in, int dt_out, const void* A, int64_t lda, int64_t stride_a, const void* B,
+                         int64_t ldb, int64_t stride_b, void* C, int64_t ldc, int64_t stride_c, size_t batch, size_t M,
+                         size_t K, size_t N, int b_trans, float alpha, bee_b200_stream_t stream) {
+    if (batch == 0 || M == 0 || N == 0) return ok();
+    if (!A || !B || !C) return fail(cudaErrorInvalidValue, "bmm_strided: null pointer");
+    if (M > (1u << 30) || N > (1u << 30) || K > (1u << 30) || batch > 65535)
+        return fail(cudaErrorInvalidValue, "bmm_strided: extent too large");
+    if (lda < static_cast<int64_t>(K) || ldb < static_cast<int64_t>(b_trans ? K : N) || ldc < static_cast<int64_t>(N))
+        return fail(cudaErrorInvalidValue, "bmm_strided: leading dimension shorter than a row");
+    if (stride_a < 0 || stride_b < 0 || stride_c < 0)
+        return fail(cudaErrorInvalidValue, "bmm_strided: negative batch stride");
+    if (batch > 1 && stride_c < static_cast<int64_t>((M - 1) * ldc + N))
+        return fail(cudaErrorInvalidValue, "bmm_strided: output batches overlap");
+    BmmStrides sd{lda, ldb, ldc, stride_a, stride_b, stride_c};
+    if (batch > 1 && stride_b == 0 && stride_a == static_cast<int64_t>(M) * lda && stride_c == static_cast<int64_t>(M) * ldc) {
+        // one B for every batch, A and C batches stacked row after row: one product of batch * M rows
+        M *= batch;
+        batch = 1;
+        sd.sa = static_cast<long long>(M) * lda;
+        sd.sc = static_cast<long long>(M) * ldc;
     }
+    // K == 0: C = 0 (row by row through the product path would read nothing); use the SIMT kernel
+    return bmm_impl(dt_in, dt_out, A, B, C, batch, M, K, N, b_trans, alpha, sd, as_stream(stream));
 }
 
 int bee_b200_matmul(int dt, const void* A, const void* B, void* C, size_t M, size_t K, size_t N,

@@ -205,6 +205,20 @@ BEE_B200_API int bee_b200_matmul(int dt, const void* A, const void* B, void* C, 
 BEE_B200_API int bee_b200_bmm(int dt_in, int dt_out, const void* A, const void* B, void* C, size_t batch, size_t M,
                               size_t K, size_t N, int b_trans, float alpha, bee_b200_stream_t stream);
 
+/* bee_b200_bmm over strided views (the bmm_strided of the boundary): element
+ * strides, A[b][m][k] at A + b*stride_a + m*lda + k; B[b][k][n] at
+ * B + b*stride_b + k*ldb + n (b_trans: B[b][n][k] at B + b*stride_b + n*ldb + k);
+ * C[b][m][n] at C + b*stride_c + m*ldc + n.  Leading dimensions at least a row;
+ * batch strides >= 0 (0 repeats an operand for every batch), output batches
+ * must not overlap.  bf16 inputs take the tensor cores when lda, ldb and the
+ * input batch strides are positive multiples of 8 elements and A, B are 16-byte
+ * aligned, else the SIMT kernel (same results up to accumulation order).
+ * New: the reference's matmul is 2-D and contiguous only. */
+BEE_B200_API int bee_b200_bmm_strided(int dt_in, int dt_out, const void* A, int64_t lda, int64_t stride_a, const void* B,
+                                      int64_t ldb, int64_t stride_b, void* C, int64_t ldc, int64_t stride_c,
+                                      size_t batch, size_t M, size_t K, size_t N, int b_trans, float alpha,
+                                      bee_b200_stream_t stream);
+
 /* Fused attention forward, per head: O = softmax(Q.K^T * scale) . V with
  * fp32 scores, softmax and accumulation; Q, K, V, O are [heads, seq, head_dim]
  * bf16, contiguous, 16-byte aligned.  One pass: scores and probabilities stay
