@@ -44,6 +44,9 @@ SIGNATURES = {
     "bee_b200_memcpy_d2d": [_vp, _vp, _sz, _vp],
     "bee_b200_memset": [_vp, _i, _sz, _vp],
     "bee_b200_stream_synchronize": [_vp],
+    "bee_b200_set_device": [_i],
+    "bee_b200_get_device": [_c.POINTER(_i)],
+    "bee_b200_device_count": [_c.POINTER(_i)],
     "bee_b200_ew_binary": [_i, _i, _vp, _vp, _vp, _sz, _vp],
     "bee_b200_ew_binary_strided": [_i, _i, _i, _c.POINTER(_c.c_int64), _vp, _c.POINTER(_c.c_int64), _vp,
                                    _c.POINTER(_c.c_int64), _vp, _vp],

@@ -174,6 +174,26 @@ int bee_b200_ipc_close(void* ptr) {
     return ok();
 }
 
+int bee_b200_set_device(int device) {
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "set_device(%d): %s", device, cudaGetErrorString(e));
+    return ok();
+}
+
+int bee_b200_get_device(int* device) {
+    if (!device) return fail(cudaErrorInvalidValue, "get_device: null pointer");
+    cudaError_t e = cudaGetDevice(device);
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "get_device: %s", cudaGetErrorString(e));
+    return ok();
+}
+
+int bee_b200_device_count(int* count) {
+    if (!count) return fail(cudaErrorInvalidValue, "device_count: null pointer");
+    cudaError_t e = cudaGetDeviceCount(count);
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "device_count: %s", cudaGetErrorString(e));
+    return ok();
+}
+
 int bee_b200_stream_synchronize(bee_b200_stream_t stream) {
     cudaError_t e = cudaStreamSynchronize(as_stream(stream));
     if (e != cudaSuccess) return fail(static_cast<int>(e), "stream_synchronize: %s", cudaGetErrorString(e));

@@ -63,6 +63,15 @@ BEE_B200_API int bee_b200_memcpy_d2d(void* dst, const void* src, size_t nbytes, 
 BEE_B200_API int bee_b200_memset(void* ptr, int value, size_t nbytes, bee_b200_stream_t stream);
 BEE_B200_API int bee_b200_stream_synchronize(bee_b200_stream_t stream);
 
+/* Device selection.  Every entry point works on the calling thread's current
+ * device (the reference's Device has no index, Bee/Base/Memory/Device.hpp:10);
+ * the stream passed to a call must belong to that device.  These wrap
+ * cudaSetDevice / cudaGetDevice / cudaGetDeviceCount for callers that do not
+ * link the CUDA runtime themselves (one process per GPU: set it once). */
+BEE_B200_API int bee_b200_set_device(int device);
+BEE_B200_API int bee_b200_get_device(int* device);
+BEE_B200_API int bee_b200_device_count(int* count);
+
 /* ------------------------------------------------------------- elementwise */
 
 /* out[i] = a[i] (op) b[i] over n contiguous elements of dtype dt.

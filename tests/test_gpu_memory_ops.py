@@ -375,3 +375,18 @@ def test_rms_norm_rope_llama_config(cuda, oracle):
     y2 = torch.empty_like(y)
     tc.rope(n, y2, seq, heads, hd, 10000.0, 0)
     assert_scaled(bf16_host(y2)[sel], out, pair, 1e-2, what="rms_norm then rope bf16")
+
+
+def test_device_selection(cuda):
+    import ctypes
+    from bee_b200 import _capi
+    torch = cuda
+    n = ctypes.c_int(-1)
+    _capi.call("bee_b200_device_count", ctypes.byref(n))
+    assert n.value == torch.cuda.device_count() >= 1
+    _capi.call("bee_b200_set_device", 0)
+    d = ctypes.c_int(-1)
+    _capi.call("bee_b200_get_device", ctypes.byref(d))
+    assert d.value == 0
+    with pytest.raises(_capi.BeeError):
+        _capi.call("bee_b200_set_device", 1000)
