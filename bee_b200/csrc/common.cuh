@@ -30,6 +30,9 @@ enum RedOp : int { RED_SUM = 0, RED_MIN = 1, RED_MAX = 2, RED_PROD = 3 };
 
 // Records a message for bee_b200_last_error() and returns `code`.
 int fail(int code, const char* fmt, ...);
+// fail() for a failed CUDA runtime call: also clears the runtime's last error,
+// so that the next launch check does not report it again.
+int api_fail(cudaError_t e, const char* fmt, ...);
 // Clears the thread-local message; returns 0.
 int ok();
 // Converts the pending launch error (if any) into a status.

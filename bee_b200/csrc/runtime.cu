@@ -30,6 +30,15 @@ int ok() {
     return 0;
 }
 
+int api_fail(cudaError_t e, const char* fmt, ...) {
+    cudaGetLastError();  // a failed runtime call must not be reported again by the next launch check
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+    va_end(ap);
+    return static_cast<int>(e);
+}
+
 int launch_status(const char* what) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(static_cast<int>(e), "%s: launch failed: %s", what, cudaGetErrorString(e));
@@ -91,14 +100,14 @@ int bee_b200_allocate(void** out_ptr, size_t nbytes, size_t alignment, bee_b200_
         return fail(cudaErrorInvalidValue, "allocate: alignment %zu unsupported (power of two <= 256)", alignment);
     if (nbytes == 0) return ok();
     cudaError_t e = pool_malloc(out_ptr, nbytes, as_stream(stream));
-    if (e != cudaSuccess) return fail(static_cast<int>(e), "allocate(%zu): %s", nbytes, cudaGetErrorString(e));
+    if (e != cudaSuccess) return api_fail(e, "allocate(%zu): %s", nbytes, cudaGetErrorString(e));
     return ok();
 }
 
 int bee_b200_deallocate(void* ptr, bee_b200_stream_t stream) {
     if (!ptr) return ok();
     cudaError_t e = cudaFreeAsync(ptr, as_stream(stream));
-    if (e != cudaSuccess) return fail(static_cast<int>(e), "deallocate: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return api_fail(e, "deallocate: %s", cudaGetErrorString(e));
     return ok();
 }
 
@@ -107,7 +116,7 @@ static int copy(void* dst, const void* src, size_t nbytes, cudaMemcpyKind kind, 
     if (nbytes == 0) return ok();
     if (!dst || !src) return fail(cudaErrorInvalidValue, "%s: null pointer", what);
     cudaError_t e = cudaMemcpyAsync(dst, src, nbytes, kind, as_stream(stream));
-    if (e != cudaSuccess) return fail(static_cast<int>(e), "%s(%zu): %s", what, nbytes, cudaGetErrorString(e));
+    if (e != cudaSuccess) return api_fail(e, "%s(%zu): %s", what, nbytes, cudaGetErrorString(e));
     return ok();
 }
 
@@ -127,7 +136,7 @@ int bee_b200_memset(void* ptr, int value, size_t nbytes, bee_b200_stream_t strea
     if (nbytes == 0) return ok();
     if (!ptr) return fail(cudaErrorInvalidValue, "memset: null pointer");
     cudaError_t e = cudaMemsetAsync(ptr, value & 0xff, nbytes, as_stream(stream));
-    if (e != cudaSuccess) return fail(static_cast<int>(e), "memset(%zu): %s", nbytes, cudaGetErrorString(e));
+    if (e != cudaSuccess) return api_fail(e, "memset(%zu): %s", nbytes, cudaGetErrorString(e));
     return ok();
 }
 
@@ -137,14 +146,14 @@ int bee_b200_ipc_alloc(void** out_ptr, size_t nbytes) {
     *out_ptr = nullptr;
     if (nbytes == 0) return fail(cudaErrorInvalidValue, "ipc_alloc: zero bytes");
     cudaError_t e = cudaMalloc(out_ptr, nbytes);
-    if (e != cudaSuccess) return fail(static_cast<int>(e), "ipc_alloc(%zu): %s", nbytes, cudaGetErrorString(e));
+    if (e != cudaSuccess) return api_fail(e, "ipc_alloc(%zu): %s", nbytes, cudaGetErrorString(e));
     return ok();
 }
 
 int bee_b200_ipc_free(void* ptr) {
     if (!ptr) return ok();
     cudaError_t e = cudaFree(ptr);
-    if (e != cudaSuccess) return fail(static_cast<int>(e), "ipc_free: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return api_fail(e, "ipc_free: %s", cudaGetErrorString(e));
     return ok();
 }
 
@@ -152,7 +161,7 @@ int bee_b200_ipc_handle(const void* ptr, void* handle_out) {
     if (!ptr || !handle_out) return fail(cudaErrorInvalidValue, "ipc_handle: null pointer");
     cudaIpcMemHandle_t h;
     cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
-    if (e != cudaSuccess) return fail(static_cast<int>(e), "ipc_handle: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return api_fail(e, "ipc_handle: %s", cudaGetErrorString(e));
     static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t is 64 bytes");
     memcpy(handle_out, &h, sizeof(h));
     return ok();
@@ -163,40 +172,40 @@ int bee_b200_ipc_open(const void* handle, void** out_ptr) {
     cudaIpcMemHandle_t h;
     memcpy(&h, handle, sizeof(h));
     cudaError_t e = cudaIpcOpenMemHandle(out_ptr, h, cudaIpcMemLazyEnablePeerAccess);
-    if (e != cudaSuccess) return fail(static_cast<int>(e), "ipc_open: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return api_fail(e, "ipc_open: %s", cudaGetErrorString(e));
     return ok();
 }
 
 int bee_b200_ipc_close(void* ptr) {
     if (!ptr) return ok();
     cudaError_t e = cudaIpcCloseMemHandle(ptr);
-    if (e != cudaSuccess) return fail(static_cast<int>(e), "ipc_close: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return api_fail(e, "ipc_close: %s", cudaGetErrorString(e));
     return ok();
 }
 
 int bee_b200_set_device(int device) {
     cudaError_t e = cudaSetDevice(device);
-    if (e != cudaSuccess) return fail(static_cast<int>(e), "set_device(%d): %s", device, cudaGetErrorString(e));
+    if (e != cudaSuccess) return api_fail(e, "set_device(%d): %s", device, cudaGetErrorString(e));
     return ok();
 }
 
 int bee_b200_get_device(int* device) {
     if (!device) return fail(cudaErrorInvalidValue, "get_device: null pointer");
     cudaError_t e = cudaGetDevice(device);
-    if (e != cudaSuccess) return fail(static_cast<int>(e), "get_device: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return api_fail(e, "get_device: %s", cudaGetErrorString(e));
     return ok();
 }
 
 int bee_b200_device_count(int* count) {
     if (!count) return fail(cudaErrorInvalidValue, "device_count: null pointer");
     cudaError_t e = cudaGetDeviceCount(count);
-    if (e != cudaSuccess) return fail(static_cast<int>(e), "device_count: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return api_fail(e, "device_count: %s", cudaGetErrorString(e));
     return ok();
 }
 
 int bee_b200_stream_synchronize(bee_b200_stream_t stream) {
     cudaError_t e = cudaStreamSynchronize(as_stream(stream));
-    if (e != cudaSuccess) return fail(static_cast<int>(e), "stream_synchronize: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return api_fail(e, "stream_synchronize: %s", cudaGetErrorString(e));
     return ok();
 }
 

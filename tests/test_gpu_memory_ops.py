@@ -390,3 +390,10 @@ def test_device_selection(cuda):
     assert d.value == 0
     with pytest.raises(_capi.BeeError):
         _capi.call("bee_b200_set_device", 1000)
+    # the failed call leaves no error behind for the next launch
+    x = torch.ones(64, device="cuda")
+    y = torch.empty_like(x)
+    _capi.call("bee_b200_ew_binary", _capi.ADD, _capi.F32, x.data_ptr(), x.data_ptr(), y.data_ptr(), 64,
+               torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert float(y.sum()) == 128.0
