@@ -37,11 +37,13 @@ CUDA_INC = str(Path(NVCC).resolve().parent.parent / "include")
 HOST_FLAGS = ["-O2", "-std=c++23", "-fPIC", "-I", str(ROOT / "include"), "-I", str(HOST), "-I", CUDA_INC]
 HOST_TEST_SRC = ROOT / "tests" / "cpp" / "test_host_bridge.cpp"
 HOST_TEST_BIN = LIB_DIR / "test_host_bridge"
+BRIDGE_BENCH_SRC = HOST / "bridge_bench.cpp"
+BRIDGE_BENCH_BIN = LIB_DIR / "bridge_bench"
 
 
 def _sources():
     cu = sorted(CSRC.glob("*.cu"))
-    cpp = sorted(HOST.glob("*.cpp"))
+    cpp = sorted(p for p in HOST.glob("*.cpp") if p.name != "bridge_bench.cpp")  # a program, not library code
     headers = sorted(CSRC.glob("*.cuh")) + sorted((ROOT / "include").glob("*.h")) + sorted(HOST.glob("*.hpp"))
     return cu, cpp, headers
 
@@ -85,6 +87,10 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if HOST_TEST_SRC.exists() and (force or _stale(HOST_TEST_BIN, [HOST_TEST_SRC, LIB] + headers)):
         _run(["g++", *HOST_FLAGS, str(HOST_TEST_SRC), "-o", str(HOST_TEST_BIN), "-L", str(LIB_DIR), "-lbee_b200",
               "-Wl,-rpath,$ORIGIN"])
+    # measurement program for the bridge's plumbing cost (run by bench.py)
+    if BRIDGE_BENCH_SRC.exists() and (force or _stale(BRIDGE_BENCH_BIN, [BRIDGE_BENCH_SRC, LIB] + headers)):
+        _run(["g++", *HOST_FLAGS, str(BRIDGE_BENCH_SRC), "-o", str(BRIDGE_BENCH_BIN), "-L", str(LIB_DIR),
+              "-lbee_b200", "-Wl,-rpath,$ORIGIN"])
     return LIB
 
 

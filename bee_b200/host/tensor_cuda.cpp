@@ -1,10 +1,12 @@
 // Implementation of the bee::tensor::cuda mirror over the bee_b200 C ABI.
-// Every call runs on the per-thread default stream and synchronises it before
-// returning, which is the observable contract of the reference's bridge.
+// Every call runs on the per-thread default stream and (in the default,
+// synchronous mode) synchronises it before returning, which is the observable
+// contract of the reference's bridge.
 #include "tensor_cuda.hpp"
 
 #include <cuda_runtime_api.h>
 
+#include <atomic>
 #include <format>
 
 #include "bee_b200.h"
@@ -14,6 +16,8 @@ namespace bee_b200::tensor_cuda {
 namespace {
 
 bee_b200_stream_t per_thread_stream() { return reinterpret_cast<bee_b200_stream_t>(cudaStreamPerThread); }
+
+std::atomic<bool> g_synchronous{true};
 
 Error make_error(int err, const char* op) {
     Error e;
@@ -31,20 +35,25 @@ Error plain_error(const char* msg) {
     return e;
 }
 
-// Converts a status into Result and, on success, synchronises the stream so
-// the call is complete when it returns.
+// Converts a status into Result and, on success in synchronous mode,
+// synchronises the stream so the call is complete when it returns.
 Result<void> finish(int err, const char* op) {
-    if (err == 0) err = bee_b200_stream_synchronize(per_thread_stream());
+    if (err == 0 && g_synchronous.load(std::memory_order_relaxed))
+        err = bee_b200_stream_synchronize(per_thread_stream());
     if (err != 0) return std::unexpected(make_error(err, op));
     return {};
 }
 
 }  // namespace
 
+auto set_synchronous(bool on) -> void { g_synchronous.store(on, std::memory_order_relaxed); }
+
+auto is_synchronous() -> bool { return g_synchronous.load(std::memory_order_relaxed); }
+
 auto allocate(std::size_t nbytes, std::size_t alignment) -> Result<void*> {
     void* p = nullptr;
     int err = bee_b200_allocate(&p, nbytes, alignment, per_thread_stream());
-    if (err == 0) err = bee_b200_stream_synchronize(per_thread_stream());
+    if (err == 0 && is_synchronous()) err = bee_b200_stream_synchronize(per_thread_stream());
     if (err != 0) return std::unexpected(make_error(err, "cuda::allocate"));
     return p;
 }
@@ -52,7 +61,7 @@ auto allocate(std::size_t nbytes, std::size_t alignment) -> Result<void*> {
 auto deallocate(void* p, std::size_t, std::size_t) -> void {
     if (!p) return;
     (void)bee_b200_deallocate(p, per_thread_stream());
-    (void)bee_b200_stream_synchronize(per_thread_stream());
+    if (is_synchronous()) (void)bee_b200_stream_synchronize(per_thread_stream());
 }
 
 auto memcpy_h2d(void* dst, const void* src, std::size_t nbytes) -> Result<void> {
@@ -60,7 +69,11 @@ auto memcpy_h2d(void* dst, const void* src, std::size_t nbytes) -> Result<void> 
 }
 
 auto memcpy_d2h(void* dst, const void* src, std::size_t nbytes) -> Result<void> {
-    return finish(bee_b200_memcpy_d2h(dst, src, nbytes, per_thread_stream()), "cuda::memcpy_d2h");
+    // waits in both modes: the host reads the data next
+    int err = bee_b200_memcpy_d2h(dst, src, nbytes, per_thread_stream());
+    if (err == 0) err = bee_b200_stream_synchronize(per_thread_stream());
+    if (err != 0) return std::unexpected(make_error(err, "cuda::memcpy_d2h"));
+    return {};
 }
 
 auto memcpy_d2d(void* dst, const void* src, std::size_t nbytes) -> Result<void> {

@@ -33,6 +33,19 @@ struct Error {
 
 template <typename T> using Result = std::expected<T, Error>;
 
+// ---- execution mode
+// Synchronous (the default) is the reference's contract: every call has
+// finished when it returns.  Asynchronous mode (a process-wide switch, like the
+// reference's backend choice, Bee/CUDA/Api.cpp:327-344) removes the per-call
+// synchronisation that the reference pays on every allocation, copy and kernel
+// (Bee/CUDA/Api.cpp:131-133, 188-190): calls are only enqueued on the calling
+// thread's per-thread stream, allocations come from the stream-ordered pool, and
+// synchronize() is the fence (kernel faults surface there).  Copies stay ordered
+// with the kernels of the same thread; memcpy_d2h waits in both modes, since
+// the host reads the data next.
+auto set_synchronous(bool on) -> void;
+[[nodiscard]] auto is_synchronous() -> bool;
+
 // ---- memory (Backend.hpp:20-46, 84)
 [[nodiscard]] auto allocate(std::size_t nbytes, std::size_t alignment) -> Result<void*>;
 auto deallocate(void* p, std::size_t nbytes, std::size_t alignment) -> void;

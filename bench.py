@@ -546,6 +546,22 @@ def run_extras(args, d, dev, stream, peaks):
                                          "op": "contiguous() of K^T, K [256, 2048, 128] bf16 (128 MiB each way)",
                                          "bytes_per_gpu": nbytes, "scaling": "weak"}
             del x, y, rmax, kq, kt
+
+        if want("bridge_matmul") and d.world == 1:
+            # plumbing cost around a matmul through the C++ bridge (bee_b200/host/bridge_bench.cpp),
+            # on the same GPU (the child inherits the device selection)
+            exe = ROOT / "bee_b200" / "_lib" / "bridge_bench"
+            if exe.exists():
+                stream.synchronize()
+                r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+                if r.returncode == 0:
+                    res = json.loads(r.stdout.strip().splitlines()[-1])
+                    res["what"] = ("allocate C + zero fill + matmul + free, every call synchronous (the reference's "
+                                   "bridge sequence) vs the asynchronous bridge (pool allocation, no fill) with one "
+                                   "fence per call, and pipelined")
+                    out["bridge_matmul"] = res
+                else:
+                    out["bridge_matmul"] = {"error": (r.stderr or r.stdout)[-300:]}
     stream.synchronize()
     return out
 

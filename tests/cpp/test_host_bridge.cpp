@@ -109,6 +109,31 @@ int main() {
               e1.error().message.find("cudaErrorInvalidValue") != std::string::npos && !e1.error().detail.empty(),
           "unknown dtype must give cudaErrorInvalidValue with a detail message");
 
+    // asynchronous mode: the same calls only enqueue; synchronize() is the fence
+    CHECK(tc::is_synchronous(), "synchronous is the default");
+    tc::set_synchronous(false);
+    {
+        std::vector<float> a2(n), c2(n);
+        for (size_t i = 0; i < n; ++i) a2[i] = uni(rng);
+        auto rt = tc::allocate(n * 4, 64);
+        CHECK(rt.has_value(), "async allocate");
+        float* dt2 = static_cast<float*>(*rt);
+        CHECK(tc::memcpy_h2d(da, a2.data(), n * 4).has_value(), "async h2d");
+        CHECK(tc::ew_binary(2, F32, da, da, dt2, n).has_value(), "async mul");
+        CHECK(tc::ew_binary(0, F32, dt2, da, dc, n).has_value(), "async add");
+        CHECK(tc::memcpy_d2h(c2.data(), dc, n * 4).has_value(), "async d2h (waits)");
+        for (size_t i = 0; i < n; ++i) {
+            volatile float sq = a2[i] * a2[i];  // two roundings, as the two kernels do
+            if (c2[i] != sq + a2[i]) {
+                CHECK(false, "async chain mismatch at %zu", i);
+                break;
+            }
+        }
+        tc::deallocate(dt2, n * 4, 64);
+        CHECK(tc::synchronize().has_value(), "async synchronize");
+    }
+    tc::set_synchronous(true);
+
     for (void* p : {static_cast<void*>(da), static_cast<void*>(db), static_cast<void*>(dc), static_cast<void*>(dxi),
                     static_cast<void*>(dsum), static_cast<void*>(dbf)})
         tc::deallocate(p, 0, 64);
