@@ -128,6 +128,38 @@ auto matmul(int dt, const void* A, const void* B, void* C, std::size_t M, std::s
     return finish(bee_b200_matmul(dt, A, B, C, M, K, N, per_thread_stream()), "cuda::ops::matmul");
 }
 
+auto transpose_2d(int dt, const void* src, void* dst, std::size_t rows, std::size_t cols) -> Result<void> {
+    if (rows == 0 || cols == 0) return {};
+    return finish(bee_b200_transpose_2d(dt, src, dst, rows, cols, per_thread_stream()), "cuda::ops::transpose_2d");
+}
+
+auto strided_copy(int dt, const void* src, int ndim, const std::int64_t* shape, const std::int64_t* strides, void* dst)
+    -> Result<void> {
+    return finish(bee_b200_strided_copy(dt, src, ndim, shape, strides, dst, per_thread_stream()),
+                  "cuda::ops::strided_copy");
+}
+
+auto ew_binary_strided(int op, int dt, int ndim, const std::int64_t* shape, const void* a, const std::int64_t* a_strides,
+                       const void* b, const std::int64_t* b_strides, void* out) -> Result<void> {
+    return finish(bee_b200_ew_binary_strided(op, dt, ndim, shape, a, a_strides, b, b_strides, out, per_thread_stream()),
+                  "cuda::ops::binary_strided");
+}
+
+auto reduce_mean_int(int dt, const void* src, double* dst, std::size_t outer, std::size_t axis, std::size_t inner)
+    -> Result<void> {
+    return finish(bee_b200_reduce_mean_int(dt, src, dst, outer, axis, inner, per_thread_stream()),
+                  "cuda::ops::reduce_mean_int");
+}
+
+auto bmm_strided(int dt_in, int dt_out, const void* A, std::int64_t lda, std::int64_t stride_a, const void* B,
+                 std::int64_t ldb, std::int64_t stride_b, void* C, std::int64_t ldc, std::int64_t stride_c,
+                 std::size_t batch, std::size_t M, std::size_t K, std::size_t N, bool b_transposed, float alpha)
+    -> Result<void> {
+    return finish(bee_b200_bmm_strided(dt_in, dt_out, A, lda, stride_a, B, ldb, stride_b, C, ldc, stride_c, batch, M, K,
+                                       N, b_transposed ? 1 : 0, alpha, per_thread_stream()),
+                  "cuda::ops::bmm_strided");
+}
+
 auto bmm(int dt_in, int dt_out, const void* A, const void* B, void* C, std::size_t batch, std::size_t M, std::size_t K,
          std::size_t N, bool b_transposed, float alpha) -> Result<void> {
     return finish(bee_b200_bmm(dt_in, dt_out, A, B, C, batch, M, K, N, b_transposed ? 1 : 0, alpha, per_thread_stream()),

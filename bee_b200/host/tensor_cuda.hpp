@@ -66,7 +66,24 @@ auto deallocate(void* p, std::size_t nbytes, std::size_t alignment) -> void;
 [[nodiscard]] auto matmul(int dt, const void* A, const void* B, void* C, std::size_t M, std::size_t K, std::size_t N)
     -> Result<void>;
 
+// 2-D transpose dst[i, j] = src[j, i] (Backend.hpp:72-73)
+[[nodiscard]] auto transpose_2d(int dt, const void* src, void* dst, std::size_t rows, std::size_t cols) -> Result<void>;
+
 // ---- new operators
+// Tensor::contiguous() of any view (shape / strides in elements, ndim <= 8; src at the first element)
+[[nodiscard]] auto strided_copy(int dt, const void* src, int ndim, const std::int64_t* shape, const std::int64_t* strides,
+                                void* dst) -> Result<void>;
+// a op b with broadcasting: out contiguous of `shape`, a and b strided views of it (stride 0 broadcasts)
+[[nodiscard]] auto ew_binary_strided(int op, int dt, int ndim, const std::int64_t* shape, const void* a,
+                                     const std::int64_t* a_strides, const void* b, const std::int64_t* b_strides,
+                                     void* out) -> Result<void>;
+// mean over `axis` of an I32 / I64 [outer, axis, inner] tensor into F64 [outer, inner]
+[[nodiscard]] auto reduce_mean_int(int dt, const void* src, double* dst, std::size_t outer, std::size_t axis,
+                                   std::size_t inner) -> Result<void>;
+[[nodiscard]] auto bmm_strided(int dt_in, int dt_out, const void* A, std::int64_t lda, std::int64_t stride_a,
+                               const void* B, std::int64_t ldb, std::int64_t stride_b, void* C, std::int64_t ldc,
+                               std::int64_t stride_c, std::size_t batch, std::size_t M, std::size_t K, std::size_t N,
+                               bool b_transposed, float alpha) -> Result<void>;
 [[nodiscard]] auto bmm(int dt_in, int dt_out, const void* A, const void* B, void* C, std::size_t batch, std::size_t M,
                        std::size_t K, std::size_t N, bool b_transposed, float alpha) -> Result<void>;
 [[nodiscard]] auto softmax_rows(int dt, const void* src, void* dst, std::size_t rows, std::size_t cols) -> Result<void>;

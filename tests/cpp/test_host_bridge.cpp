@@ -109,6 +109,27 @@ int main() {
               e1.error().message.find("cudaErrorInvalidValue") != std::string::npos && !e1.error().detail.empty(),
           "unknown dtype must give cudaErrorInvalidValue with a detail message");
 
+    // transpose_2d (Tests/CUDA/TransposeTests.cu:79-92: 3x5 f64, i * 0.5) and contiguous() of its view
+    {
+        std::vector<double> t(15), tt(15), tv(15);
+        for (int i = 0; i < 15; ++i) t[i] = i * 0.5;
+        auto rs = tc::allocate(15 * 8, 64), rd = tc::allocate(15 * 8, 64);
+        CHECK(rs.has_value() && rd.has_value(), "allocate transpose");
+        CHECK(tc::memcpy_h2d(*rs, t.data(), 15 * 8).has_value(), "h2d transpose");
+        CHECK(tc::transpose_2d(5, *rs, *rd, 3, 5).has_value(), "transpose_2d");
+        CHECK(tc::memcpy_d2h(tt.data(), *rd, 15 * 8).has_value(), "d2h transpose");
+        const std::int64_t shape[2] = {5, 3}, strides[2] = {1, 5};
+        CHECK(tc::strided_copy(5, *rs, 2, shape, strides, *rd).has_value(), "strided_copy");
+        CHECK(tc::memcpy_d2h(tv.data(), *rd, 15 * 8).has_value(), "d2h strided");
+        for (int i = 0; i < 5; ++i)
+            for (int j = 0; j < 3; ++j) {
+                CHECK(tt[i * 3 + j] == t[j * 5 + i], "transpose (%d, %d)", i, j);
+                CHECK(tv[i * 3 + j] == t[j * 5 + i], "strided copy (%d, %d)", i, j);
+            }
+        tc::deallocate(*rs, 0, 64);
+        tc::deallocate(*rd, 0, 64);
+    }
+
     // asynchronous mode: the same calls only enqueue; synchronize() is the fence
     CHECK(tc::is_synchronous(), "synchronous is the default");
     tc::set_synchronous(false);
