@@ -55,6 +55,8 @@ SIGNATURES = {
     "bee_b200_scale_fp": [_i, _vp, _d, _sz, _vp],
     "bee_b200_reduce_global": [_i, _i, _vp, _vp, _sz, _vp],
     "bee_b200_reduce_global_noalloc": [_i, _i, _vp, _vp, _sz, _vp],
+    "bee_b200_reduce_global_allranks": [_i, _i, _vp, _sz, _vp, _c.POINTER(_vp), _i, _i, _c.c_uint,
+                                        _c.c_ulonglong, _vp],
     "bee_b200_reduce_axis": [_i, _i, _vp, _vp, _sz, _sz, _sz, _vp],
     "bee_b200_reduce_mean_int": [_i, _vp, _vp, _sz, _sz, _sz, _vp],
     "bee_b200_softmax_rows": [_i, _vp, _vp, _sz, _sz, _vp],

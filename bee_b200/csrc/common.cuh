@@ -51,6 +51,8 @@ cudaError_t pool_malloc(void** ptr, size_t bytes, cudaStream_t st);
 
 // Reads and clears the status word of the fused attention kernel (cudaError_t).
 int attention_status_take(int* code);
+// Reads and clears the status word of the cross-GPU reduce (a peer that never arrived).
+int allranks_status_take(int* code);
 
 inline cudaStream_t as_stream(bee_b200_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 

@@ -924,12 +924,14 @@ int bee_b200_matmul(int dt, const void* A, const void* B, void* C, size_t M, siz
 
 int bee_b200_device_status(int* out_code) {
     if (!out_code) return fail(cudaErrorInvalidValue, "device_status: null pointer");
-    int zero = 0, attn = 0;
+    int zero = 0, attn = 0, coll = 0;
     cudaError_t e = cudaMemcpyFromSymbol(out_code, g_gemm_status, sizeof(int));
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_gemm_status, &zero, sizeof(int));
     if (e == cudaSuccess) e = static_cast<cudaError_t>(attention_status_take(&attn));
+    if (e == cudaSuccess) e = static_cast<cudaError_t>(allranks_status_take(&coll));
     if (e != cudaSuccess) return fail(static_cast<int>(e), "device_status: %s", cudaGetErrorString(e));
     if (*out_code == 0) *out_code = attn;
+    if (*out_code == 0) *out_code = coll;
     return ok();
 }
 

@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "reduce.cuh"
+#include "sm100.cuh"
 
 namespace bee_b200 {
 
@@ -373,6 +374,146 @@ static int run_axis(const void* src, void* dst, size_t outer, size_t axis, size_
     return with_split_scratch(tiles, G * outer * inner * sizeof(Acc), st, "reduce_axis", launch);
 }
 
+// ---------------------------------------------------------------- reduce across GPUs
+
+// Status word of the cross-GPU reduce (a peer that never delivered its partial
+// within the wait limit): read and cleared by bee_b200_device_status.
+__device__ int g_allranks_status = 0;
+
+int allranks_status_take(int* code) {
+    int zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(code, g_allranks_status, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_allranks_status, &zero, sizeof(int));
+    return static_cast<int>(e);
+}
+
+constexpr int kMaxRanks = 8;
+struct PeerSlots {
+    unsigned long long* slot[kMaxRanks];  // rank r's receive array (world words), mapped in this process
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// The global reduce of reduce_global_kernel, then, in the last CTA, the
+// exchange with the other GPUs of the job: thread 0 stores (tag, partial) as
+// one 64-bit word into slot `rank` of bank tag & 1 of every rank's receive
+// array (two banks of `world` words; peer stores
+// over NVLink), waits until its own array holds this call's tag in every slot
+// (bounded by wait_ns: on expiry it records the status and writes its local
+// partial), and folds the world partials in rank order, so every rank writes
+// the same bits.  32-bit element types only (the value and the tag share one
+// word, so a reader never sees a torn update).
+template <typename P>
+__global__ void __launch_bounds__(kGlobalThreads) reduce_allranks_kernel(const typename P::In* __restrict__ src,
+                                                                         typename P::Out* __restrict__ dst, size_t n,
+                                                                         GlobalScratch* scratch, PeerSlots peers,
+                                                                         int world, int rank, unsigned int tag,
+                                                                         unsigned long long wait_ns) {
+    using In = typename P::In;
+    using Acc = typename P::Acc;
+    static_assert(sizeof(Acc) == 4, "32-bit partials");
+    constexpr size_t E = 16 / sizeof(In);
+    constexpr size_t UNIT = static_cast<size_t>(kGlobalThreads) * kGlobalUnroll;
+    __shared__ Acc smem[32];
+    __shared__ bool last;
+    Acc* partials = reinterpret_cast<Acc*>(scratch + 1);
+    const unsigned tid = threadIdx.x;
+    Acc acc = P::identity();
+    if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+        const uint4* v = reinterpret_cast<const uint4*>(src);
+        const size_t nvec = n / E;
+        for (size_t base = static_cast<size_t>(blockIdx.x) * UNIT; base < nvec; base += static_cast<size_t>(gridDim.x) * UNIT) {
+            if (base + UNIT <= nvec) {
+                uint4 r[kGlobalUnroll];
+#pragma unroll
+                for (int k = 0; k < kGlobalUnroll; ++k) r[k] = ld_stream_u4(v + base + k * kGlobalThreads + tid);
+#pragma unroll
+                for (int k = 0; k < kGlobalUnroll; ++k) acc = fold<P>(acc, r[k]);
+            } else {
+                for (int k = 0; k < kGlobalUnroll; ++k) {
+                    const size_t idx = base + k * kGlobalThreads + tid;
+                    if (idx < nvec) acc = fold<P>(acc, ld_stream_u4(v + idx));
+                }
+            }
+        }
+        if (blockIdx.x == 0)
+            for (size_t j = nvec * E + tid; j < n; j += kGlobalThreads) acc = P::add(acc, src[j]);
+    } else {
+        const size_t stride = static_cast<size_t>(gridDim.x) * kGlobalThreads;
+        for (size_t j = static_cast<size_t>(blockIdx.x) * kGlobalThreads + tid; j < n; j += stride)
+            acc = P::add(acc, src[j]);
+    }
+    acc = block_reduce<P>(acc, smem);
+    if (tid == 0) {
+        partials[blockIdx.x] = acc;
+        __threadfence();
+        last = atomicAdd(&scratch->ticket, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    Acc r = P::identity();
+    for (unsigned i = tid; i < gridDim.x; i += kGlobalThreads)
+        r = P::combine(r, *reinterpret_cast<volatile Acc*>(partials + i));
+    r = block_reduce<P>(r, smem);
+    if (tid == 0) {
+        scratch->ticket = 0;
+        uint32_t bits;
+        memcpy(&bits, &r, 4);
+        const unsigned long long word = (static_cast<unsigned long long>(tag) << 32) | bits;
+        // two banks by tag parity: a rank that finished this call may already store the next
+        // call's word while a slower rank still reads this one
+        const int bank = static_cast<int>(tag & 1u) * world;
+        for (int p = 0; p < world; ++p) st_release_sys(peers.slot[p] + bank + rank, word);
+        Acc total = P::identity();
+        const unsigned long long* mine = peers.slot[rank] + bank;
+        const unsigned long long t0 = sm100::globaltimer_ns();
+        bool ok = true;
+        for (int s = 0; s < world && ok; ++s) {
+            unsigned long long w = ld_acquire_sys(mine + s);
+            for (uint32_t i = 0; static_cast<unsigned int>(w >> 32) != tag; ++i) {
+                if ((i & 255u) == 255u && sm100::globaltimer_ns() - t0 > wait_ns) {
+                    atomicCAS(&g_allranks_status, 0, 40 + s);
+                    ok = false;
+                    break;
+                }
+                w = ld_acquire_sys(mine + s);
+            }
+            if (ok) {
+                const uint32_t vb = static_cast<uint32_t>(w);
+                Acc v;
+                memcpy(&v, &vb, 4);
+                total = P::combine(total, v);
+            }
+        }
+        *dst = ok ? P::finish(total, n) : P::finish(r, n);
+    }
+}
+
+template <typename P>
+static int run_allranks(const void* src, void* dst, size_t n, const PeerSlots& peers, int world, int rank,
+                        unsigned int tag, unsigned long long wait_ns, cudaStream_t st) {
+    using In = typename P::In;
+    using Out = typename P::Out;
+    const unsigned grid = global_grid<In>(n, sm_count());
+    const size_t bytes = sizeof(GlobalScratch) + static_cast<size_t>(grid) * sizeof(typename P::Acc);
+    void* scratch = nullptr;
+    if (bytes > kStreamScratchBytes || stream_scratch(st, &scratch) != 0)
+        return fail(cudaErrorInvalidValue, "reduce_global_allranks: no per-stream scratch (stream capture?)");
+    cudaGetLastError();
+    reduce_allranks_kernel<P><<<grid, kGlobalThreads, 0, st>>>(static_cast<const In*>(src), static_cast<Out*>(dst), n,
+                                                               static_cast<GlobalScratch*>(scratch), peers, world,
+                                                               rank, tag, wait_ns);
+    return launch_status("reduce_global_allranks");
+}
+
 template <typename T>
 static int dispatch_global(int op, const void* src, void* dst, size_t n, cudaStream_t st) {
     switch (op) {
@@ -442,6 +583,47 @@ int bee_b200_reduce_mean_int(int dt, const void* src, double* dst, size_t outer,
     case DT_I64: return run_axis<MeanInt<int64_t>>(src, dst, outer, axis, inner, st);
     default: return fail(cudaErrorInvalidValue, "reduce_mean_int: dtype %d is not I32 or I64", dt);
     }
+}
+
+int bee_b200_reduce_global_allranks(int op, int dt, const void* src, size_t n, void* dst, void* const* recv_slots,
+                                    int world, int rank, unsigned int tag, unsigned long long wait_ns,
+                                    bee_b200_stream_t stream) {
+    if (n == 0) return fail(cudaErrorInvalidValue, "reduce_global_allranks: empty input");
+    if (!src || !dst || !recv_slots) return fail(cudaErrorInvalidValue, "reduce_global_allranks: null pointer");
+    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
+        return fail(cudaErrorInvalidValue, "reduce_global_allranks: rank %d / world %d out of range (world <= %d)", rank,
+                    world, kMaxRanks);
+    if (tag == 0) return fail(cudaErrorInvalidValue, "reduce_global_allranks: tag 0 is reserved (fresh slots read 0)");
+    PeerSlots peers{};
+    for (int r = 0; r < world; ++r) {
+        if (!recv_slots[r] || (reinterpret_cast<uintptr_t>(recv_slots[r]) & 7u) != 0)
+            return fail(cudaErrorInvalidValue, "reduce_global_allranks: receive array %d missing or misaligned", r);
+        peers.slot[r] = static_cast<unsigned long long*>(recv_slots[r]);
+    }
+    cudaStream_t st = as_stream(stream);
+    switch (dt) {
+    case DT_I32:
+        switch (op) {
+        case RED_SUM: return run_allranks<ElemRed<RED_SUM, int32_t>>(src, dst, n, peers, world, rank, tag, wait_ns, st);
+        case RED_MIN: return run_allranks<ElemRed<RED_MIN, int32_t>>(src, dst, n, peers, world, rank, tag, wait_ns, st);
+        case RED_MAX: return run_allranks<ElemRed<RED_MAX, int32_t>>(src, dst, n, peers, world, rank, tag, wait_ns, st);
+        case RED_PROD: return run_allranks<ElemRed<RED_PROD, int32_t>>(src, dst, n, peers, world, rank, tag, wait_ns, st);
+        default: break;
+        }
+        break;
+    case DT_F32:
+        switch (op) {
+        case RED_SUM: return run_allranks<ElemRed<RED_SUM, float>>(src, dst, n, peers, world, rank, tag, wait_ns, st);
+        case RED_MIN: return run_allranks<ElemRed<RED_MIN, float>>(src, dst, n, peers, world, rank, tag, wait_ns, st);
+        case RED_MAX: return run_allranks<ElemRed<RED_MAX, float>>(src, dst, n, peers, world, rank, tag, wait_ns, st);
+        case RED_PROD: return run_allranks<ElemRed<RED_PROD, float>>(src, dst, n, peers, world, rank, tag, wait_ns, st);
+        default: break;
+        }
+        break;
+    default:
+        return fail(cudaErrorInvalidValue, "reduce_global_allranks: dtype %d unsupported (I32 or F32)", dt);
+    }
+    return fail(cudaErrorInvalidValue, "reduce_global_allranks: unknown op code %d", op);
 }
 
 }  // extern "C"

@@ -5,8 +5,10 @@ NCCL (through torch.distributed) carries the only exchange steps:
 
 * row-wise ops (elementwise, cast, row reduce, softmax, RMSNorm, RoPE) shard by
   rows and need no collective;
-* the global integer sum all-reduces one partial per rank (integer addition
-  wraps identically in any order, so the result is bit-exact);
+* the global integer sum exchanges one partial per rank inside the reduce kernel
+  (PeerReduce: the last block stores its partial into every rank's CUDA IPC
+  receive array over NVLink and folds the world partials in rank order; integer
+  addition wraps identically in any order, so the result is bit-exact);
 * GEMM shards by output columns (no collective) or by K (split-K, SplitKGemm:
   the GEMM epilogue stores fp32 partial tiles straight into the owning GPU's
   receive buffer over NVLink, the owner sums and casts its tiles and writes
@@ -46,6 +48,80 @@ def allgather_rows(local, group=None):
     parts = [torch.empty_like(local) for _ in range(dist.get_world_size(group))]
     dist.all_gather(parts, local.contiguous(), group=group)
     return torch.cat(parts, 0)
+
+
+def _exchange_handles(handle: bytes, world: int, group, device):
+    """All-gathers one IPC handle (bytes) per rank over the process group."""
+    import torch
+    import torch.distributed as dist
+    mine = torch.tensor(list(handle), dtype=torch.uint8, device=device)
+    if world == 1:
+        return [handle]
+    allh = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(allh, mine, group=group)
+    return [bytes(h.cpu().tolist()) for h in allh]
+
+
+class PeerReduce:
+    """Global reduce over the ranks of one box in one kernel launch
+    (bee_b200_reduce_global_allranks): every rank's dst receives the reduction
+    of all ranks' inputs, folded in rank order.  Set-up allocates this rank's
+    IPC receive array (one 8-byte slot per rank, zeroed), all-gathers the
+    handles and opens the peers' arrays; each call uses a fresh tag."""
+
+    def __init__(self, device, group=None, wait_ns: int = 2_000_000_000):
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        from . import _capi
+        self._capi = _capi
+        self.device = torch.device(device)
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world > 8:
+            raise ValueError("PeerReduce supports at most 8 GPUs")
+        self.group, self.wait_ns, self.tag = group, int(wait_ns), 0
+        self._own, self._opened = [], []
+        buf = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _capi.call("bee_b200_ipc_alloc", ctypes.byref(buf), 256)
+            self._own.append(buf.value)
+            _capi.call("bee_b200_memset", buf, 0, 256, None)
+            _capi.call("bee_b200_stream_synchronize", None)
+            h = (ctypes.c_ubyte * 64)()
+            _capi.call("bee_b200_ipc_handle", buf, ctypes.byref(h))
+            ptrs = []
+            for r, hb in enumerate(_exchange_handles(bytes(h), self.world, group, self.device)):
+                if r == self.rank:
+                    ptrs.append(buf.value)
+                    continue
+                out = ctypes.c_void_p()
+                _capi.call("bee_b200_ipc_open", ctypes.byref((ctypes.c_ubyte * 64).from_buffer_copy(hb)),
+                           ctypes.byref(out))
+                self._opened.append(out.value)
+                ptrs.append(out.value)
+            self._slots = (ctypes.c_void_p * self.world)(*ptrs)
+            torch.cuda.synchronize(self.device)
+
+    def __call__(self, op: int, dt: int, src_ptr: int, n: int, dst_ptr: int, stream_ptr):
+        self.tag = self.tag % 0xFFFFFFFF + 1  # 1 .. 2^32 - 1: never the zero of a fresh slot
+        self._capi.call("bee_b200_reduce_global_allranks", op, dt, src_ptr, n, dst_ptr, self._slots, self.world,
+                        self.rank, self.tag, self.wait_ns, stream_ptr)
+
+    def close(self):
+        import torch
+        if not self._own:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier(group=self.group)  # no peer still stores into our array
+        with torch.cuda.device(self.device):
+            for ptr in self._opened:
+                self._capi.call("bee_b200_ipc_close", ptr)
+            for ptr in self._own:
+                self._capi.call("bee_b200_ipc_free", ptr)
+        self._opened, self._own = [], []
 
 
 class SplitKGemm:

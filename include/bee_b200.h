@@ -143,6 +143,22 @@ BEE_B200_API int bee_b200_reduce_global(int op, int dt, const void* src, void* d
 BEE_B200_API int bee_b200_reduce_global_noalloc(int op, int dt, const void* src, void* dst, size_t n,
                                                 bee_b200_stream_t stream);
 
+/* New: the global reduce across the GPUs of one box in one launch (the only
+ * exchange step of the row-sharded sweep).  Each rank reduces its shard; the
+ * kernel's last block stores (tag, partial) as one 64-bit word into slot `rank`
+ * of every rank's receive array (peer stores over NVLink), waits until its own
+ * array holds `tag` in all `world` slots, and folds the partials in rank order,
+ * so every rank's dst gets the same bits.  recv_slots[r]: rank r's receive
+ * array (2 * world 8-byte words, two banks used by tag parity; CUDA IPC memory
+ * opened in this process, zeroed once); tag: nonzero, consecutive calls
+ * consecutive values (e.g. a call counter), the same on every rank.  The wait
+ * is bounded by wait_ns: a peer that does not deliver in time leaves dst = the
+ * local partial and a nonzero code for bee_b200_device_status.  I32 and F32,
+ * every reduce op; world <= 8; all ranks call with the same op, dtype and tag. */
+BEE_B200_API int bee_b200_reduce_global_allranks(int op, int dt, const void* src, size_t n, void* dst,
+                                                 void* const* recv_slots, int world, int rank, unsigned int tag,
+                                                 unsigned long long wait_ns, bee_b200_stream_t stream);
+
 /* [outer, axis, inner] -> [outer, inner] (same dtype set as reduce_global;
  * F32 sums accumulate in fp32).  Replaces ops_reduce_axis
  * (Bee/CUDA/Ops/OpsBridge.hpp:32) behind tensor::cuda::reduce_axis

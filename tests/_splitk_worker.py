@@ -1,5 +1,6 @@
-"""One rank of the two-process split-K parity check (launched by
-tests/test_gpu_splitk.py under torch.distributed.run, one process per GPU).
+"""One rank of the two-process checks of the multi-GPU paths (launched by
+tests/test_gpu_splitk.py under torch.distributed.run, one process per GPU):
+the split-K GEMM and the cross-GPU global reduce (PeerReduce).
 
 Every rank builds the same A [M, K] and B [K, N] (same seed), multiplies its
 K shard through SplitKGemm (peer stores over NVLink, NCCL barriers), and checks
@@ -19,7 +20,7 @@ def main():
     import torch
     import torch.distributed as dist
     from bee_b200 import _capi
-    from bee_b200.shard import SplitKGemm, shard_range
+    from bee_b200.shard import PeerReduce, SplitKGemm, shard_range
 
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dev = torch.device("cuda", int(os.environ["LOCAL_RANK"]))
@@ -53,6 +54,23 @@ def main():
                 print(f"rank {rank}: {bad} of {m * n} entries differ ({m}x{k}x{n})", flush=True)
                 dist.destroy_process_group()
                 sys.exit(1)
+        # cross-GPU int32 sum: every call (both tag banks) equals the NCCL sum of the partials
+        pr = PeerReduce(dev)
+        for call in range(5):
+            g = torch.Generator(device=dev).manual_seed(100 * call + rank)
+            x = torch.randint(-1000, 1001, ((1 << 20) + 7 * call,), device=dev, generator=g, dtype=torch.int32)
+            out = torch.zeros(1, dtype=torch.int32, device=dev)
+            pr(_capi.SUM, _capi.I32, x.data_ptr(), x.numel(), out.data_ptr(), stream.cuda_stream)
+            part = torch.zeros(1, dtype=torch.int32, device=dev)
+            _capi.call("bee_b200_reduce_global", _capi.SUM, _capi.I32, x.data_ptr(), part.data_ptr(), x.numel(),
+                       stream.cuda_stream)
+            dist.all_reduce(part)
+            stream.synchronize()
+            if int(out.item()) != int(part.item()):
+                print(f"rank {rank}: peer reduce {int(out.item())} != {int(part.item())} (call {call})", flush=True)
+                dist.destroy_process_group()
+                sys.exit(1)
+        pr.close()
     dist.destroy_process_group()
     print(f"SPLITK_OK rank {rank}", flush=True)
 
