@@ -29,7 +29,6 @@ import os
 import statistics
 import subprocess
 import sys
-import threading
 import time
 from pathlib import Path
 
@@ -73,9 +72,31 @@ def load_peaks():
 
 # ---------------------------------------------------------------- clocks
 
+_SAMPLER_CHILD = r"""
+import sys, time
+import pynvml as nv
+bus, period = sys.argv[1], float(sys.argv[2])
+nv.nvmlInit()
+h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+print("max", nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM), flush=True)
+import select
+while True:
+    print("s", nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), nv.nvmlDeviceGetCurrentClocksEventReasons(h), flush=True)
+    r, _, _ = select.select([sys.stdin], [], [], period)
+    if r:
+        break
+print("s", nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), nv.nvmlDeviceGetCurrentClocksEventReasons(h), flush=True)
+nv.nvmlShutdown()
+"""
+
+
 class ClockSampler:
     """Samples SM clock and throttle reasons through NVML every few ms while the
-    timed region runs (nvidia-smi's 200 ms period is longer than the region)."""
+    timed region runs (nvidia-smi's 200 ms period is longer than the region).
+
+    The sampling runs in a separate process: a sampling thread inside a bench
+    process measurably delayed that process's launches (most visibly at N > 1,
+    where every rank waits for the slowest one at the step's exchange)."""
 
     def __init__(self, bus_id: str, period_s: float = 0.002, enabled: bool = True):
         self.enabled = enabled
@@ -83,9 +104,7 @@ class ClockSampler:
         self.period = period_s
         self.samples = []
         self.max_mhz = None
-        self._stop = threading.Event()
-        self._thread = None
-        self._nvml = None
+        self._proc = None
         self.error = None
 
     def __enter__(self):
@@ -93,49 +112,40 @@ class ClockSampler:
             self.error = "disabled (--no-clocks, or not rank 0)"
             return self
         try:
-            import pynvml as nv
-            nv.nvmlInit()
-            self._nvml = nv
-            self._h = nv.nvmlDeviceGetHandleByPciBusId(self.bus_id)
-            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self._h, nv.NVML_CLOCK_SM)
-            self._sample()
-            self._thread = threading.Thread(target=self._run, daemon=True)
-            self._thread.start()
+            self._proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_CHILD, self.bus_id, str(self.period)],
+                                          stdin=subprocess.PIPE, stdout=subprocess.PIPE, stderr=subprocess.PIPE,
+                                          text=True)
+            first = self._proc.stdout.readline().split()  # "max <MHz>" once NVML is up
+            if len(first) != 2 or first[0] != "max":
+                raise RuntimeError("sampler did not start: " + (self._proc.stderr.read() or "")[-200:])
+            self.max_mhz = int(first[1])
+            self._proc.stdout.readline()  # the first sample has been taken: sampling is running
         except Exception as e:  # NVML missing: report no samples rather than fail the bench
             self.error = f"{type(e).__name__}: {e}"
+            if self._proc is not None:
+                self._proc.kill()
+                self._proc = None
         return self
 
-    def _sample(self):
-        nv = self._nvml
-        mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
-        reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-        self.samples.append((mhz, reasons))
-
-    def _run(self):
-        while not self._stop.is_set():
-            try:
-                self._sample()
-            except Exception:
-                break
-            time.sleep(self.period)
-
     def __exit__(self, *exc):
-        self._stop.set()
-        if self._thread is not None:
-            self._thread.join(timeout=2)
+        if self._proc is None:
+            return
         try:
-            if self._nvml is not None:
-                self._sample()
-                self._nvml.nvmlShutdown()
-        except Exception:
-            pass
+            out, _ = self._proc.communicate(input="stop\n", timeout=10)
+            for line in out.splitlines():
+                f = line.split()
+                if len(f) == 3 and f[0] == "s":
+                    self.samples.append((int(f[1]), int(f[2])))
+        except Exception as e:
+            self.error = f"{type(e).__name__}: {e}"
+            self._proc.kill()
 
     def summary(self):
         bits = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
         reasons = sorted({name for _, r in self.samples for name, b in bits.items() if r & b})
         out = {"sm_mhz": statistics.median([m for m, _ in self.samples]) if self.samples else None,
-               "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples), "source": "nvml",
-               "gpu": "rank 0's", "period_ms": self.period * 1e3}
+               "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples),
+               "source": "nvml, separate sampling process", "gpu": "rank 0's", "period_ms": self.period * 1e3}
         if self.error:
             out["error"] = self.error
         return out
@@ -288,11 +298,8 @@ def run_ours(args, d: Dist):
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     d.barrier()
     torch.cuda.synchronize()
-    # One sampler, on rank 0, for its own GPU: with a sampling thread in every rank the
-    # NVML calls of 8 processes measurably stretched the 8-GPU step (0.77 ms against
-    # 0.59 ms without sampling); one sampler every 10 ms costs nothing measurable.
-    with ClockSampler(smi_id(dev), period_s=0.002 if d.world == 1 else 0.01,
-                      enabled=not args.no_clocks and d.rank == 0) as clk:
+    # One sampler (its own process), on rank 0, for rank 0's GPU.
+    with ClockSampler(smi_id(dev), period_s=0.002, enabled=not args.no_clocks and d.rank == 0) as clk:
         t0.record(stream)
         for k in range(args.steps):
             step(per_step_events[k])
