@@ -392,12 +392,14 @@ struct PeerSlots {
     unsigned long long* slot[kMaxRanks];  // rank r's receive array (world words), mapped in this process
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+// Relaxed system-scope accesses: the tag and the value travel in one 64-bit
+// word, so a reader that sees the tag has the value; no fence is needed.
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long* p) {
     unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
@@ -471,20 +473,21 @@ __global__ void __launch_bounds__(kGlobalThreads) reduce_allranks_kernel(const t
         // two banks by tag parity: a rank that finished this call may already store the next
         // call's word while a slower rank still reads this one
         const int bank = static_cast<int>(tag & 1u) * world;
-        for (int p = 0; p < world; ++p) st_release_sys(peers.slot[p] + bank + rank, word);
+        for (int p = 0; p < world; ++p) st_relaxed_sys(peers.slot[p] + bank + rank, word);
         Acc total = P::identity();
         const unsigned long long* mine = peers.slot[rank] + bank;
         const unsigned long long t0 = sm100::globaltimer_ns();
         bool ok = true;
         for (int s = 0; s < world && ok; ++s) {
-            unsigned long long w = ld_acquire_sys(mine + s);
+            unsigned long long w = ld_relaxed_sys(mine + s);
             for (uint32_t i = 0; static_cast<unsigned int>(w >> 32) != tag; ++i) {
-                if ((i & 255u) == 255u && sm100::globaltimer_ns() - t0 > wait_ns) {
+                if ((i & 63u) == 63u && sm100::globaltimer_ns() - t0 > wait_ns) {
                     atomicCAS(&g_allranks_status, 0, 40 + s);
                     ok = false;
                     break;
                 }
-                w = ld_acquire_sys(mine + s);
+                __nanosleep(64);  // poll gently: the wait is normally a few microseconds
+                w = ld_relaxed_sys(mine + s);
             }
             if (ok) {
                 const uint32_t vb = static_cast<uint32_t>(w);

@@ -7,7 +7,8 @@ Workload "sweep" (the headline): the memory-bound op sweep on row-major
 row sum, row max, row softmax, and the bit-exact int32 full sum of a uniform
 [-1000, 1000] tensor.  A step runs every op once over the GPU's shard; rows are
 sharded over GPUs with 8192 rows per GPU (weak scaling: the global tensor is
-[8192*N, 8192]); the only exchange is the int32 sum's, done inside its reduce
+[8192*N, 8192]); the only exchange is the int32 sum's: an NCCL all-reduce of
+the per-GPU partials, or with --exchange peer the exchange inside the reduce
 kernel over NVLink peer memory (bee_b200.shard.PeerReduce).  Each tensor is 256 MiB, larger than the 126 MB L2, so no L2 flush is
 needed between ops or steps.  ``value`` is the algorithmic bytes moved by all
 ranks per second (GB/s, 1e9).
@@ -29,6 +30,7 @@ import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 from pathlib import Path
 
@@ -72,39 +74,26 @@ def load_peaks():
 
 # ---------------------------------------------------------------- clocks
 
-_SAMPLER_CHILD = r"""
-import sys, time
-import pynvml as nv
-bus, period = sys.argv[1], float(sys.argv[2])
-nv.nvmlInit()
-h = nv.nvmlDeviceGetHandleByPciBusId(bus)
-print("max", nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM), flush=True)
-import select
-while True:
-    print("s", nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), nv.nvmlDeviceGetCurrentClocksEventReasons(h), flush=True)
-    r, _, _ = select.select([sys.stdin], [], [], period)
-    if r:
-        break
-print("s", nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), nv.nvmlDeviceGetCurrentClocksEventReasons(h), flush=True)
-nv.nvmlShutdown()
-"""
-
-
 class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML every few ms while the
-    timed region runs (nvidia-smi's 200 ms period is longer than the region).
+    """Samples the SM clock (every period) and the clock-event (throttle) reasons
+    (every `reasons_every` samples) through NVML while the timed region runs
+    (nvidia-smi's 200 ms period is longer than the region).  One thread, in rank
+    0's process: NVML queries stretch cross-GPU waits (NCCL's and ours) on the
+    queried GPU, a sampler in every rank or in a separate process much more so
+    than one thread in one rank, and the reasons query more than the clock one."""
 
-    The sampling runs in a separate process: a sampling thread inside a bench
-    process measurably delayed that process's launches (most visibly at N > 1,
-    where every rank waits for the slowest one at the step's exchange)."""
-
-    def __init__(self, bus_id: str, period_s: float = 0.002, enabled: bool = True):
+    def __init__(self, bus_id: str, period_s: float = 0.002, enabled: bool = True, reasons_every: int = 10,
+                 at_s=None):
         self.enabled = enabled
         self.bus_id = bus_id
         self.period = period_s
+        self.at_s = at_s  # instead of periodic sampling: one sample per offset (seconds after entry)
+        self.reasons_every = max(1, reasons_every)
         self.samples = []
         self.max_mhz = None
-        self._proc = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
         self.error = None
 
     def __enter__(self):
@@ -112,40 +101,67 @@ class ClockSampler:
             self.error = "disabled (--no-clocks, or not rank 0)"
             return self
         try:
-            self._proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_CHILD, self.bus_id, str(self.period)],
-                                          stdin=subprocess.PIPE, stdout=subprocess.PIPE, stderr=subprocess.PIPE,
-                                          text=True)
-            first = self._proc.stdout.readline().split()  # "max <MHz>" once NVML is up
-            if len(first) != 2 or first[0] != "max":
-                raise RuntimeError("sampler did not start: " + (self._proc.stderr.read() or "")[-200:])
-            self.max_mhz = int(first[1])
-            self._proc.stdout.readline()  # the first sample has been taken: sampling is running
+            import pynvml as nv
+            nv.nvmlInit()
+            self._nvml = nv
+            self._h = nv.nvmlDeviceGetHandleByPciBusId(self.bus_id)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self._h, nv.NVML_CLOCK_SM)
+            self._sample(True)
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
         except Exception as e:  # NVML missing: report no samples rather than fail the bench
             self.error = f"{type(e).__name__}: {e}"
-            if self._proc is not None:
-                self._proc.kill()
-                self._proc = None
         return self
 
-    def __exit__(self, *exc):
-        if self._proc is None:
+    def _sample(self, with_reasons: bool):
+        nv = self._nvml
+        mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+        reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h) if with_reasons else None
+        self.samples.append((mhz, reasons))
+
+    def _run(self):
+        if self.at_s is not None:
+            t0 = time.perf_counter()
+            for t in self.at_s:
+                if self._stop.wait(max(0.0, t - (time.perf_counter() - t0))):
+                    return
+                try:
+                    self._sample(True)
+                except Exception:
+                    return
             return
+        k = 0
+        while not self._stop.wait(self.period):
+            k += 1
+            try:
+                self._sample(k % self.reasons_every == 0)
+            except Exception:
+                break
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
         try:
-            out, _ = self._proc.communicate(input="stop\n", timeout=10)
-            for line in out.splitlines():
-                f = line.split()
-                if len(f) == 3 and f[0] == "s":
-                    self.samples.append((int(f[1]), int(f[2])))
-        except Exception as e:
-            self.error = f"{type(e).__name__}: {e}"
-            self._proc.kill()
+            if self._nvml is not None:
+                self._sample(True)
+                self._nvml.nvmlShutdown()
+        except Exception:
+            pass
 
     def summary(self):
         bits = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
-        reasons = sorted({name for _, r in self.samples for name, b in bits.items() if r & b})
+        reasons = sorted({name for _, r in self.samples if r is not None for name, b in bits.items() if r & b})
         out = {"sm_mhz": statistics.median([m for m, _ in self.samples]) if self.samples else None,
                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples),
-               "source": "nvml, separate sampling process", "gpu": "rank 0's", "period_ms": self.period * 1e3}
+               "reason_samples": sum(1 for _, r in self.samples if r is not None), "source": "nvml",
+               "gpu": "rank 0's"}
+        if self.at_s is None:
+            out["period_ms"] = self.period * 1e3
+        else:
+            out["schedule"] = ("one sample at entry and at exit, and during the timed region at "
+                               + ", ".join(f"{t * 1e3:.1f} ms" for t in self.at_s)
+                               + " (sparse: at N > 1 each NVML query stretches the step)")
         if self.error:
             out["error"] = self.error
         return out
@@ -239,22 +255,32 @@ def run_ours(args, d: Dist):
         o_rsum = torch.empty(ROWS, dtype=torch.float32, device=dev)
         o_rmax = torch.empty(ROWS, dtype=torch.float32, device=dev)
         o_sm = torch.empty_like(dx)
-        o_isum = torch.zeros(1, dtype=torch.int32, device=dev)
     stream.synchronize()
 
     F32, BF16, I32 = _capi.F32, _capi.BF16, _capi.I32
-    # Across GPUs the int32 sum is one kernel: its last block exchanges the partials with
-    # the other GPUs over NVLink (CUDA IPC slots) and every rank folds them in rank order.
+    # Across GPUs the int32 partials are combined by an NCCL all-reduce after the kernel
+    # (default), or with --exchange peer inside the reduce kernel itself: its last block
+    # stores the partial into every rank's CUDA IPC slot over NVLink and folds the world
+    # partials in rank order (PeerReduce).  The peer exchange measures 0.576 ms per step at
+    # N=2 against 0.595 with NCCL, but its spin-wait slows sharply while NVML is queried
+    # on the GPU (the clock sampling the timed region needs), so NCCL is the default.
     peer = None
-    if d.pg is not None:
+    if d.pg is not None and args.exchange == "peer":
         from bee_b200.shard import PeerReduce
         peer = PeerReduce(dev, group=d.pg)
 
+    # step k writes its int32 sum into its own slot, so that the NCCL all-reduce of step k
+    # (on a second stream, overlapping step k + 1) never races the next step's kernel
+    ring = torch.zeros(args.warmup + args.steps + 1, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()
+    slot = [0]
+
     def sum_i32():
+        dst = ring[slot[0]].data_ptr()
         if peer is not None:
-            peer(0, I32, dxi.data_ptr(), N_EL, o_isum.data_ptr(), st)
+            peer(0, I32, dxi.data_ptr(), N_EL, dst, st)
         else:
-            call("bee_b200_reduce_global", 0, I32, dxi.data_ptr(), o_isum.data_ptr(), N_EL, st)
+            call("bee_b200_reduce_global", 0, I32, dxi.data_ptr(), dst, N_EL, st)
     ops = [
         ("add_f32", lambda: call("bee_b200_ew_binary", 0, F32, dx.data_ptr(), dy.data_ptr(), o_add.data_ptr(), N_EL, st)),
         ("mul_f32", lambda: call("bee_b200_ew_binary", 2, F32, dx.data_ptr(), dy.data_ptr(), o_mul.data_ptr(), N_EL, st)),
@@ -266,10 +292,24 @@ def run_ours(args, d: Dist):
     ]
     launches_per_step = len(ops)
 
-    def allreduce_isum():
-        pass  # the cross-GPU exchange is inside sum_i32 (PeerReduce)
+    comm = torch.cuda.Stream(device=dev) if (d.pg is not None and peer is None) else None
 
-    def step(evs=None):
+    def allreduce_isum(overlap=True):
+        """Combines this step's int32 partials across GPUs: an NCCL all-reduce on the
+        communication stream, after this step's kernels, overlapping the next step."""
+        if comm is None:
+            return
+        import torch.distributed as dist
+        if overlap:
+            comm.wait_stream(stream)
+            with torch.cuda.stream(comm):
+                dist.all_reduce(ring[slot[0]], op=dist.ReduceOp.SUM)
+        else:
+            with torch.cuda.stream(stream):
+                dist.all_reduce(ring[slot[0]], op=dist.ReduceOp.SUM)
+
+    def step(k, evs=None):
+        slot[0] = k
         for i, (_, fn) in enumerate(ops):
             if evs is not None:
                 evs[i].record(stream)
@@ -278,10 +318,19 @@ def run_ours(args, d: Dist):
             evs[len(ops)].record(stream)
         allreduce_isum()
 
-    # warm-up (also checks the int32 sum against the host, bit-exact)
-    for _ in range(args.warmup):
-        step()
+    # warm-up (also checks the int32 sum against the host, bit-exact); the last warm-up
+    # step's duration places the clock samples inside the timed region at N > 1
+    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for k in range(args.warmup):
+        if k == args.warmup - 1:
+            w0.record(stream)
+        step(k)
+        if k == args.warmup - 1:
+            w1.record(stream)
+    if comm is not None:
+        stream.wait_stream(comm)
     stream.synchronize()
+    est_region_s = w0.elapsed_time(w1) / 1e3 * args.steps
     want = int(xi.astype(np.int64).sum())
     if d.pg is not None:
         import torch.distributed as dist
@@ -289,7 +338,7 @@ def run_ours(args, d: Dist):
         dist.all_reduce(t)
         want = int(t.item())
     want32 = ((want + 2**31) % 2**32) - 2**31
-    got = int(o_isum.item())
+    got = int(ring[args.warmup - 1].item())
     if got != want32:
         raise SystemExit(f"int32 sum mismatch: {got} != {want32}")
 
@@ -299,10 +348,18 @@ def run_ours(args, d: Dist):
     d.barrier()
     torch.cuda.synchronize()
     # One sampler (its own process), on rank 0, for rank 0's GPU.
-    with ClockSampler(smi_id(dev), period_s=0.002, enabled=not args.no_clocks and d.rank == 0) as clk:
+    # N = 1: periodic sampling (no measurable cost).  N > 1: every NVML query stretches
+    # the step (measured at N = 2: 0.57 ms per step without sampling, 0.71 with the SM
+    # clock read every 2 ms), so the samples are few: a quarter, half and three quarters
+    # of the way through the region.
+    at_s = None if d.world == 1 else [est_region_s * f for f in (0.25, 0.5, 0.75)]
+    with ClockSampler(smi_id(dev), period_s=args.clock_period_ms / 1e3, reasons_every=args.clock_reasons_every,
+                      enabled=not args.no_clocks and d.rank == 0, at_s=at_s) as clk:
         t0.record(stream)
         for k in range(args.steps):
-            step(per_step_events[k])
+            step(args.warmup + k, per_step_events[k])
+        if comm is not None:
+            stream.wait_stream(comm)  # every step's exchange is inside the timed region
         t1.record(stream)
         stream.synchronize()
     d.barrier()
@@ -325,8 +382,9 @@ def run_ours(args, d: Dist):
     # end to end through the C ABI with host buffers: H2D inputs, ops, D2H outputs
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, d, lib, dev, stream, hx, hy, hxi, ops, allreduce_isum,
-                      [o_add, o_mul, o_bf, o_rsum, o_rmax, o_sm, o_isum], [dx, dy, dxi])
+        slot[0] = ring.numel() - 1  # a slot of its own, exchanged on the compute stream
+        e2e = run_e2e(args, d, lib, dev, stream, hx, hy, hxi, ops, lambda: allreduce_isum(overlap=False),
+                      [o_add, o_mul, o_bf, o_rsum, o_rmax, o_sm, ring[slot[0]:slot[0] + 1]], [dx, dy, dxi])
 
     clocks = clk.summary()
     if peer is not None:
@@ -347,9 +405,9 @@ def run_ours(args, d: Dist):
                                    "(8192 rows per GPU, global [8192*N, 8192])",
                        "ops": [n for n, _ in ops], "bytes_per_step_per_gpu": STEP_BYTES,
                        "l2": "inputs larger than L2 (each tensor 256 MiB > 126 MB), no flush",
-                       "parallelism": f"rows sharded over {d.world} GPU(s); the int32 partial sums exchanged "
-                                      "inside the reduce kernel over NVLink peer memory (no NCCL in the step)"
-                                      if d.world > 1 else "1 GPU"},
+                       "parallelism": (f"rows sharded over {d.world} GPUs; int32 partial sums combined "
+                                       + ("inside the reduce kernel over NVLink peer memory" if peer is not None
+                                          else "by an NCCL all-reduce")) if d.world > 1 else "1 GPU"},
             "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(dom_gbs, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(dom_gbs / peaks["hbm_gbs"], 3),
                          "peak_source": peaks["source"], "algorithmic_bytes": OP_BYTES[dominant],
@@ -720,6 +778,11 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the GEMM / RMSNorm+RoPE / attention configs")
     ap.add_argument("--no-clocks", action="store_true", help="do not sample SM clocks during the timed region")
+    ap.add_argument("--clock-period-ms", type=float, default=2.0, help="SM clock sampling period")
+    ap.add_argument("--clock-reasons-every", type=int, default=10,
+                    help="query the throttle reasons every this many clock samples")
+    ap.add_argument("--exchange", choices=["nccl", "peer"], default="nccl",
+                    help="how the int32 partial sums are combined across GPUs")
     ap.add_argument("--only", default=None,
                     help="profiling mode: run only the named extra config (e.g. attention_bf16) and print its timing")
     args = ap.parse_args(argv)
