@@ -44,6 +44,7 @@ SIGNATURES = {
     "bee_b200_memcpy_d2d": [_vp, _vp, _sz, _vp],
     "bee_b200_memset": [_vp, _i, _sz, _vp],
     "bee_b200_stream_synchronize": [_vp],
+    "bee_b200_clock_probe": [_c.c_ulonglong, _vp, _vp],
     "bee_b200_set_device": [_i],
     "bee_b200_get_device": [_c.POINTER(_i)],
     "bee_b200_device_count": [_c.POINTER(_i)],

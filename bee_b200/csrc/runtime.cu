@@ -81,6 +81,20 @@ cudaError_t pool_malloc(void** ptr, size_t bytes, cudaStream_t st) {
     return cudaMallocFromPoolAsync(ptr, bytes, pool, st);
 }
 
+// SM clock of the SM this runs on, measured against the global nanosecond
+// timer over `ns` nanoseconds (one thread; bounded by the timer and by an
+// iteration cap).  Launched on a side stream while other work runs, it reads
+// the clock under load without querying NVML.
+__global__ void clock_probe_kernel(unsigned long long ns, float* out_mhz) {
+    unsigned long long t0, t1, c0, c1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    c0 = clock64();
+    t1 = t0;
+    for (unsigned int i = 0; i < (1u << 26) && t1 - t0 < ns; ++i) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    c1 = clock64();
+    *out_mhz = t1 > t0 ? static_cast<float>(static_cast<double>(c1 - c0) * 1e3 / static_cast<double>(t1 - t0)) : 0.f;
+}
+
 }  // namespace bee_b200
 
 using namespace bee_b200;
@@ -201,6 +215,13 @@ int bee_b200_device_count(int* count) {
     cudaError_t e = cudaGetDeviceCount(count);
     if (e != cudaSuccess) return api_fail(e, "device_count: %s", cudaGetErrorString(e));
     return ok();
+}
+
+int bee_b200_clock_probe(unsigned long long ns, float* out_mhz, bee_b200_stream_t stream) {
+    if (!out_mhz) return fail(cudaErrorInvalidValue, "clock_probe: null pointer");
+    if (ns == 0 || ns > 10000000ull) return fail(cudaErrorInvalidValue, "clock_probe: duration must be in (0, 10 ms]");
+    clock_probe_kernel<<<1, 1, 0, as_stream(stream)>>>(ns, out_mhz);
+    return launch_status("clock_probe");
 }
 
 int bee_b200_stream_synchronize(bee_b200_stream_t stream) {

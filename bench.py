@@ -348,15 +348,26 @@ def run_ours(args, d: Dist):
     d.barrier()
     torch.cuda.synchronize()
     # One sampler (its own process), on rank 0, for rank 0's GPU.
-    # N = 1: periodic sampling (no measurable cost).  N > 1: every NVML query stretches
-    # the step (measured at N = 2: 0.57 ms per step without sampling, 0.71 with the SM
-    # clock read every 2 ms), so the samples are few: a quarter, half and three quarters
-    # of the way through the region.
-    at_s = None if d.world == 1 else [est_region_s * f for f in (0.25, 0.5, 0.75)]
+    # SM clock during the region: N = 1, NVML every 2 ms (no measurable cost).  N > 1:
+    # an NVML query while the GPUs exchange data stretched the step by milliseconds
+    # (N = 2: 0.57 ms per step unsampled, 0.71-3.3 ms sampled), so NVML is read only at
+    # entry and exit (clock and throttle reasons), and the clock during the region comes
+    # from bee_b200_clock_probe kernels on a side stream (clock64 against the global
+    # timer, 0.2 ms each) a quarter, half and three quarters of the way through, on
+    # every rank.
+    at_s = None if d.world == 1 else []
+    probe_at = {args.steps // 4, args.steps // 2, (3 * args.steps) // 4}
+    probe_buf = torch.zeros(len(probe_at), dtype=torch.float32, device=dev)
+    probe_stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
     with ClockSampler(smi_id(dev), period_s=args.clock_period_ms / 1e3, reasons_every=args.clock_reasons_every,
                       enabled=not args.no_clocks and d.rank == 0, at_s=at_s) as clk:
         t0.record(stream)
+        np_i = 0
         for k in range(args.steps):
+            if k in probe_at and not args.no_clocks:
+                call("bee_b200_clock_probe", 200_000, probe_buf[np_i].data_ptr(), probe_stream.cuda_stream)
+                np_i += 1
             step(args.warmup + k, per_step_events[k])
         if comm is not None:
             stream.wait_stream(comm)  # every step's exchange is inside the timed region
@@ -387,6 +398,21 @@ def run_ours(args, d: Dist):
                       [o_add, o_mul, o_bf, o_rsum, o_rmax, o_sm, ring[slot[0]:slot[0] + 1]], [dx, dy, dxi])
 
     clocks = clk.summary()
+    probe_stream.synchronize()
+    probe_mhz = [round(v, 1) for v in probe_buf[:np_i].tolist()] if not args.no_clocks else []
+    if d.world > 1 and probe_mhz:
+        import torch.distributed as dist
+        t = torch.tensor(probe_mhz, dtype=torch.float64, device=dev)
+        lo = t.clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)  # the slowest clock any rank saw at each probe
+        probe_mhz = [round(v, 1) for v in lo.tolist()]
+    if probe_mhz:
+        clocks["probe_mhz_during"] = probe_mhz
+        if d.world > 1:
+            clocks["nvml_mhz_entry_exit"] = clocks.get("sm_mhz")
+            clocks["sm_mhz"] = statistics.median(probe_mhz)
+            clocks["sm_mhz_source"] = ("median of in-kernel probes during the timed region (min over ranks); "
+                                       "throttle reasons from NVML at entry and exit")
     if peer is not None:
         peer.close()
     extra = None if args.no_extras else run_extras(args, d, dev, stream, peaks)

@@ -68,6 +68,11 @@ BEE_B200_API int bee_b200_stream_synchronize(bee_b200_stream_t stream);
  * the stream passed to a call must belong to that device.  These wrap
  * cudaSetDevice / cudaGetDevice / cudaGetDeviceCount for callers that do not
  * link the CUDA runtime themselves (one process per GPU: set it once). */
+/* Measures the SM clock (MHz) of the SM it lands on over `ns` nanoseconds
+ * (<= 10 ms) with one thread, clock64 against the global timer, writing the
+ * result to out_mhz (device memory).  Run on a side stream during a timed
+ * region, it samples the clock under load without an NVML query. */
+BEE_B200_API int bee_b200_clock_probe(unsigned long long ns, float* out_mhz, bee_b200_stream_t stream);
 BEE_B200_API int bee_b200_set_device(int device);
 BEE_B200_API int bee_b200_get_device(int* device);
 BEE_B200_API int bee_b200_device_count(int* count);
