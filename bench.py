@@ -348,24 +348,26 @@ def run_ours(args, d: Dist):
     d.barrier()
     torch.cuda.synchronize()
     # One sampler (its own process), on rank 0, for rank 0's GPU.
-    # SM clock during the region: N = 1, NVML every 2 ms (no measurable cost).  N > 1:
-    # an NVML query while the GPUs exchange data stretched the step by milliseconds
-    # (N = 2: 0.57 ms per step unsampled, 0.71-3.3 ms sampled), so NVML is read only at
-    # entry and exit (clock and throttle reasons), and the clock during the region comes
-    # from bee_b200_clock_probe kernels on a side stream (clock64 against the global
-    # timer, 0.2 ms each) a quarter, half and three quarters of the way through, on
-    # every rank.
-    at_s = None if d.world == 1 else []
+    # SM clock during the region.  N = 1: NVML every 2 ms (no measurable cost) and three
+    # in-kernel probes.  N > 1: NVML in the process stretches the multi-GPU step even with
+    # no query inside the region (N = 2: 0.570 ms per step without NVML, 0.882 ms with
+    # NVML initialised and read just before and after the region, 0.572 ms with the
+    # probes alone), so the clock during the region comes from the probes only
+    # (bee_b200_clock_probe on a side stream: clock64 against the global timer for
+    # 0.2 ms, a quarter, half and three quarters of the way through, on every rank) and
+    # NVML is read once after the region for the throttle reasons.
+    at_s = None
     probe_at = {args.steps // 4, args.steps // 2, (3 * args.steps) // 4}
     probe_buf = torch.zeros(len(probe_at), dtype=torch.float32, device=dev)
     probe_stream = torch.cuda.Stream(device=dev)
     torch.cuda.synchronize()
     with ClockSampler(smi_id(dev), period_s=args.clock_period_ms / 1e3, reasons_every=args.clock_reasons_every,
-                      enabled=not args.no_clocks and d.rank == 0, at_s=at_s) as clk:
+                      enabled=not args.no_clocks and d.rank == 0 and args.clock_source != "probe"
+                      and d.world == 1, at_s=at_s) as clk:
         t0.record(stream)
         np_i = 0
         for k in range(args.steps):
-            if k in probe_at and not args.no_clocks:
+            if k in probe_at and not args.no_clocks and args.clock_source != "nvml":
                 call("bee_b200_clock_probe", 200_000, probe_buf[np_i].data_ptr(), probe_stream.cuda_stream)
                 np_i += 1
             step(args.warmup + k, per_step_events[k])
@@ -408,14 +410,23 @@ def run_ours(args, d: Dist):
         probe_mhz = [round(v, 1) for v in lo.tolist()]
     if probe_mhz:
         clocks["probe_mhz_during"] = probe_mhz
-        if d.world > 1:
-            clocks["nvml_mhz_entry_exit"] = clocks.get("sm_mhz")
-            clocks["sm_mhz"] = statistics.median(probe_mhz)
-            clocks["sm_mhz_source"] = ("median of in-kernel probes during the timed region (min over ranks); "
-                                       "throttle reasons from NVML at entry and exit")
+    if d.world > 1 and not args.no_clocks:
+        clocks = {"sm_mhz": statistics.median(probe_mhz) if probe_mhz else None, "probe_mhz_during": probe_mhz,
+                  "sm_mhz_source": "median of in-kernel probes during the timed region (min over ranks)"}
+        # the NVML read for the throttle reasons waits until every measurement of this run
+        # (extras included) is done: NVML in the process slows multi-GPU steps
     if peer is not None:
         peer.close()
     extra = None if args.no_extras else run_extras(args, d, dev, stream, peaks)
+    if d.world > 1 and not args.no_clocks and d.rank == 0:
+        after = ClockSampler(smi_id(dev), enabled=True)
+        with after:
+            pass  # one NVML read (clock, throttle reasons), after every measurement of the run
+        s_after = after.summary()
+        clocks.update({"sm_max_mhz": s_after.get("sm_max_mhz"), "reasons": s_after.get("reasons", []),
+                       "nvml_after_run": {"sm_mhz": s_after.get("sm_mhz"), "reasons": s_after.get("reasons"),
+                                          "error": s_after.get("error")},
+                       "reasons_source": "NVML read on rank 0's GPU after the run's measurements"})
     out = None
     if d.rank == 0:
         ops_json = {n: {"ms": round(per_op_ms[n], 4), "GB/s": round(OP_BYTES[n] / (per_op_ms[n] / 1e3) / 1e9, 1),
@@ -807,6 +818,8 @@ def main(argv=None):
     ap.add_argument("--clock-period-ms", type=float, default=2.0, help="SM clock sampling period")
     ap.add_argument("--clock-reasons-every", type=int, default=10,
                     help="query the throttle reasons every this many clock samples")
+    ap.add_argument("--clock-source", choices=["both", "nvml", "probe"], default="both",
+                    help="SM clock evidence: NVML samples, in-kernel probes, or both")
     ap.add_argument("--exchange", choices=["nccl", "peer"], default="nccl",
                     help="how the int32 partial sums are combined across GPUs")
     ap.add_argument("--only", default=None,
