@@ -11,7 +11,9 @@
 //   * warp 1 — MMA, ping-pong between the tiles: O_A += P_A(j).V_j,
 //     S_A(j+1) = Q_A.K_{j+1}^T, O_B += P_B(j).V_j, S_B(j+1) = Q_B.K_{j+1}^T,
 //     so the tensor core works on one tile while the other tile's softmax runs;
-//   * warps 2-5 / 6-9 — softmax of tile A / B, one thread per query row: the
+//     warps 2-3 idle; this warpgroup gives most of its registers to the next two
+//     (setmaxnreg);
+//   * warps 4-7 / 8-11 — softmax of tile A / B, one thread per query row: the
 //     thread reads its 128 scores from TMEM, keeps a running max m (log2 units)
 //     and sum l, and writes P = 2^(s*c - m) as bf16 back into TMEM over the
 //     first 64 columns of its own scores; P.V then reads P straight from TMEM
@@ -27,6 +29,8 @@
 // word read by bee_b200_device_status and the CTA abandons its work.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+
+#include <atomic>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -65,6 +69,51 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// Packed fp32 pairs: one instruction computes both lanes of a .f32x2 register pair.
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+__device__ __forceinline__ void unpack_f32x2(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// Maximum of 128 values as a tree of three-input maxima (depth 5 rather than a
+// chain of 127 dependent two-input maxima).
+__device__ __forceinline__ float row_max128(const uint32_t (&s)[128]) {
+    float t[43];
+#pragma unroll
+    for (int i = 0; i < 42; ++i)
+        t[i] = max3(__uint_as_float(s[3 * i]), __uint_as_float(s[3 * i + 1]), __uint_as_float(s[3 * i + 2]));
+    t[42] = fmaxf(__uint_as_float(s[126]), __uint_as_float(s[127]));
+    float u[15];
+#pragma unroll
+    for (int i = 0; i < 14; ++i) u[i] = max3(t[3 * i], t[3 * i + 1], t[3 * i + 2]);
+    u[14] = t[42];
+    float v[5];
+#pragma unroll
+    for (int i = 0; i < 5; ++i) v[i] = max3(u[3 * i], u[3 * i + 1], u[3 * i + 2]);
+    return fmaxf(max3(v[0], v[1], v[2]), fmaxf(v[3], v[4]));
+}
+
 struct AttnParams {
     int seq;          // queries == keys per head (multiple of 128)
     int nkv;          // seq / 128
@@ -72,12 +121,19 @@ struct AttnParams {
     uint16_t* O;      // [heads, seq, 128] bf16
 };
 
-constexpr int kThreads = 320;  // TMA warp, MMA warp, 2 x 4 softmax warps
+constexpr int kThreads = 384;  // warpgroup 0: TMA warp, MMA warp, 2 idle; warpgroups 1-2: softmax
+// Register split.  The launch gives every thread 168 registers (three warps per
+// SM sub-partition, 16384 registers each); warpgroup 0 drops to 56 and the two
+// softmax warpgroups take what it frees, so the total stays what was launched.
+constexpr int kRegsLaunch = 168, kRegsControl = 56, kRegsSoftmax = 224;
+static_assert(kRegsControl * 128 + kRegsSoftmax * 256 <= kRegsLaunch * kThreads,
+              "setmaxnreg split exceeds the registers the block was launched with");
+static_assert(kRegsLaunch * kThreads <= 65536 && kRegsLaunch * 3 * 32 <= 16384, "launch register budget");
 
 __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
-                                                               const __grid_constant__ CUtensorMap tmK,
-                                                               const __grid_constant__ CUtensorMap tmV,
-                                                               const AttnParams p) {
+                                                                         const __grid_constant__ CUtensorMap tmK,
+                                                                         const __grid_constant__ CUtensorMap tmV,
+                                                                         const AttnParams p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t q_full;
     __shared__ __align__(8) uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
@@ -123,106 +179,111 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
     tc_fence_after();
     const uint32_t tmem = tmem_base_sh;
 
-    if (warp == 0) {
-        // ------------------------------------------------ TMA producer
-        if (lane == 0) {
-            mbar_arrive_expect_tx(&q_full, ntiles * kTile);
-            for (int t = 0; t < ntiles; ++t) {
-                tma_load_3d(sQ + t * kTile, &tmQ, &q_full, 0, q0 + t * kBlock, head);
-                tma_load_3d(sQ + t * kTile + kHalf, &tmQ, &q_full, 64, q0 + t * kBlock, head);
-            }
-            int k_issued = 0, v_issued = 0;
-            for (int j = 0; j < nkv; ++j) {
-                const int s = j & 1;
-                const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
-                if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag, status, 21)) break;
-                mbar_arrive_expect_tx(&k_full[s], kTile);
-                tma_load_3d(sK + s * kTile, &tmK, &k_full[s], 0, j * kBlock, head);
-                tma_load_3d(sK + s * kTile + kHalf, &tmK, &k_full[s], 64, j * kBlock, head);
-                k_issued = j + 1;
-                if (!mbar_wait(&v_empty[s], ph ^ 1u, abort_flag, status, 22)) break;
-                mbar_arrive_expect_tx(&v_full[s], kTile);
-                tma_load_3d(sV + s * kTile, &tmV, &v_full[s], 0, j * kBlock, head);
-                tma_load_3d(sV + s * kTile + kHalf, &tmV, &v_full[s], 64, j * kBlock, head);
-                v_issued = j + 1;
-            }
-            // the last loads of each ring must have landed before the CTA may exit
-            // (normally the MMA warp consumed them already)
-            mbar_wait(&q_full, 0, abort_flag, status, 33, 200000000ull);
-            for (int j = k_issued > 2 ? k_issued - 2 : 0; j < k_issued; ++j)
-                mbar_wait(&k_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, status, 34, 200000000ull);
-            for (int j = v_issued > 2 ? v_issued - 2 : 0; j < v_issued; ++j)
-                mbar_wait(&v_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, status, 35, 200000000ull);
-        }
-        __syncwarp();
-    } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false);  // B = K rows, K-major
-            constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, true);   // B = V, MN-major
-            bool ok = mbar_wait(&q_full, 0, abort_flag, status, 23);
-            bool issued = false;
-            // S_t = Q_t . K_j^T into TMEM columns t * 128
-            auto issue_s = [&](int t, int j) {
-                const uint32_t q_base = smem_u32(sQ + t * kTile);
-                const uint32_t k_base = smem_u32(sK + (j & 1) * kTile);
-#pragma unroll
-                for (int k = 0; k < kHead / 16; ++k) {
-                    const uint32_t off = (k / 4) * kHalf + (k % 4) * 32;
-                    mma_f16_ss(tmem + static_cast<uint32_t>(t * 128), sdesc_sw128(q_base + off, 16, 1024),
-                               sdesc_sw128(k_base + off, 16, 1024), idesc_s, k != 0 ? 1u : 0u);
+    if (warp < 4) {
+        // warpgroup 0 needs few registers: hand them to the softmax warpgroups
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegsControl) : "memory");
+        if (warp == 0) {
+            // ------------------------------------------------ TMA producer
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&q_full, ntiles * kTile);
+                for (int t = 0; t < ntiles; ++t) {
+                    tma_load_3d(sQ + t * kTile, &tmQ, &q_full, 0, q0 + t * kBlock, head);
+                    tma_load_3d(sQ + t * kTile + kHalf, &tmQ, &q_full, 64, q0 + t * kBlock, head);
                 }
-                mma_commit(&s_full[t]);
-                issued = true;
-            };
-            // O_t += P_t . V_j, P_t in TMEM columns t * 128 .. + 63 (bf16 pairs)
-            auto issue_o = [&](int t, int j) {
-                const uint32_t v_base = smem_u32(sV + (j & 1) * kTile);
-#pragma unroll
-                for (int k = 0; k < kBlock / 16; ++k)
-                    mma_f16_ts(tmem + 256u + static_cast<uint32_t>(t * 128), tmem + static_cast<uint32_t>(t * 128 + k * 8),
-                               sdesc_sw128(v_base + k * 16 * 128, kHalf, 1024), idesc_o, (j | k) != 0 ? 1u : 0u);
-                issued = true;
-            };
-            if (ok && nkv > 0) {
-                ok = mbar_wait(&k_full[0], 0, abort_flag, status, 24);
-                if (ok) {
-                    tc_fence_after();
-                    for (int t = 0; t < ntiles; ++t) issue_s(t, 0);
-                    mma_commit(&k_empty[0]);
+                int k_issued = 0, v_issued = 0;
+                for (int j = 0; j < nkv; ++j) {
+                    const int s = j & 1;
+                    const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
+                    if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag, status, 21)) break;
+                    mbar_arrive_expect_tx(&k_full[s], kTile);
+                    tma_load_3d(sK + s * kTile, &tmK, &k_full[s], 0, j * kBlock, head);
+                    tma_load_3d(sK + s * kTile + kHalf, &tmK, &k_full[s], 64, j * kBlock, head);
+                    k_issued = j + 1;
+                    if (!mbar_wait(&v_empty[s], ph ^ 1u, abort_flag, status, 22)) break;
+                    mbar_arrive_expect_tx(&v_full[s], kTile);
+                    tma_load_3d(sV + s * kTile, &tmV, &v_full[s], 0, j * kBlock, head);
+                    tma_load_3d(sV + s * kTile + kHalf, &tmV, &v_full[s], 64, j * kBlock, head);
+                    v_issued = j + 1;
                 }
+                // the last loads of each ring must have landed before the CTA may exit
+                // (normally the MMA warp consumed them already)
+                mbar_wait(&q_full, 0, abort_flag, status, 33, 200000000ull);
+                for (int j = k_issued > 2 ? k_issued - 2 : 0; j < k_issued; ++j)
+                    mbar_wait(&k_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, status, 34, 200000000ull);
+                for (int j = v_issued > 2 ? v_issued - 2 : 0; j < v_issued; ++j)
+                    mbar_wait(&v_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, status, 35, 200000000ull);
             }
-            for (int j = 0; ok && j < nkv; ++j) {
-                const int s = j & 1;
-                const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
-                const bool next = j + 1 < nkv;
-                const int s1 = (j + 1) & 1;
-                const uint32_t ph1 = static_cast<uint32_t>(((j + 1) >> 1) & 1);
-                for (int t = 0; ok && t < ntiles; ++t) {
-                    ok = mbar_wait(&p_full[t], static_cast<uint32_t>(j & 1), abort_flag, status, 26);
-                    if (ok && t == 0) ok = mbar_wait(&v_full[s], ph, abort_flag, status, 27);
-                    if (!ok) break;
-                    tc_fence_after();
-                    issue_o(t, j);
-                    if (t == ntiles - 1) mma_commit(&v_empty[s]);
-                    if (next) {
-                        if (t == 0) ok = mbar_wait(&k_full[s1], ph1, abort_flag, status, 24);
-                        if (!ok) break;
+            __syncwarp();
+        } else if (warp == 1) {
+            // ------------------------------------------------ MMA issuer
+            if (lane == 0) {
+                constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false);  // B = K rows, K-major
+                constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, true);   // B = V, MN-major
+                bool ok = mbar_wait(&q_full, 0, abort_flag, status, 23);
+                bool issued = false;
+                // S_t = Q_t . K_j^T into TMEM columns t * 128
+                auto issue_s = [&](int t, int j) {
+                    const uint32_t q_base = smem_u32(sQ + t * kTile);
+                    const uint32_t k_base = smem_u32(sK + (j & 1) * kTile);
+#pragma unroll
+                    for (int k = 0; k < kHead / 16; ++k) {
+                        const uint32_t off = (k / 4) * kHalf + (k % 4) * 32;
+                        mma_f16_ss(tmem + static_cast<uint32_t>(t * 128), sdesc_sw128(q_base + off, 16, 1024),
+                                   sdesc_sw128(k_base + off, 16, 1024), idesc_s, k != 0 ? 1u : 0u);
+                    }
+                    mma_commit(&s_full[t]);
+                    issued = true;
+                };
+                // O_t += P_t . V_j, P_t in TMEM columns t * 128 .. + 63 (bf16 pairs)
+                auto issue_o = [&](int t, int j) {
+                    const uint32_t v_base = smem_u32(sV + (j & 1) * kTile);
+#pragma unroll
+                    for (int k = 0; k < kBlock / 16; ++k)
+                        mma_f16_ts(tmem + 256u + static_cast<uint32_t>(t * 128), tmem + static_cast<uint32_t>(t * 128 + k * 8),
+                                   sdesc_sw128(v_base + k * 16 * 128, kHalf, 1024), idesc_o, (j | k) != 0 ? 1u : 0u);
+                    issued = true;
+                };
+                if (ok && nkv > 0) {
+                    ok = mbar_wait(&k_full[0], 0, abort_flag, status, 24);
+                    if (ok) {
                         tc_fence_after();
-                        issue_s(t, j + 1);
-                        if (t == ntiles - 1) mma_commit(&k_empty[s1]);
+                        for (int t = 0; t < ntiles; ++t) issue_s(t, 0);
+                        mma_commit(&k_empty[0]);
                     }
                 }
+                for (int j = 0; ok && j < nkv; ++j) {
+                    const int s = j & 1;
+                    const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
+                    const bool next = j + 1 < nkv;
+                    const int s1 = (j + 1) & 1;
+                    const uint32_t ph1 = static_cast<uint32_t>(((j + 1) >> 1) & 1);
+                    for (int t = 0; ok && t < ntiles; ++t) {
+                        ok = mbar_wait(&p_full[t], static_cast<uint32_t>(j & 1), abort_flag, status, 26);
+                        if (ok && t == 0) ok = mbar_wait(&v_full[s], ph, abort_flag, status, 27);
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue_o(t, j);
+                        if (t == ntiles - 1) mma_commit(&v_empty[s]);
+                        if (next) {
+                            if (t == 0) ok = mbar_wait(&k_full[s1], ph1, abort_flag, status, 24);
+                            if (!ok) break;
+                            tc_fence_after();
+                            issue_s(t, j + 1);
+                            if (t == ntiles - 1) mma_commit(&k_empty[s1]);
+                        }
+                    }
+                }
+                if (issued) {
+                    mma_commit(&done_bar);
+                    mbar_wait(&done_bar, 0, abort_flag, status, 28, 200000000ull);
+                }
             }
-            if (issued) {
-                mma_commit(&done_bar);
-                mbar_wait(&done_bar, 0, abort_flag, status, 28, 200000000ull);
-            }
+            __syncwarp();
         }
-        __syncwarp();
     } else {
-        // ------------------------------------------------ softmax / epilogue (warps 2-9)
-        const int t = (warp - 2) >> 2;          // tile A (warps 2-5) or B (warps 6-9)
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegsSoftmax) : "memory");
+        // ------------------------------------------------ softmax / epilogue (warps 4-11)
+        const int t = (warp - 4) >> 2;          // tile A (warps 4-7) or B (warps 8-11)
         const int q = warp & 3;                 // TMEM lane quarter
         const int row = q * 32 + lane;          // query row within the tile
         const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
@@ -238,19 +299,18 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
                 break;
             }
             tc_fence_after();
-            float sc[128];
+            // all four 32-column loads in flight before one wait
+            uint32_t sc[128];
+            tmem_ld_32x32b_x32(s_col + 0u, *reinterpret_cast<uint32_t(*)[32]>(&sc[0]));
+            tmem_ld_32x32b_x32(s_col + 32u, *reinterpret_cast<uint32_t(*)[32]>(&sc[32]));
+            tmem_ld_32x32b_x32(s_col + 64u, *reinterpret_cast<uint32_t(*)[32]>(&sc[64]));
+            tmem_ld_32x32b_x32(s_col + 96u, *reinterpret_cast<uint32_t(*)[32]>(&sc[96]));
+            tmem_ld_wait();
+            // the loaded registers are defined only after the wait: route them
+            // through it so no use is scheduled ahead of it
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(s_col + static_cast<uint32_t>(cc * 32), r);
-                tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) sc[cc * 32 + i] = __uint_as_float(r[i]);
-            }
-            float mx = sc[0];
-#pragma unroll
-            for (int i = 1; i < 128; ++i) mx = fmaxf(mx, sc[i]);
-            mx *= c;  // scale > 0: the max of the scaled scores
+            for (int i = 0; i < 128; ++i) asm volatile("" : "+r"(sc[i]));
+            float mx = row_max128(sc) * c;  // scale > 0: the max of the scaled scores
             if (j == 0) {
                 m = mx;
             } else if (__any_sync(0xffffffffu, mx > m + kRescaleThreshold)) {
@@ -270,16 +330,21 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
                 l *= alpha;
                 m = m_new;
             }
-            // P = 2^(s*c - m) as bf16 pairs over the first 64 score columns
-            float rs = 0.f;
+            // P = 2^(s*c - m) as bf16 pairs over the first 64 score columns; the
+            // arguments and the row sum in packed pairs, the sum in four
+            // independent accumulators
+            const uint64_t c2 = pack_f32x2(c, c), nm2 = pack_f32x2(-m, -m);
+            uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 uint32_t w[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                    const float e0 = ex2(fmaf(sc[h * 64 + 2 * i], c, -m));
-                    const float e1 = ex2(fmaf(sc[h * 64 + 2 * i + 1], c, -m));
-                    rs += e0 + e1;
+                    const int k = h * 64 + 2 * i;
+                    float x0, x1;
+                    unpack_f32x2(fma_f32x2(pack_f32x2(__uint_as_float(sc[k]), __uint_as_float(sc[k + 1])), c2, nm2), x0, x1);
+                    const float e0 = ex2(x0), e1 = ex2(x1);
+                    acc[i & 3] = add_f32x2(acc[i & 3], pack_f32x2(e0, e1));
                     w[i] = pack_bf16x2(e0, e1);
                 }
                 tmem_st_32x32b_x32(s_col + static_cast<uint32_t>(h * 32), w);
@@ -288,7 +353,12 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[t]);
-            l += rs;
+            float a0, a1, a2, a3, a4, a5, a6, a7;
+            unpack_f32x2(acc[0], a0, a1);
+            unpack_f32x2(acc[1], a2, a3);
+            unpack_f32x2(acc[2], a4, a5);
+            unpack_f32x2(acc[3], a6, a7);
+            l += ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7));
         }
         // epilogue: O / l -> bf16, the thread's whole row
         if (ok && nkv > 0) {
@@ -384,13 +454,22 @@ extern "C" int bee_b200_attention(int dt, const void* q, const void* k, const vo
     p.nkv = static_cast<int>(seq / kBlock);
     p.scale_log2 = scale * 1.4426950408889634f;
     p.O = static_cast<uint16_t*>(o);
-    static bool attr_set[64] = {false};
+    static std::atomic<bool> ready[64];
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(attention_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return fail(cudaErrorInvalidDevice, "attention: no usable current device");
+    if (!ready[dev].load(std::memory_order_acquire)) {
+        // setmaxnreg.inc waits until the registers it asks for are free, so the
+        // split is only safe when the kernel launches with exactly kRegsLaunch
+        cudaFuncAttributes fa;
+        cudaError_t e = cudaFuncGetAttributes(&fa, attention_fwd_kernel);
+        if (e != cudaSuccess) return fail(static_cast<int>(e), "attention: kernel attributes: %s", cudaGetErrorString(e));
+        if (fa.numRegs != kRegsLaunch)
+            return fail(cudaErrorLaunchOutOfResources, "attention: kernel built with %d registers per thread, the "
+                        "register split assumes %d", fa.numRegs, kRegsLaunch);
+        e = cudaFuncSetAttribute(attention_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
         if (e != cudaSuccess) return fail(static_cast<int>(e), "attention: shared memory attribute: %s", cudaGetErrorString(e));
-        attr_set[dev] = true;
+        ready[dev].store(true, std::memory_order_release);
     }
     dim3 grid(static_cast<unsigned>((seq / kBlock + 1) / 2), static_cast<unsigned>(heads));
     attention_fwd_kernel<<<grid, kThreads, kSmem, as_stream(stream)>>>(tq, tk, tv, p);
