@@ -462,7 +462,10 @@ def run_ours(args, d: Dist):
 
 def run_extras(args, d, dev, stream, peaks):
     """The other configs of the path, each timed on its own (CUDA events on the
-    launching stream, max over ranks) after the headline sweep:
+    launching stream, max over ranks) after the headline sweep, the memory-bound ones
+    first: after the 8192^3 GEMMs, which run at the 1000 W power cap, the SM clock
+    stays low for longer than a warm-up (each config reports the SM clock an
+    in-kernel probe saw during its timed region, ``sm_mhz_probe``):
 
     * gemm_bf16_8192: C = A.B, M = N = K = 8192, bf16 in, fp32 accumulate, bf16 out;
       B sharded by output columns (each GPU owns an [8192, 8192] column block of a
@@ -492,18 +495,42 @@ def run_extras(args, d, dev, stream, peaks):
     g = torch.Generator(device=dev).manual_seed(4321 + d.rank)
     out = {}
 
-    def timed(fn):
-        for _ in range(warm):
+    probe_buf = torch.zeros(1, dtype=torch.float32, device=dev)
+    probe_stream = torch.cuda.Stream(device=dev)
+    probe_log = {}
+
+    def timed(fn, label=None):
+        """ms per call of fn.  Warm-up: at least `warm` calls and about 30 ms of work, so
+        that the SM clock has recovered from the previous config (the 8192^3 GEMMs run at
+        the 1000 W power cap); the timed region: at least `steps` calls and about 10 ms.
+        Call counts come from the slowest rank's estimate, so every rank makes the same
+        calls (fn may hold collectives).  With a label, one in-kernel clock probe
+        (0.2 ms on a side stream) runs mid-region and its SM MHz is reported."""
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        stream.synchronize()
+        est = max(d.max(e0.elapsed_time(e1)), 1e-3)
+        n_warm = max(warm, min(int(30.0 / est), 2000))
+        n_time = max(steps, min(int(10.0 / est), 2000))
+        for _ in range(n_warm):
             fn()
         d.barrier()
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(steps):
+        for i in range(n_time):
+            if label is not None and i == n_time // 2 and not args.no_clocks:
+                call("bee_b200_clock_probe", 200_000, probe_buf.data_ptr(), probe_stream.cuda_stream)
             fn()
         e1.record(stream)
         stream.synchronize()
-        return d.max(e0.elapsed_time(e1)) / steps
+        if label is not None and not args.no_clocks:
+            probe_stream.synchronize()
+            probe_log[label] = round(float(probe_buf.item()), 1)
+        return d.max(e0.elapsed_time(e1)) / n_time
 
     def status_ok():
         import ctypes
@@ -512,6 +539,109 @@ def run_extras(args, d, dev, stream, peaks):
         return c.value == 0
 
     with torch.cuda.stream(stream):
+        if want("rms_norm_rope_bf16"):
+            rows, cols, seq, heads, hd = 16 * 2048, 4096, 2048, 32, 128
+            x = torch.randn(rows, cols, device=dev, generator=g).to(torch.bfloat16)
+            w = (1 + 0.02 * torch.randn(cols, device=dev, generator=g)).to(torch.bfloat16)
+            y = torch.empty_like(x)
+            ms = timed(lambda: call("bee_b200_rms_norm_rope", _capi.BF16, x.data_ptr(), w.data_ptr(), y.data_ptr(), rows,
+                                    seq, heads, hd, 1e-6, 10000.0, 0, st), label="rms_norm_rope_bf16")
+            nbytes = 2 * rows * cols * 2 + cols * 2
+            gbs = d.world * nbytes / (ms / 1e3) / 1e9
+            out["rms_norm_rope_bf16"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                         "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                         "bytes_per_gpu": nbytes, "scaling": "weak (rows sharded)"}
+            del x, w, y
+        if want("gemm_f32_1024"):
+            a32 = torch.rand(1024, 1024, device=dev, generator=g) * 2 - 1
+            b32 = torch.rand(1024, 1024, device=dev, generator=g) * 2 - 1
+            c32 = torch.empty_like(a32)
+            ms = timed(lambda: call("bee_b200_matmul", _capi.F32, a32.data_ptr(), b32.data_ptr(), c32.data_ptr(), 1024,
+                                    1024, 1024, st), label="gemm_f32_1024")
+            out["gemm_f32_1024"] = {"ms": round(ms, 4), "TFLOP/s": round(2.0 * 1024 ** 3 / (ms / 1e3) / 1e12, 2),
+                                    "unit": "TFLOP/s (per GPU)", "path": "SIMT fp32 (parity config, rel tol 1e-4)"}
+            del a32, b32, c32
+        if want("transpose_f32_8192", "bcast_sub_rowmax_f32_8192", "sum_dim0_f32_8192", "contiguous_kt_bf16"):
+            # layout and broadcast ops on the [8192, 8192] fp32 shard (HBM-bound, 2 x 256 MiB moved)
+            import ctypes
+            x = torch.randn(8192, 8192, device=dev, generator=g)
+            y = torch.empty_like(x)
+            ms = timed(lambda: call("bee_b200_transpose_2d", _capi.F32, x.data_ptr(), y.data_ptr(), 8192, 8192, st),
+                       label="transpose_f32_8192")
+            nbytes = 2 * 8192 * 8192 * 4
+            gbs = d.world * nbytes / (ms / 1e3) / 1e9
+            out["transpose_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                         "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                         "bytes_per_gpu": nbytes, "scaling": "weak"}
+            rmax = torch.empty(8192, device=dev)
+            call("bee_b200_reduce_axis", _capi.MAX, _capi.F32, x.data_ptr(), rmax.data_ptr(), 8192, 8192, 1, st)
+            shp = (ctypes.c_int64 * 2)(8192, 8192)
+            sa = (ctypes.c_int64 * 2)(8192, 1)
+            sb = (ctypes.c_int64 * 2)(1, 0)
+            ms = timed(lambda: call("bee_b200_ew_binary_strided", _capi.SUB, _capi.F32, 2, shp, x.data_ptr(), sa,
+                                    rmax.data_ptr(), sb, y.data_ptr(), st), label="bcast_sub_rowmax_f32_8192")
+            nbytes = 2 * 8192 * 8192 * 4 + 8192 * 4
+            gbs = d.world * nbytes / (ms / 1e3) / 1e9
+            out["bcast_sub_rowmax_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                                "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                                "op": "x[8192, 8192] - rowmax[8192, 1] (broadcast, stride 0)",
+                                                "bytes_per_gpu": nbytes, "scaling": "weak"}
+            colsum = torch.empty(8192, device=dev)
+            ms = timed(lambda: call("bee_b200_reduce_axis", _capi.SUM, _capi.F32, x.data_ptr(), colsum.data_ptr(), 1, 8192,
+                                    8192, st), label="sum_dim0_f32_8192")
+            nbytes = 8192 * 8192 * 4 + 8192 * 4
+            gbs = d.world * nbytes / (ms / 1e3) / 1e9
+            out["sum_dim0_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                        "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                        "op": "sum(x, 0) of [8192, 8192] fp32 (column reduce, axis split over CTAs)",
+                                        "bytes_per_gpu": nbytes, "scaling": "weak"}
+            del colsum
+            kq = torch.randn(256, 2048, 128, device=dev, generator=g).to(torch.bfloat16)
+            kt = torch.empty(256, 128, 2048, device=dev, dtype=torch.bfloat16)
+            vsh = (ctypes.c_int64 * 3)(256, 128, 2048)
+            vst = (ctypes.c_int64 * 3)(2048 * 128, 1, 128)
+            ms = timed(lambda: call("bee_b200_strided_copy", _capi.BF16, kq.data_ptr(), 3, vsh, vst, kt.data_ptr(), st),
+                       label="contiguous_kt_bf16")
+            nbytes = 2 * 256 * 2048 * 128 * 2
+            gbs = d.world * nbytes / (ms / 1e3) / 1e9
+            out["contiguous_kt_bf16"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
+                                         "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
+                                         "op": "contiguous() of K^T, K [256, 2048, 128] bf16 (128 MiB each way)",
+                                         "bytes_per_gpu": nbytes, "scaling": "weak"}
+            del x, y, rmax, kq, kt
+
+        if want("attention_bf16"):
+            h, s_, dh = 32, 2048, 128
+            q = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
+            k = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
+            v = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
+            S = torch.empty(h, s_, s_, device=dev, dtype=torch.float32)
+            P = torch.empty(h, s_, s_, device=dev, dtype=torch.bfloat16)
+            o = torch.empty(h, s_, dh, device=dev, dtype=torch.bfloat16)
+            scale = 1.0 / np.sqrt(dh)
+
+            def attention_chain():
+                call("bee_b200_bmm", _capi.BF16, _capi.F32, q.data_ptr(), k.data_ptr(), S.data_ptr(), h, s_, dh, s_, 1,
+                     scale, st)
+                call("bee_b200_softmax_rows_to", _capi.F32, S.data_ptr(), _capi.BF16, P.data_ptr(), h * s_, s_, st)
+                call("bee_b200_bmm", _capi.BF16, _capi.BF16, P.data_ptr(), v.data_ptr(), o.data_ptr(), h, s_, s_, dh, 0,
+                     1.0, st)
+
+            def attention_fused():
+                call("bee_b200_attention", _capi.BF16, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), h, s_, dh,
+                     scale, st)
+            aflop = 2.0 * 2 * h * s_ * s_ * dh
+            ms = timed(attention_fused, label="attention_bf16")
+            tf = d.world * aflop / (ms / 1e3) / 1e12
+            ms_c = timed(attention_chain)
+            tf_c = d.world * aflop / (ms_c / 1e3) / 1e12
+            out["attention_bf16"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
+                                     "frac_of_measured_bf16_burst": round(tf / d.world / peaks["bf16_tflops"], 3),
+                                     "kernels": "fused (scores and probabilities stay on chip)",
+                                     "unfused_chain": {"ms": round(ms_c, 4), "TFLOP/s": round(tf_c, 1),
+                                                       "kernels": "bmm (QK^T, fp32 out) -> softmax fp32->bf16 -> bmm (PV)"},
+                                     "scaling": "weak (heads sharded)", "status_ok": status_ok()}
+            del q, k, v, S, P, o
         if want("gemm_bf16_8192", "gemm_bf16_8192_splitk"):
             n = 8192
             std = (1.0 / np.sqrt(n)) ** 0.5  # N(0, variance 1/sqrt(8192))
@@ -520,7 +650,7 @@ def run_extras(args, d, dev, stream, peaks):
             c = torch.empty(n, n, device=dev, dtype=torch.bfloat16)
             flop = 2.0 * n ** 3
             ms = timed(lambda: call("bee_b200_bmm", _capi.BF16, _capi.BF16, a.data_ptr(), b.data_ptr(), c.data_ptr(),
-                                    1, n, n, n, 0, 1.0, st))
+                                    1, n, n, n, 0, 1.0, st), label="gemm_bf16_8192")
             tf = d.world * flop / (ms / 1e3) / 1e12
             out["gemm_bf16_8192"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
                                      "frac_of_measured_bf16_burst": round(tf / d.world / peaks["bf16_tflops"], 3),
@@ -549,7 +679,7 @@ def run_extras(args, d, dev, stream, peaks):
             fused = SplitKGemm(n, n, dev, group=d.pg)
             a_ptr = a.data_ptr() + 2 * klo
             b_ptr = b[klo:khi].data_ptr()
-            ms = timed(lambda: fused(a_ptr, n, b_ptr, kr, st))
+            ms = timed(lambda: fused(a_ptr, n, b_ptr, kr, st), label="gemm_bf16_8192_splitk")
             ok_fused = status_ok()
             fused.close()
             tf = flop / (ms / 1e3) / 1e12
@@ -566,107 +696,6 @@ def run_extras(args, d, dev, stream, peaks):
                                          "kernels": "bmm fp32 out -> NCCL all-reduce (fp32) -> cast",
                                          "allreduce_bytes_per_gpu": n * n * 4 if d.world > 1 else 0}}
             del a, b, c
-        if want("rms_norm_rope_bf16"):
-            rows, cols, seq, heads, hd = 16 * 2048, 4096, 2048, 32, 128
-            x = torch.randn(rows, cols, device=dev, generator=g).to(torch.bfloat16)
-            w = (1 + 0.02 * torch.randn(cols, device=dev, generator=g)).to(torch.bfloat16)
-            y = torch.empty_like(x)
-            ms = timed(lambda: call("bee_b200_rms_norm_rope", _capi.BF16, x.data_ptr(), w.data_ptr(), y.data_ptr(), rows,
-                                    seq, heads, hd, 1e-6, 10000.0, 0, st))
-            nbytes = 2 * rows * cols * 2 + cols * 2
-            gbs = d.world * nbytes / (ms / 1e3) / 1e9
-            out["rms_norm_rope_bf16"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
-                                         "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
-                                         "bytes_per_gpu": nbytes, "scaling": "weak (rows sharded)"}
-            del x, w, y
-        if want("attention_bf16"):
-            h, s_, dh = 32, 2048, 128
-            q = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
-            k = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
-            v = torch.randn(h, s_, dh, device=dev, generator=g).to(torch.bfloat16)
-            S = torch.empty(h, s_, s_, device=dev, dtype=torch.float32)
-            P = torch.empty(h, s_, s_, device=dev, dtype=torch.bfloat16)
-            o = torch.empty(h, s_, dh, device=dev, dtype=torch.bfloat16)
-            scale = 1.0 / np.sqrt(dh)
-
-            def attention_chain():
-                call("bee_b200_bmm", _capi.BF16, _capi.F32, q.data_ptr(), k.data_ptr(), S.data_ptr(), h, s_, dh, s_, 1,
-                     scale, st)
-                call("bee_b200_softmax_rows_to", _capi.F32, S.data_ptr(), _capi.BF16, P.data_ptr(), h * s_, s_, st)
-                call("bee_b200_bmm", _capi.BF16, _capi.BF16, P.data_ptr(), v.data_ptr(), o.data_ptr(), h, s_, s_, dh, 0,
-                     1.0, st)
-
-            def attention_fused():
-                call("bee_b200_attention", _capi.BF16, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), h, s_, dh,
-                     scale, st)
-            aflop = 2.0 * 2 * h * s_ * s_ * dh
-            ms = timed(attention_fused)
-            tf = d.world * aflop / (ms / 1e3) / 1e12
-            ms_c = timed(attention_chain)
-            tf_c = d.world * aflop / (ms_c / 1e3) / 1e12
-            out["attention_bf16"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "unit": "TFLOP/s",
-                                     "frac_of_measured_bf16_burst": round(tf / d.world / peaks["bf16_tflops"], 3),
-                                     "kernels": "fused (scores and probabilities stay on chip)",
-                                     "unfused_chain": {"ms": round(ms_c, 4), "TFLOP/s": round(tf_c, 1),
-                                                       "kernels": "bmm (QK^T, fp32 out) -> softmax fp32->bf16 -> bmm (PV)"},
-                                     "scaling": "weak (heads sharded)", "status_ok": status_ok()}
-            del q, k, v, S, P, o
-        if want("gemm_f32_1024"):
-            a32 = torch.rand(1024, 1024, device=dev, generator=g) * 2 - 1
-            b32 = torch.rand(1024, 1024, device=dev, generator=g) * 2 - 1
-            c32 = torch.empty_like(a32)
-            ms = timed(lambda: call("bee_b200_matmul", _capi.F32, a32.data_ptr(), b32.data_ptr(), c32.data_ptr(), 1024,
-                                    1024, 1024, st))
-            out["gemm_f32_1024"] = {"ms": round(ms, 4), "TFLOP/s": round(2.0 * 1024 ** 3 / (ms / 1e3) / 1e12, 2),
-                                    "unit": "TFLOP/s (per GPU)", "path": "SIMT fp32 (parity config, rel tol 1e-4)"}
-            del a32, b32, c32
-        if want("transpose_f32_8192", "bcast_sub_rowmax_f32_8192", "sum_dim0_f32_8192", "contiguous_kt_bf16"):
-            # layout and broadcast ops on the [8192, 8192] fp32 shard (HBM-bound, 2 x 256 MiB moved)
-            import ctypes
-            x = torch.randn(8192, 8192, device=dev, generator=g)
-            y = torch.empty_like(x)
-            ms = timed(lambda: call("bee_b200_transpose_2d", _capi.F32, x.data_ptr(), y.data_ptr(), 8192, 8192, st))
-            nbytes = 2 * 8192 * 8192 * 4
-            gbs = d.world * nbytes / (ms / 1e3) / 1e9
-            out["transpose_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
-                                         "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
-                                         "bytes_per_gpu": nbytes, "scaling": "weak"}
-            rmax = torch.empty(8192, device=dev)
-            call("bee_b200_reduce_axis", _capi.MAX, _capi.F32, x.data_ptr(), rmax.data_ptr(), 8192, 8192, 1, st)
-            shp = (ctypes.c_int64 * 2)(8192, 8192)
-            sa = (ctypes.c_int64 * 2)(8192, 1)
-            sb = (ctypes.c_int64 * 2)(1, 0)
-            ms = timed(lambda: call("bee_b200_ew_binary_strided", _capi.SUB, _capi.F32, 2, shp, x.data_ptr(), sa,
-                                    rmax.data_ptr(), sb, y.data_ptr(), st))
-            nbytes = 2 * 8192 * 8192 * 4 + 8192 * 4
-            gbs = d.world * nbytes / (ms / 1e3) / 1e9
-            out["bcast_sub_rowmax_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
-                                                "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
-                                                "op": "x[8192, 8192] - rowmax[8192, 1] (broadcast, stride 0)",
-                                                "bytes_per_gpu": nbytes, "scaling": "weak"}
-            colsum = torch.empty(8192, device=dev)
-            ms = timed(lambda: call("bee_b200_reduce_axis", _capi.SUM, _capi.F32, x.data_ptr(), colsum.data_ptr(), 1, 8192,
-                                    8192, st))
-            nbytes = 8192 * 8192 * 4 + 8192 * 4
-            gbs = d.world * nbytes / (ms / 1e3) / 1e9
-            out["sum_dim0_f32_8192"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
-                                        "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
-                                        "op": "sum(x, 0) of [8192, 8192] fp32 (column reduce, axis split over CTAs)",
-                                        "bytes_per_gpu": nbytes, "scaling": "weak"}
-            del colsum
-            kq = torch.randn(256, 2048, 128, device=dev, generator=g).to(torch.bfloat16)
-            kt = torch.empty(256, 128, 2048, device=dev, dtype=torch.bfloat16)
-            vsh = (ctypes.c_int64 * 3)(256, 128, 2048)
-            vst = (ctypes.c_int64 * 3)(2048 * 128, 1, 128)
-            ms = timed(lambda: call("bee_b200_strided_copy", _capi.BF16, kq.data_ptr(), 3, vsh, vst, kt.data_ptr(), st))
-            nbytes = 2 * 256 * 2048 * 128 * 2
-            gbs = d.world * nbytes / (ms / 1e3) / 1e9
-            out["contiguous_kt_bf16"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "unit": "GB/s",
-                                         "frac_of_hbm": round(gbs / d.world / peaks["hbm_gbs"], 3),
-                                         "op": "contiguous() of K^T, K [256, 2048, 128] bf16 (128 MiB each way)",
-                                         "bytes_per_gpu": nbytes, "scaling": "weak"}
-            del x, y, rmax, kq, kt
-
         if want("bridge_matmul") and d.world == 1:
             # plumbing cost around a matmul through the C++ bridge (bee_b200/host/bridge_bench.cpp),
             # on the same GPU (the child inherits the device selection)
@@ -683,6 +712,9 @@ def run_extras(args, d, dev, stream, peaks):
                 else:
                     out["bridge_matmul"] = {"error": (r.stderr or r.stdout)[-300:]}
     stream.synchronize()
+    for label, mhz in probe_log.items():
+        if isinstance(out.get(label), dict):
+            out[label]["sm_mhz_probe"] = mhz
     return out
 
 
