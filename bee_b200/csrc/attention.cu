@@ -30,8 +30,6 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
-#include <atomic>
-
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -454,23 +452,22 @@ extern "C" int bee_b200_attention(int dt, const void* q, const void* k, const vo
     p.nkv = static_cast<int>(seq / kBlock);
     p.scale_log2 = scale * 1.4426950408889634f;
     p.O = static_cast<uint16_t*>(o);
-    static std::atomic<bool> ready[64];
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
-        return fail(cudaErrorInvalidDevice, "attention: no usable current device");
-    if (!ready[dev].load(std::memory_order_acquire)) {
-        // setmaxnreg.inc waits until the registers it asks for are free, so the
-        // split is only safe when the kernel launches with exactly kRegsLaunch
+    // setmaxnreg.inc waits until the registers it asks for are free, so the
+    // split is only safe when the kernel launches with exactly kRegsLaunch
+    static std::atomic<int> launch_regs{0};
+    int regs = launch_regs.load(std::memory_order_acquire);
+    if (regs == 0) {
         cudaFuncAttributes fa;
         cudaError_t e = cudaFuncGetAttributes(&fa, attention_fwd_kernel);
-        if (e != cudaSuccess) return fail(static_cast<int>(e), "attention: kernel attributes: %s", cudaGetErrorString(e));
-        if (fa.numRegs != kRegsLaunch)
-            return fail(cudaErrorLaunchOutOfResources, "attention: kernel built with %d registers per thread, the "
-                        "register split assumes %d", fa.numRegs, kRegsLaunch);
-        e = cudaFuncSetAttribute(attention_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-        if (e != cudaSuccess) return fail(static_cast<int>(e), "attention: shared memory attribute: %s", cudaGetErrorString(e));
-        ready[dev].store(true, std::memory_order_release);
+        if (e != cudaSuccess) return api_fail(e, "attention: kernel attributes: %s", cudaGetErrorString(e));
+        regs = fa.numRegs;
+        launch_regs.store(regs, std::memory_order_release);
     }
+    if (regs != kRegsLaunch)
+        return fail(cudaErrorLaunchOutOfResources, "attention: kernel built with %d registers per thread, the register "
+                    "split assumes %d", regs, kRegsLaunch);
+    static SmemLimit smem_limit;
+    if (int rc = smem_limit.ensure(attention_fwd_kernel, kSmem, "attention")) return rc;
     dim3 grid(static_cast<unsigned>((seq / kBlock + 1) / 2), static_cast<unsigned>(heads));
     attention_fwd_kernel<<<grid, kThreads, kSmem, as_stream(stream)>>>(tq, tk, tv, p);
     return launch_status("attention");

@@ -9,6 +9,7 @@
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 
@@ -39,6 +40,25 @@ int ok();
 int launch_status(const char* what);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Raises a kernel's dynamic shared-memory limit once per device
+// (cudaFuncSetAttribute applies to the current device); safe to call from any
+// host thread.  Keep one instance per kernel as a function-local static.
+constexpr int kMaxDevices = 64;
+struct SmemLimit {
+    std::atomic<int> raised[kMaxDevices];
+    template <typename Kernel>
+    int ensure(Kernel kernel, int bytes, const char* what) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+            return fail(cudaErrorInvalidDevice, "%s: no usable current device", what);
+        if (raised[dev].load(std::memory_order_acquire) >= bytes) return 0;
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e != cudaSuccess) return api_fail(e, "%s: shared memory attribute: %s", what, cudaGetErrorString(e));
+        raised[dev].store(bytes, std::memory_order_release);
+        return 0;
+    }
+};
 
 // Number of SMs of the current device (cached per device ordinal).
 int sm_count();

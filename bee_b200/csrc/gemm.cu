@@ -741,14 +741,8 @@ template <int BN, bool B_KMAJOR, bool OUT_F32>
 static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
     using Cfg = TileCfg<BN>;
     auto kern = gemm_bf16_tcgen05_kernel<BN, B_KMAJOR, OUT_F32>;
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-        if (e != cudaSuccess) return fail(static_cast<int>(e), "bmm: shared memory attribute: %s", cudaGetErrorString(e));
-        attr_set[dev] = true;
-    }
+    static SmemLimit smem_limit;
+    if (int rc = smem_limit.ensure(kern, Cfg::SMEM, "bmm")) return rc;
     const int grid = p.total_tiles < sm_count() ? p.total_tiles : sm_count();
     kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(ta, tb, p);
     return launch_status("bmm(tcgen05)");
@@ -762,14 +756,8 @@ static int dispatch_tc_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, 
 template <bool B_KMAJOR, bool OUT_F32>
 static int launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
     auto kern = gemm_bf16_tcgen05_2sm_kernel<B_KMAJOR, OUT_F32>;
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Pair2Cfg::SMEM);
-        if (e != cudaSuccess) return fail(static_cast<int>(e), "bmm: shared memory attribute: %s", cudaGetErrorString(e));
-        attr_set[dev] = true;
-    }
+    static SmemLimit smem_limit;
+    if (int rc = smem_limit.ensure(kern, Pair2Cfg::SMEM, "bmm")) return rc;
     const int pairs = sm_count() / 2;
     const int grid = 2 * (p.total_tiles < pairs ? p.total_tiles : pairs);
     kern<<<grid, 192, Pair2Cfg::SMEM, st>>>(ta, tb, p);
@@ -978,14 +966,8 @@ int bee_b200_gemm_splitk_scatter(const void* A, size_t lda, const void* B, size_
     p.owned = (p.total_tiles + world - 1) / world;
     for (int r = 0; r < world; ++r) p.peer_recv[r] = static_cast<float*>(recv_peers[r]);
     auto kern = gemm_bf16_tcgen05_2sm_kernel<false, true, true>;
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Pair2Cfg::SMEM);
-        if (e != cudaSuccess) return fail(static_cast<int>(e), "splitk_scatter: shared memory attribute: %s", cudaGetErrorString(e));
-        attr_set[dev] = true;
-    }
+    static SmemLimit smem_limit;
+    if (int rc = smem_limit.ensure(kern, Pair2Cfg::SMEM, "splitk_scatter")) return rc;
     const int pairs = sm_count() / 2;
     const int grid = 2 * (p.total_tiles < pairs ? p.total_tiles : pairs);
     kern<<<grid, 192, Pair2Cfg::SMEM, as_stream(stream)>>>(ta, tb, p);
