@@ -842,6 +842,235 @@ static int launch_simt(const void* A, const void* B, void* C, size_t batch, size
     return launch_status("matmul(simt)");
 }
 
+// ---------------------------------------------------------------- fp32 matmul on the bf16 tensor cores
+//
+// Exact-enough fp32 products from bf16 MMAs.  Every fp32 value x is split into
+// three bf16 pieces, hi = bf16(x), mid = bf16(x - hi), lo = bf16(x - hi - mid)
+// (each subtraction is exact in fp32), so x = hi + mid + lo to within 2^-27 |x|.
+// Of the nine piece products of a*b the six largest, hh, hm, mh, hl, lh and mm,
+// are kept (the dropped ones are below 2^-26 |a||b|); bf16 products are exact
+// and the tensor core accumulates them in fp32, so the result carries the error
+// of an fp32 accumulation, like the scalar fp32 kernel.  The six products
+// are laid out along K: the split writes A' [S][M][g*K] and B' [S][g*K][N]
+// (g = 6 / S products per batch, piece of A / B per product below), one
+// batched bf16 GEMM with fp32 output computes the S partial products, and for
+// S > 1 a last kernel adds the partials.  S > 1 only when the output has too
+// few tiles to fill the GPU.  Rows of A or columns of B holding a value that
+// is not finite or is too large for bf16 (|x| >= 3e38) are marked by the
+// split; their outputs are recomputed by plain fp32 dot products at the end,
+// so infinities and NaNs propagate as in an fp32 product.
+
+constexpr int kSplitProducts = 6;
+// piece of A and of B in product p (0 = hi, 1 = mid, 2 = lo): hh hm mh hl lh mm
+__host__ __device__ constexpr int piece_a(int p) { return p == 2 || p == 5 ? 1 : (p == 4 ? 2 : 0); }
+__host__ __device__ constexpr int piece_b(int p) { return p == 1 || p == 5 ? 1 : (p == 3 ? 2 : 0); }
+
+__device__ __forceinline__ uint16_t bf16_rn_bits(float x) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
+// One operand of the split: src [rows, cols] fp32 -> dst pieces.  For A
+// element (r, c) of product p = s*g + q goes to dst[s][r][q*cols + c]
+// and a bad value marks flags[1 + r]; for B element (r, c) goes to
+// dst[s][q*rows + r][c] and marks flags[1 + M + c].
+struct SplitOperand {
+    const float* src;
+    size_t rows, cols;
+    uint16_t* dst;
+};
+
+// Both operands in one launch, 8 consecutive elements of a row per thread
+// (cols % 8 == 0): the first A.rows * A.cols / 8 work items split A, the rest B.
+__global__ void __launch_bounds__(256) split3_bf16_kernel(const SplitOperand opA, const SplitOperand opB, int g,
+                                                         size_t M, int* __restrict__ flags) {
+    const size_t groups_a = opA.rows * (opA.cols / 8);
+    const size_t groups = groups_a + opB.rows * (opB.cols / 8);
+    for (size_t gi0 = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; gi0 < groups;
+         gi0 += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const bool is_a = gi0 < groups_a;
+        const float* src = is_a ? opA.src : opB.src;
+        uint16_t* dst = is_a ? opA.dst : opB.dst;
+        const size_t gi = is_a ? gi0 : gi0 - groups_a;
+        const size_t rows = is_a ? opA.rows : opB.rows, cols = is_a ? opA.cols : opB.cols;
+        const size_t slab = rows * cols * static_cast<size_t>(g);  // elements per batch of dst
+        const size_t r = gi / (cols / 8), c = (gi % (cols / 8)) * 8;
+        const float4 v0 = reinterpret_cast<const float4*>(src + r * cols + c)[0];
+        const float4 v1 = reinterpret_cast<const float4*>(src + r * cols + c)[1];
+        const float x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        uint32_t piece[3][4];
+        bool bad = false;
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+            uint16_t h[2], m[2], l[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const float xv = x[e + u];
+                if (!(fabsf(xv) < 3.0e38f)) {  // inf, NaN, or beyond bf16's range
+                    bad = true;
+                    h[u] = m[u] = l[u] = 0;
+                    continue;
+                }
+                h[u] = bf16_rn_bits(xv);
+                const float r1 = xv - __uint_as_float(static_cast<uint32_t>(h[u]) << 16);
+                m[u] = bf16_rn_bits(r1);
+                const float r2 = r1 - __uint_as_float(static_cast<uint32_t>(m[u]) << 16);
+                l[u] = bf16_rn_bits(r2);
+            }
+            piece[0][e / 2] = static_cast<uint32_t>(h[0]) | (static_cast<uint32_t>(h[1]) << 16);
+            piece[1][e / 2] = static_cast<uint32_t>(m[0]) | (static_cast<uint32_t>(m[1]) << 16);
+            piece[2][e / 2] = static_cast<uint32_t>(l[0]) | (static_cast<uint32_t>(l[1]) << 16);
+        }
+        if (bad) {
+            flags[0] = 1;
+            if (is_a) {
+                flags[1 + r] = 1;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    if (!(fabsf(x[e]) < 3.0e38f)) flags[1 + M + c + e] = 1;
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < kSplitProducts; ++p) {
+            const int s = p / g, q = p % g;
+            const int pa = piece_a(p), pb = piece_b(p);  // constants once p is unrolled
+            const size_t off = is_a ? s * slab + r * (cols * g) + q * cols + c : s * slab + (q * rows + r) * cols + c;
+            const uint4 w = is_a ? make_uint4(piece[pa][0], piece[pa][1], piece[pa][2], piece[pa][3])
+                                 : make_uint4(piece[pb][0], piece[pb][1], piece[pb][2], piece[pb][3]);
+            *reinterpret_cast<uint4*>(dst + off) = w;
+        }
+    }
+}
+
+// Plain fp32 dot product of row r of A and column c of B in k order.
+__device__ __forceinline__ float dot_f32(const float* __restrict__ A, const float* __restrict__ B, size_t r, size_t c,
+                                         size_t K, size_t N) {
+    float acc = 0.f;
+    for (size_t k = 0; k < K; ++k) acc = fmaf(A[r * K + k], B[k * N + c], acc);
+    return acc;
+}
+
+// C[i] = sum of the S partials, the later (smaller) products first (M*N % 4 ==
+// 0); outputs in a marked row or column are replaced by plain fp32 dot products.
+__global__ void __launch_bounds__(256) sum_partials_kernel(const float* __restrict__ part, float* __restrict__ C, int S,
+                                                          const float* __restrict__ A, const float* __restrict__ B,
+                                                          size_t M, size_t K, size_t N, const int* __restrict__ flags) {
+    const size_t n = M * N;
+    const bool any_bad = flags[0] != 0;
+    for (size_t i = (blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x) * 4; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x * 4) {
+        float4 acc = *reinterpret_cast<const float4*>(part + static_cast<size_t>(S - 1) * n + i);
+        for (int s = S - 2; s >= 0; --s) {
+            const float4 v = *reinterpret_cast<const float4*>(part + static_cast<size_t>(s) * n + i);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        if (any_bad) {
+            float* a4 = &acc.x;
+            for (int e = 0; e < 4; ++e) {
+                const size_t r = (i + e) / N, c = (i + e) % N;
+                if (flags[1 + r] || flags[1 + M + c]) a4[e] = dot_f32(A, B, r, c, K, N);
+            }
+        }
+        *reinterpret_cast<float4*>(C + i) = acc;
+    }
+}
+
+// Outputs whose row of A or column of B was marked (single-batch case): plain
+// fp32 dot products.  Returns at once when nothing was marked (flags[0] == 0).
+__global__ void __launch_bounds__(256) split_fixup_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                                         float* __restrict__ C, size_t M, size_t K, size_t N,
+                                                         const int* __restrict__ flags) {
+    if (flags[0] == 0) return;
+    for (size_t r = blockIdx.x; r < M; r += gridDim.x) {
+        const bool row_bad = flags[1 + r] != 0;
+        for (size_t c = threadIdx.x; c < N; c += blockDim.x)
+            if (row_bad || flags[1 + M + c] != 0) C[r * N + c] = dot_f32(A, B, r, c, K, N);
+    }
+}
+
+// Number of batches S (1, 2, 3 or 6) for an M x N output: 1 unless the output
+// tiles cannot fill the GPU, else the S with the fewest tile waves times the
+// products per batch (ties to the smaller S, which writes fewer partials).
+static int split_batches(size_t M, size_t N) {
+    const bool pair = M > 128 && N > 128;
+    const size_t tiles = pair ? ((M + 255) / 256) * ((N + 255) / 256) : ((M + 127) / 128) * ((N + (N > 128 ? 255 : 127)) /
+                                                                                         (N > 128 ? 256 : 128));
+    const size_t slots = static_cast<size_t>(pair ? sm_count() / 2 : sm_count());
+    if (slots == 0 || tiles >= slots) return 1;
+    int best = 1;
+    size_t best_cost = ~size_t(0);
+    for (int S : {1, 2, 3, 6}) {
+        const size_t cost = ((tiles * S + slots - 1) / slots) * static_cast<size_t>(kSplitProducts / S);
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = S;
+        }
+    }
+    return best;
+}
+
+// C = A . B for contiguous row-major fp32 A [M, K], B [K, N], C [M, N] through
+// the split above.  Returns -1 (nothing launched, nothing allocated) when the
+// shape does not suit it; the caller then runs the scalar kernel.
+static int matmul_f32_split(const float* A, const float* B, float* C, size_t M, size_t K, size_t N, cudaStream_t st) {
+    if (K % 8 != 0 || N % 8 != 0 || K < 64 || !aligned16(A) || !aligned16(B) || !aligned16(C)) return -1;
+    // ~25 us of fixed cost (scratch, split, partial sum, fix-up launches): below 2^28
+    // multiply-adds the scalar kernel finishes first
+    if (static_cast<double>(M) * static_cast<double>(N) * static_cast<double>(K) < 268435456.0) return -1;
+    if (M > (1u << 30) || N > (1u << 30) || K * kSplitProducts > (1u << 30)) return -1;
+    const int S = split_batches(M, N);
+    const int g = kSplitProducts / S;
+    auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
+    const size_t a_bytes = up(static_cast<size_t>(kSplitProducts) * M * K * 2);
+    const size_t b_bytes = up(static_cast<size_t>(kSplitProducts) * K * N * 2);
+    const size_t p_bytes = S > 1 ? up(static_cast<size_t>(S) * M * N * 4) : 0;
+    const size_t f_bytes = up((1 + M + N) * sizeof(int));
+    void* mem = nullptr;
+    cudaError_t e = pool_malloc(&mem, a_bytes + b_bytes + p_bytes + f_bytes, st);
+    if (e != cudaSuccess) return api_fail(e, "matmul(f32 split): scratch of %zu bytes: %s",
+                                          a_bytes + b_bytes + p_bytes + f_bytes, cudaGetErrorString(e));
+    uint8_t* base = static_cast<uint8_t*>(mem);
+    uint16_t* a3 = reinterpret_cast<uint16_t*>(base);
+    uint16_t* b3 = reinterpret_cast<uint16_t*>(base + a_bytes);
+    float* part = S > 1 ? reinterpret_cast<float*>(base + a_bytes + b_bytes) : C;
+    int* flags = reinterpret_cast<int*>(base + a_bytes + b_bytes + p_bytes);
+    int rc = 0;
+    e = cudaMemsetAsync(flags, 0, (1 + M + N) * sizeof(int), st);
+    if (e != cudaSuccess) rc = api_fail(e, "matmul(f32 split): %s", cudaGetErrorString(e));
+    const int sms = sm_count() > 0 ? sm_count() : 148;
+    auto grid_for = [&](size_t work) {
+        const size_t blocks = (work + 255) / 256;
+        return static_cast<unsigned>(blocks < static_cast<size_t>(sms) * 8 ? (blocks ? blocks : 1) : static_cast<size_t>(sms) * 8);
+    };
+    if (rc == 0) {
+        const SplitOperand opA{A, M, K, a3}, opB{B, K, N, b3};
+        split3_bf16_kernel<<<grid_for(M * (K / 8) + K * (N / 8)), 256, 0, st>>>(opA, opB, g, M, flags);
+        rc = launch_status("matmul(f32 split)");
+    }
+    if (rc == 0) {
+        const long long gk = static_cast<long long>(g) * static_cast<long long>(K);
+        BmmStrides sd{gk, static_cast<long long>(N), static_cast<long long>(N), static_cast<long long>(M) * gk,
+                      gk * static_cast<long long>(N), static_cast<long long>(M * N)};
+        rc = bmm_bf16_tc(DT_F32, a3, b3, part, static_cast<size_t>(S), M, static_cast<size_t>(gk), N, 0, 1.0f, sd, st);
+        if (rc == -1) rc = fail(cudaErrorNotSupported, "matmul(f32 split): tensor-core path rejected the split operands");
+    }
+    if (rc == 0 && S > 1) {
+        sum_partials_kernel<<<grid_for(M * N / 4), 256, 0, st>>>(part, C, S, A, B, M, K, N, flags);
+        rc = launch_status("matmul(f32 split sum)");
+    }
+    if (rc == 0 && S == 1) {
+        split_fixup_kernel<<<static_cast<unsigned>(M < static_cast<size_t>(sms) * 4 ? M : static_cast<size_t>(sms) * 4), 256, 0,
+                             st>>>(A, B, C, M, K, N, flags);
+        rc = launch_status("matmul(f32 split fixup)");
+    }
+    cudaError_t e2 = cudaFreeAsync(mem, st);
+    if (rc == 0 && e2 != cudaSuccess) rc = api_fail(e2, "matmul(f32 split): %s", cudaGetErrorString(e2));
+    return rc;
+}
+
 }  // namespace bee_b200
 
 using namespace bee_b200;
@@ -907,6 +1136,11 @@ int bee_b200_bmm_strided(int dt_in, int dt_out, const void* A, int64_t lda, int6
 
 int bee_b200_matmul(int dt, const void* A, const void* B, void* C, size_t M, size_t K, size_t N,
                     bee_b200_stream_t stream) {
+    if (dt == DT_F32 && M != 0 && N != 0 && A && B && C) {
+        const int rc = matmul_f32_split(static_cast<const float*>(A), static_cast<const float*>(B), static_cast<float*>(C),
+                                        M, K, N, as_stream(stream));
+        if (rc != -1) return rc == 0 ? ok() : rc;
+    }
     return bee_b200_bmm(dt, dt, A, B, C, 1, M, K, N, 0, 1.0f, stream);
 }
 

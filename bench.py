@@ -559,7 +559,9 @@ def run_extras(args, d, dev, stream, peaks):
             ms = timed(lambda: call("bee_b200_matmul", _capi.F32, a32.data_ptr(), b32.data_ptr(), c32.data_ptr(), 1024,
                                     1024, 1024, st), label="gemm_f32_1024")
             out["gemm_f32_1024"] = {"ms": round(ms, 4), "TFLOP/s": round(2.0 * 1024 ** 3 / (ms / 1e3) / 1e12, 2),
-                                    "unit": "TFLOP/s (per GPU)", "path": "SIMT fp32 (parity config, rel tol 1e-4)"}
+                                    "unit": "TFLOP/s (per GPU)",
+                                    "path": "fp32 as three bf16 pieces, six products on the tcgen05 tensor cores, "
+                                            "fp32 accumulate (parity config, rel tol 1e-4)"}
             del a32, b32, c32
         if want("transpose_f32_8192", "bcast_sub_rowmax_f32_8192", "sum_dim0_f32_8192", "contiguous_kt_bf16"):
             # layout and broadcast ops on the [8192, 8192] fp32 shard (HBM-bound, 2 x 256 MiB moved)

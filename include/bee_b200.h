@@ -219,9 +219,17 @@ BEE_B200_API int bee_b200_rms_norm_rope(int dt, const void* x, const void* w, vo
 
 /* C[M,N] = A[M,K] . B[K,N], row-major contiguous, same dtype.
  * BF16: tcgen05 tensor cores with fp32 accumulation and a bf16 (RNE) result;
- * F32 / F64 / I32 / I64: tiled SIMT kernel accumulating in the element type
- * (I32/I64 wrap).  Replaces ops_matmul (Bee/CUDA/Ops/OpsBridge.hpp:38) behind
- * tensor::cuda::matmul (Bee/Tensor/Cuda/Backend.hpp:70). */
+ * F32 from 2^28 multiply-adds up (K and N multiples of 8, 16-byte aligned
+ * buffers): every value split into three bf16 pieces, six piece products on
+ * the same tensor cores with fp32 accumulation (fp32-level error; rows and
+ * columns holding inf, NaN or |x| >= 3e38 recomputed in plain fp32), with
+ * 12*(M*K + K*N) + 4*(1 + M + N) bytes of scratch from the stream-ordered
+ * pool, plus 4*S*M*N for S > 1 batches of partial products (S <= 6; S = 1
+ * when the output tiles fill the GPU);
+ * smaller F32, and F64 / I32 / I64: tiled SIMT kernel
+ * accumulating in the element type (I32/I64 wrap).  Replaces ops_matmul
+ * (Bee/CUDA/Ops/OpsBridge.hpp:38) behind tensor::cuda::matmul
+ * (Bee/Tensor/Cuda/Backend.hpp:70). */
 BEE_B200_API int bee_b200_matmul(int dt, const void* A, const void* B, void* C, size_t M, size_t K, size_t N,
                                  bee_b200_stream_t stream);
 

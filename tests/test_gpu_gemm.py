@@ -1,4 +1,5 @@
-"""GPU parity of the GEMM kernels (tcgen05 bf16 path and the SIMT path)
+"""GPU parity of the GEMM kernels (tcgen05 bf16 path, the fp32 path through split bf16
+products on the tensor cores, and the SIMT path)
 against the oracle, the golden fixtures and the reference's known answers.
 Tolerances: tests/_tol.py (bf16 outputs: 1e-2 relative with a 1e-2*rms floor
 for entries that cancel to ~0; fp32 outputs: 1e-4 of the |A||B| condition)."""
@@ -47,7 +48,7 @@ def rand_bf16(rng, shape, scale=1.0):
     return f32_to_bf16_bits((rng.standard_normal(shape) * scale).astype(np.float32))
 
 
-# ---------------------------------------------------------------- fp32 (SIMT)
+# ---------------------------------------------------------------- fp32 (SIMT below 2^28 multiply-adds, split bf16 on the tensor cores above)
 
 def test_matmul_f32_kat(cuda):
     """Tests/Tensor/MatmulTests.cpp:31-62."""
@@ -88,6 +89,61 @@ def test_matmul_f32_1024_config(cuda, oracle):
                stream(torch))
     torch.cuda.synchronize()
     assert_dot_close(c.cpu().numpy(), oracle.matmul_f32(a, b), a, b, 1e-4, what="fp32 1024^3")
+
+
+def _matmul_f32(torch, a, b):
+    from bee_b200 import _capi
+    (m, k), n = a.shape, b.shape[1]
+    da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    c = torch.full((m, n), 7.0, dtype=torch.float32, device="cuda")
+    _capi.call("bee_b200_matmul", _capi.F32, da.data_ptr(), db.data_ptr(), c.data_ptr(), m, k, n, stream(torch))
+    torch.cuda.synchronize()
+    return c.cpu().numpy()
+
+
+# Shapes on the tensor-core fp32 path (K and N multiples of 8, M*N*K >= 2^28); by
+# their tile counts they run as one, two, three or six batches of products (1024^3 above: three).
+@pytest.mark.parametrize("m,k,n,spread", [(1024, 256, 2048, 0), (128, 16384, 128, 0), (2048, 64, 2048, 0),
+                                          (600, 512, 1024, 0), (1024, 256, 1024, 30)])
+def test_matmul_f32_split_path(cuda, oracle, m, k, n, spread):
+    """fp32 matmul through the three-piece bf16 split on the tensor cores against
+    the oracle, 1e-4 of |A||B|; spread > 0 scales the entries by 2^-spread..2^spread."""
+    torch = cuda
+    rng = np.random.default_rng(m * 7 + k * 3 + n + spread)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    if spread:
+        a *= np.exp2(rng.integers(-spread, spread + 1, (m, k))).astype(np.float32)
+        b *= np.exp2(rng.integers(-spread, spread + 1, (k, n))).astype(np.float32)
+    got = _matmul_f32(torch, a, b)
+    assert_dot_close(got, oracle.matmul_f32(a, b), a, b, 1e-4, what=f"fp32 {m}x{k}x{n} spread {spread}")
+
+
+def test_matmul_f32_split_nonfinite(cuda, oracle):
+    """Infinities, NaNs and values beyond bf16's range in A and B: the outputs of
+    the rows and columns that hold them are recomputed in plain fp32, so the
+    NaN / +inf / -inf pattern equals the oracle's and the finite entries stay
+    within 1e-4 of |A||B|."""
+    torch = cuda
+    rng = np.random.default_rng(77)
+    m, k, n = 512, 1024, 512
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    a[3, 10] = np.inf
+    a[7, 20] = 3.39e38
+    a[9, 0] = np.nan
+    b[5, 5] = -np.inf
+    b[100, 9] = np.nan
+    b[17, 33] = -3.2e38
+    got = _matmul_f32(torch, a, b)
+    want = oracle.matmul_f32(a, b)
+    for f in (np.isnan, np.isposinf, np.isneginf):
+        assert np.array_equal(f(got), f(want)), f"{f.__name__} pattern differs"
+    with np.errstate(invalid="ignore", over="ignore"):
+        scale = np.abs(a.astype(np.float64)) @ np.abs(b.astype(np.float64))
+    ok = np.isfinite(want) & np.isfinite(scale)
+    err = np.abs(got[ok].astype(np.float64) - want[ok]) / np.maximum(scale[ok], 1e-30)
+    assert err.max() <= 1e-4, f"finite entries: max error {err.max():.3e} x (|A||B|)"
 
 
 @pytest.mark.parametrize("dt,np_t", [("float64", np.float64), ("int32", np.int32), ("int64", np.int64)])
