@@ -780,9 +780,10 @@ static BmmStrides contiguous_strides(size_t M, size_t K, size_t N, int b_trans) 
 // -1 when the shape or the strides cannot be expressed with TMA (the caller
 // falls back to the SIMT kernel).
 // M > 128 and N > 128 use 256x256 tiles on CTA pairs (cta_group::2); smaller
-// problems use 128xBN tiles on single CTAs.
+// problems use 128xBN tiles on single CTAs.  small_tiles: 128x128 tiles on single
+// CTAs whatever the shape (more tiles for outputs that would not fill the GPU).
 static int bmm_bf16_tc(int dt_out, const void* A, const void* B, void* C, size_t batch, size_t M, size_t K, size_t N,
-                       int b_trans, float alpha, const BmmStrides& sd, cudaStream_t st) {
+                       int b_trans, float alpha, const BmmStrides& sd, cudaStream_t st, bool small_tiles = false) {
     // TMA: 16-byte aligned bases, row and batch strides multiples of 16 bytes (8 bf16), positive
     auto ok16 = [](long long v) { return v > 0 && v % 8 == 0 && v < (1ll << 36); };
     if (!ok16(sd.lda) || !ok16(sd.ldb) || !aligned16(A) || !aligned16(B)) return -1;
@@ -790,8 +791,8 @@ static int bmm_bf16_tc(int dt_out, const void* A, const void* B, void* C, size_t
     if (M > (1u << 31) || N > (1u << 31) || K > (1u << 31) || batch > 65535) return -1;
     const uint64_t sa = batch > 1 ? static_cast<uint64_t>(sd.sa) : static_cast<uint64_t>(sd.lda) * M;
     const uint64_t sb = batch > 1 ? static_cast<uint64_t>(sd.sb) : static_cast<uint64_t>(sd.ldb) * (b_trans ? N : K);
-    const int bn = N > 128 ? 256 : 128;
-    const bool pair = N > 128 && M > 128;
+    const int bn = N > 128 && !small_tiles ? 256 : 128;
+    const bool pair = N > 128 && M > 128 && !small_tiles;
     CUtensorMap ta, tb;
     if (make_map(&ta, A, K, M, batch, static_cast<uint64_t>(sd.lda), sa, 64, 128)) return -1;
     if (b_trans) {
@@ -854,8 +855,9 @@ static int launch_simt(const void* A, const void* B, void* C, size_t batch, size
 // are laid out along K: the split writes A' [S][M][g*K] and B' [S][g*K][N]
 // (g = 6 / S products per batch, piece of A / B per product below), one
 // batched bf16 GEMM with fp32 output computes the S partial products, and for
-// S > 1 a last kernel adds the partials.  S > 1 only when the output has too
-// few tiles to fill the GPU.  Rows of A or columns of B holding a value that
+// S > 1 a last kernel adds the partials.  Outputs too small to fill the GPU
+// with 256x256 tiles use 128x128 tiles and, if that still leaves SMs idle,
+// S > 1.  Rows of A or columns of B holding a value that
 // is not finite or is too large for bf16 (|x| >= 3e38) are marked by the
 // split; their outputs are recomputed by plain fp32 dot products at the end,
 // so infinities and NaNs propagate as in an fp32 product.
@@ -991,25 +993,31 @@ __global__ void __launch_bounds__(256) split_fixup_kernel(const float* __restric
     }
 }
 
-// Number of batches S (1, 2, 3 or 6) for an M x N output: 1 unless the output
-// tiles cannot fill the GPU, else the S with the fewest tile waves times the
-// products per batch (ties to the smaller S, which writes fewer partials).
-static int split_batches(size_t M, size_t N) {
-    const bool pair = M > 128 && N > 128;
-    const size_t tiles = pair ? ((M + 255) / 256) * ((N + 255) / 256) : ((M + 127) / 128) * ((N + (N > 128 ? 255 : 127)) /
-                                                                                         (N > 128 ? 256 : 128));
-    const size_t slots = static_cast<size_t>(pair ? sm_count() / 2 : sm_count());
-    if (slots == 0 || tiles >= slots) return 1;
+// Tiling of the split products for an M x N output: 256x256 pair tiles and one
+// batch (S = 1) when those tiles fill the GPU; otherwise 128x128 single-CTA
+// tiles, one batch if they fill it, else the S (1, 2, 3 or 6) with the fewest
+// tile waves times products per batch (ties to the smaller S, which writes
+// fewer partials).
+struct SplitPlan {
+    int S;
+    bool small_tiles;
+};
+static SplitPlan split_plan(size_t M, size_t N) {
+    const size_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+    const size_t sms = static_cast<size_t>(sm_count() > 0 ? sm_count() : 148);
+    if (M > 128 && N > 128 && pair_tiles >= sms / 2) return {1, false};
+    const size_t tiles = ((M + 127) / 128) * ((N + 127) / 128);
+    if (tiles >= sms) return {1, true};
     int best = 1;
     size_t best_cost = ~size_t(0);
     for (int S : {1, 2, 3, 6}) {
-        const size_t cost = ((tiles * S + slots - 1) / slots) * static_cast<size_t>(kSplitProducts / S);
+        const size_t cost = ((tiles * S + sms - 1) / sms) * static_cast<size_t>(kSplitProducts / S);
         if (cost < best_cost) {
             best_cost = cost;
             best = S;
         }
     }
-    return best;
+    return {best, true};
 }
 
 // C = A . B for contiguous row-major fp32 A [M, K], B [K, N], C [M, N] through
@@ -1021,7 +1029,8 @@ static int matmul_f32_split(const float* A, const float* B, float* C, size_t M, 
     // multiply-adds the scalar kernel finishes first
     if (static_cast<double>(M) * static_cast<double>(N) * static_cast<double>(K) < 268435456.0) return -1;
     if (M > (1u << 30) || N > (1u << 30) || K * kSplitProducts > (1u << 30)) return -1;
-    const int S = split_batches(M, N);
+    const SplitPlan plan = split_plan(M, N);
+    const int S = plan.S;
     const int g = kSplitProducts / S;
     auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
     const size_t a_bytes = up(static_cast<size_t>(kSplitProducts) * M * K * 2);
@@ -1054,7 +1063,8 @@ static int matmul_f32_split(const float* A, const float* B, float* C, size_t M, 
         const long long gk = static_cast<long long>(g) * static_cast<long long>(K);
         BmmStrides sd{gk, static_cast<long long>(N), static_cast<long long>(N), static_cast<long long>(M) * gk,
                       gk * static_cast<long long>(N), static_cast<long long>(M * N)};
-        rc = bmm_bf16_tc(DT_F32, a3, b3, part, static_cast<size_t>(S), M, static_cast<size_t>(gk), N, 0, 1.0f, sd, st);
+        rc = bmm_bf16_tc(DT_F32, a3, b3, part, static_cast<size_t>(S), M, static_cast<size_t>(gk), N, 0, 1.0f, sd, st,
+                         plan.small_tiles);
         if (rc == -1) rc = fail(cudaErrorNotSupported, "matmul(f32 split): tensor-core path rejected the split operands");
     }
     if (rc == 0 && S > 1) {

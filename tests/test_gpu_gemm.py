@@ -102,9 +102,10 @@ def _matmul_f32(torch, a, b):
 
 
 # Shapes on the tensor-core fp32 path (K and N multiples of 8, M*N*K >= 2^28); by
-# their tile counts they run as one, two, three or six batches of products (1024^3 above: three).
-@pytest.mark.parametrize("m,k,n,spread", [(1024, 256, 2048, 0), (128, 16384, 128, 0), (2048, 64, 2048, 0),
-                                          (600, 512, 1024, 0), (1024, 256, 1024, 30)])
+# their tile counts they run on 256x256 pair tiles in one batch (2304 x 2304), or on
+# 128x128 tiles in one, two, three or six batches of products (1024^3 above: two).
+@pytest.mark.parametrize("m,k,n,spread", [(2304, 64, 2304, 0), (1024, 256, 2048, 0), (128, 16384, 128, 0),
+                                          (2048, 64, 2048, 0), (600, 512, 1024, 0), (1024, 256, 1024, 30)])
 def test_matmul_f32_split_path(cuda, oracle, m, k, n, spread):
     """fp32 matmul through the three-piece bf16 split on the tensor cores against
     the oracle, 1e-4 of |A||B|; spread > 0 scales the entries by 2^-spread..2^spread."""
