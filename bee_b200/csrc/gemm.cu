@@ -857,10 +857,10 @@ static int launch_simt(const void* A, const void* B, void* C, size_t batch, size
 // batched bf16 GEMM with fp32 output computes the S partial products, and for
 // S > 1 a last kernel adds the partials.  Outputs too small to fill the GPU
 // with 256x256 tiles use 128x128 tiles and, if that still leaves SMs idle,
-// S > 1.  Rows of A or columns of B holding a value that
-// is not finite or is too large for bf16 (|x| >= 3e38) are marked by the
-// split; their outputs are recomputed by plain fp32 dot products at the end,
-// so infinities and NaNs propagate as in an fp32 product.
+// S > 1.  Rows of A or columns of B holding a value that is not finite or is
+// too large for bf16 (|x| >= 3e38) are marked by the split; their outputs are
+// recomputed by plain fp32 dot products at the end, so infinities and NaNs
+// propagate as in an fp32 product.
 
 constexpr int kSplitProducts = 6;
 // piece of A and of B in product p (0 = hi, 1 = mid, 2 = lo): hh hm mh hl lh mm
