@@ -502,7 +502,8 @@ def run_extras(args, d, dev, stream, peaks):
     def timed(fn, label=None):
         """ms per call of fn.  Warm-up: at least `warm` calls and about 30 ms of work, so
         that the SM clock has recovered from the previous config (the 8192^3 GEMMs run at
-        the 1000 W power cap); the timed region: at least `steps` calls and about 10 ms.
+        the 1000 W power cap); the timed region: at least `steps` calls and about 10 ms by
+        a warm estimate (so the 0.2 ms clock probe stays small beside it).
         Call counts come from the slowest rank's estimate, so every rank makes the same
         calls (fn may hold collectives).  With a label, one in-kernel clock probe
         (0.2 ms on a side stream) runs mid-region and its SM MHz is reported."""
@@ -513,11 +514,17 @@ def run_extras(args, d, dev, stream, peaks):
         fn()
         e1.record(stream)
         stream.synchronize()
-        est = max(d.max(e0.elapsed_time(e1)), 1e-3)
+        est = max(d.max(e0.elapsed_time(e1)), 1e-3)  # the first call may carry one-time costs
         n_warm = max(warm, min(int(30.0 / est), 2000))
-        n_time = max(steps, min(int(10.0 / est), 2000))
         for _ in range(n_warm):
             fn()
+        e0.record(stream)
+        for _ in range(3):
+            fn()
+        e1.record(stream)
+        stream.synchronize()
+        est = max(d.max(e0.elapsed_time(e1)) / 3, 1e-3)  # warm estimate sizes the region
+        n_time = max(steps, min(int(10.0 / est), 2000))
         d.barrier()
         torch.cuda.synchronize()
         e0.record(stream)
