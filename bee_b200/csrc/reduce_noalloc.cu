@@ -9,16 +9,25 @@
 // on every call; this variant uses a fixed array compiled into the library
 // instead, and the caller still supplies the input and the output.
 //
-// The array is a file-scope __device__ variable, so every GPU on which the
-// library is loaded holds it (kScratchBytes) from module load until the
-// process exits.  Host code cannot use the variable's name as a device
-// address, so the first call on each device looks the address up with
-// cudaGetSymbolAddress (with that device current) and caches it; make that
-// first call before any stream capture.  All calls share the one array and it
-// keeps whatever the last call left there: the ticket word that must start at
-// zero is cleared on the stream before every launch, and calls whose kernels
-// overlap on the GPU (different streams at once) race on the array — issue
-// them on one stream, or use bee_b200_reduce_global.
+// The array is a file-scope __device__ variable: every GPU on which this
+// library's module is loaded holds it (kScratchBytes) until the process exits.
+// Host code cannot use the variable's name as a device address, so the entry
+// point looks the address up with cudaGetSymbolAddress (with the device
+// current) on every call; that lookup is a host-side table read once the module
+// is loaded, and repeating it means a device reset, which reloads the module
+// and may move the array, never leaves a stale address behind.
+//
+// Warm-up: CUDA loads modules and kernels lazily (on first use) by default, and
+// loading can itself need device memory.  The first call on each device (and
+// the first after a device reset) therefore does the set-up: it loads the
+// module, takes the array's address and loads every kernel this entry point can
+// launch (all ops and dtypes).  Make one call per device at start-up, while
+// memory is still available and before any stream capture; after that no call
+// loads anything.  All calls share the one array and it keeps whatever the last
+// call left there: the ticket word that must start at zero is cleared on the
+// stream before every launch, and calls whose kernels overlap on the GPU
+// (different streams at once) race on the array — issue them on one stream, or
+// use bee_b200_reduce_global.
 #include <mutex>
 
 #include "reduce.cuh"
@@ -34,24 +43,48 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-void* g_addr[kMaxDevices] = {nullptr};
+void* g_loaded_at[kMaxDevices] = {nullptr};  // array address seen when this device's kernels were loaded
 
-// Device address of g_noalloc_scratch on the current device (set-up once per device).
+template <int OP, typename T> int load_kernel() {
+    cudaFuncAttributes attr;
+    const cudaError_t e = cudaFuncGetAttributes(&attr, reduce_global_kernel<ElemRed<OP, T>>);
+    return e == cudaSuccess ? 0 : fail(static_cast<int>(e), "reduce_global_noalloc: loading a kernel: %s", cudaGetErrorString(e));
+}
+
+template <typename T> int load_kernels_of() {
+    int rc = load_kernel<RED_MIN, T>();
+    if (!rc) rc = load_kernel<RED_MAX, T>();
+    if constexpr (!std::is_same_v<T, uint8_t>) {
+        if (!rc) rc = load_kernel<RED_SUM, T>();
+        if (!rc) rc = load_kernel<RED_PROD, T>();
+    }
+    return rc;
+}
+
+// Device address of g_noalloc_scratch on the current device.  The first call
+// on a device (or the first after a reset moved the array) also loads every
+// kernel this entry point launches, so later calls load nothing.
 int scratch_address(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fail(static_cast<int>(e), "reduce_global_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
     if (dev < 0 || dev >= kMaxDevices) return fail(cudaErrorInvalidDevice, "reduce_global_noalloc: device %d out of range", dev);
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+        return fail(e != cudaSuccess ? static_cast<int>(e) : cudaErrorInvalidSymbol,
+                    "reduce_global_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_addr[dev]) {
-        void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p)
-            return fail(e != cudaSuccess ? static_cast<int>(e) : cudaErrorInvalidSymbol,
-                        "reduce_global_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-        g_addr[dev] = p;
+    if (g_loaded_at[dev] != p) {
+        int rc = load_kernels_of<uint8_t>();
+        if (!rc) rc = load_kernels_of<int32_t>();
+        if (!rc) rc = load_kernels_of<int64_t>();
+        if (!rc) rc = load_kernels_of<float>();
+        if (!rc) rc = load_kernels_of<double>();
+        if (rc) return rc;
+        g_loaded_at[dev] = p;
     }
-    *out = g_addr[dev];
+    *out = p;
     return 0;
 }
 

@@ -54,9 +54,9 @@ OP_BYTES = {
 }
 STEP_BYTES = sum(OP_BYTES.values())
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each
-# sweep kernel, from one ncu capture of this bench's own command; recorded in
-# profiles/memory_sweep_8192x8192.md.  Writes still dirty in L2 when a kernel
-# ends are not counted, hence slightly below the algorithmic bytes.
+# sweep kernel, from one ncu capture of this bench's own command.  Writes still
+# dirty in L2 when a kernel ends are not counted, hence slightly below the
+# algorithmic bytes.
 NCU_TRAFFIC = {
     "add_f32": 768_840_000, "mul_f32": 770_200_000, "cast_f32_bf16": 359_370_000,
     "row_sum_f32": 268_870_000, "row_max_f32": 268_560_000, "softmax_f32": 486_080_000, "sum_i32": 269_000_000,
@@ -449,8 +449,7 @@ def run_ours(args, d: Dist):
                          "unit": "GB/s", "frac": round(dom_gbs / peaks["hbm_gbs"], 3),
                          "peak_source": peaks["source"], "algorithmic_bytes": OP_BYTES[dominant],
                          "traffic": NCU_TRAFFIC.get(dominant),
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch, "
-                                           "profiles/memory_sweep_8192x8192.md"},
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch"},
             "ops": ops_json,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,

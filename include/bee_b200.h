@@ -138,11 +138,16 @@ BEE_B200_API int bee_b200_reduce_global(int op, int dt, const void* src, void* d
  * owns all device memory through its own allocator, or a latency-critical loop
  * that cannot let the stream-ordered pool grow.  Per-block scratch lives in a
  * fixed 64 KiB array compiled into the library, which every GPU that loads the
- * library holds until the process exits; a call whose partials would not fit
- * (more than 8160 blocks of 8-byte partials) is rejected with
- * cudaErrorInvalidValue and a message.  The first call on each device looks up
- * the array's device address (one-time set-up per device): make it before any
- * stream capture.  All calls share the array: calls whose kernels overlap on
+ * library's module holds until the process exits; a call whose partials would
+ * not fit (more than 8160 blocks of 8-byte partials) is rejected with
+ * cudaErrorInvalidValue and a message.  Warm-up is required: CUDA loads modules
+ * and kernels lazily, and loading can need device memory, so the first call on
+ * each device (and the first after a device reset) loads the module, looks up
+ * the array's address and loads every kernel this entry point launches, all ops
+ * and dtypes.  Make one call per device at start-up, while memory is available
+ * and before any stream capture; later calls load and allocate nothing (the
+ * address is looked up again on every call, a host-side read, so a reset never
+ * leaves it stale).  All calls share the array: calls whose kernels overlap on
  * the GPU (different streams at once) race, so keep them on one stream.
  * Same arguments, dtypes, ops and results as bee_b200_reduce_global. */
 BEE_B200_API int bee_b200_reduce_global_noalloc(int op, int dt, const void* src, void* dst, size_t n,

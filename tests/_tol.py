@@ -6,6 +6,13 @@
 * fp32 results of multi-step math: relative tolerance 1e-4.
 * bf16 results against the fp32 oracle: relative tolerance 1e-2.
 
+The stated tolerances are enforced on the output's own scale by
+assert_output_close: |got - ref| <= rtol * max(|ref|, rms(ref)) element-wise.
+That is the tolerance a caller reads off the output (a TF32 product, or an
+attention output a few percent off, fails it); the condition-number forms
+below (|A||B| for a product, P|V| for attention) are kept beside it as a
+second, looser check that names the source of an error.
+
 "Relative" is measured against max(|ref|, floor * rms(ref)) element-wise, so
 that entries whose exact value is near zero (cancellation in a sum, a dot
 product or a rotation) are judged on the scale of the tensor rather than on
@@ -26,6 +33,34 @@ def rel_err(got, ref, floor=1e-3):
 def assert_rel(got, ref, rtol, floor=1e-3, what=""):
     e = rel_err(got, ref, floor)
     assert e <= rtol, f"{what}: max relative error {e:.3e} > {rtol:.1e}"
+
+
+def output_err(got, ref):
+    """max |got - ref| / max(|ref|, rms(ref)) over the finite entries of ref."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    ok = np.isfinite(ref)
+    if not ok.any():
+        return 0.0
+    g, r = got[ok], ref[ok]
+    rms = float(np.sqrt(np.mean(r * r)))
+    scale = np.maximum(np.abs(r), rms)
+    scale = np.where(scale == 0, 1.0, scale)
+    return float(np.max(np.abs(g - r) / scale))
+
+
+def assert_output_close(got, ref, rtol, what=""):
+    """The stated tolerance on the output's own scale:
+    |got - ref| <= rtol * max(|ref|, rms(ref)) element-wise; prints the
+    observed error so a run with -s records it."""
+    e = output_err(got, ref)
+    g = np.asarray(got, np.float64)
+    r = np.asarray(ref, np.float64)
+    ok = np.isfinite(r)
+    nrm = float(np.linalg.norm(g[ok] - r[ok]) / max(np.linalg.norm(r[ok]), 1e-300)) if ok.any() else 0.0
+    print(f"[tol] {what}: max error {e:.3e} of max(|ref|, rms(ref)), norm-wise {nrm:.3e} (bound {rtol:.0e})")
+    assert e <= rtol, f"{what}: max error {e:.3e} x max(|ref|, rms(ref)) > {rtol:.1e}"
+    assert nrm <= rtol, f"{what}: norm-wise relative error {nrm:.3e} > {rtol:.1e}"
 
 
 def assert_sum_close(got, ref, abs_terms, rtol, what=""):

@@ -95,16 +95,34 @@ def _row_gather_rank(rank, world):
     np.testing.assert_array_equal(full.numpy(), orc.softmax_f32(x))
 
 
-def _missing_rank(rank, world):
-    # rank 1 leaves between steps; rank 0's next collective must fail, not hang
-    if rank == 1:
-        return
-    t = torch.ones(1)
+def _departed_worker(rank, world, port, q):
+    """Step 1 runs on both ranks; rank 1 then leaves between steps (exits
+    without tearing the group down); rank 0's step-2 collective must raise,
+    within the group's timeout, rather than hang or complete."""
+    import datetime
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
     try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+        t = torch.ones(1)
         dist.all_reduce(t)
+        if rank == 1:
+            q.put((1, "left after step 1", float(t.item()), 0.0))
+            q.close()
+            q.join_thread()  # the message is sent before the process leaves
+            os._exit(0)
+        t0 = time.monotonic()
+        try:
+            dist.all_reduce(torch.ones(1))
+            q.put((0, "completed", float(t.item()), time.monotonic() - t0))
+        except Exception as e:  # the expected outcome
+            q.put((0, f"raised {type(e).__name__}", float(t.item()), time.monotonic() - t0))
     except Exception:
-        return
-    raise AssertionError("collective with a departed rank did not fail")
+        q.put((rank, "failed before step 2: " + traceback.format_exc(), 0.0, 0.0))
+    q.close()
+    q.join_thread()
+    os._exit(0)
 
 
 def test_int32_sum_over_two_ranks():
@@ -121,18 +139,19 @@ def test_row_sharded_softmax_gather_over_two_ranks():
 
 def test_departed_rank_fails_the_collective():
     ctx = mp.get_context("spawn")
-    errq = ctx.Queue()
+    q = ctx.Queue()
     port = _free_port()
-
-    def run():
-        procs = [ctx.Process(target=_worker, args=(r, 2, port, _missing_rank, errq)) for r in range(2)]
-        for p in procs:
-            p.start()
-        return procs
-
-    procs = run()
-    results = dict(errq.get(timeout=120) for _ in procs)
+    procs = [ctx.Process(target=_departed_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in procs:
+        rank, outcome, step1, elapsed = q.get(timeout=120)
+        results[rank] = (outcome, step1, elapsed)
     for p in procs:
         p.join(timeout=60)
-    # rank 0 either saw the collective fail (returned None) or its teardown failed; it never hangs
-    assert set(results) == {0, 1}
+    assert results[1][:2] == ("left after step 1", 2.0), results
+    outcome, step1, elapsed = results[0]
+    assert step1 == 2.0, results  # step 1 completed on rank 0 as well
+    assert outcome.startswith("raised "), f"rank 0's collective after rank 1 left: {outcome}"
+    assert elapsed < 60.0, f"rank 0 learned of the departure only after {elapsed:.1f} s"

@@ -51,6 +51,61 @@ def test_noalloc_fp32_matches_allocating_entry(cuda, op):
             assert got == want
 
 
+def _pool_attr(rt, pool, attr):
+    err, v = rt.cudaMemPoolGetAttribute(pool, attr)
+    assert err == rt.cudaError_t.cudaSuccess, err
+    return int(v)
+
+
+def test_noalloc_allocates_nothing(cuda):
+    """After the warm-up call, further calls (on new streams, where the
+    allocating entry point would take new scratch) take nothing from the
+    device's stream-ordered pool, the one every allocation of this library comes
+    from, and do not lower the device's free memory; the same check does see an
+    allocation from that pool."""
+    from cuda.bindings import driver as drv
+    from cuda.bindings import runtime as rt
+
+    from bee_b200 import _capi
+    torch = cuda
+    dev = torch.cuda.current_device()
+    err, pool = rt.cudaDeviceGetDefaultMemPool(dev)
+    assert err == rt.cudaError_t.cudaSuccess, err
+    used_now, used_high = rt.cudaMemPoolAttr.cudaMemPoolAttrUsedMemCurrent, rt.cudaMemPoolAttr.cudaMemPoolAttrUsedMemHigh
+    x = torch.from_numpy(np.random.default_rng(5).integers(-1000, 1001, 4 << 20).astype(np.int32)).cuda()
+    out = torch.zeros(1, dtype=torch.int32, device="cuda")
+    want = int(x.sum().item())
+    assert _reduce(torch, "bee_b200_reduce_global_noalloc", 0, _capi.I32, x, out) == want  # warm-up
+    torch.cuda.synchronize()
+    base = _pool_attr(rt, pool, used_now)
+    err, = rt.cudaMemPoolSetAttribute(pool, used_high, drv.cuuint64_t(0))  # high-water mark := current use
+    assert err == rt.cudaError_t.cudaSuccess, err
+    streams = [torch.cuda.Stream() for _ in range(3)]  # new streams: the allocating entry would take new scratch
+    for s in streams:
+        with torch.cuda.stream(s):
+            out.fill_(7)
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    for s in streams:
+        with torch.cuda.stream(s):
+            out.fill_(7)
+            _capi.call("bee_b200_reduce_global_noalloc", 0, _capi.I32, x.data_ptr(), out.data_ptr(), x.numel(),
+                       s.cuda_stream)
+            s.synchronize()
+            assert int(out.item()) == want  # read without a device allocation
+    torch.cuda.synchronize()
+    assert _pool_attr(rt, pool, used_high) == base, "the no-allocation entry point took memory from the pool"
+    assert _pool_attr(rt, pool, used_now) == base
+    assert torch.cuda.mem_get_info()[0] == free_before
+    # the check is live: an allocation from the library's pool shows up in it
+    import ctypes
+    p = ctypes.c_void_p()
+    _capi.call("bee_b200_allocate", ctypes.byref(p), 1 << 20, 256, None)
+    _capi.call("bee_b200_deallocate", p, None)
+    torch.cuda.synchronize()
+    assert _pool_attr(rt, pool, used_high) >= base + (1 << 20)
+
+
 def test_noalloc_other_dtypes_and_errors(cuda):
     from bee_b200 import _capi
     torch = cuda
