@@ -9,6 +9,7 @@
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <atomic>
 #include <cstddef>
 #include <cstdint>
@@ -104,6 +105,12 @@ __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w 
 // Packs two floats into a bf16x2 word with round-to-nearest-even (cvt.rn.bf16x2.f32).
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Packs two floats into an f16x2 word with round-to-nearest-even (cvt.rn.f16x2.f32).
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
 }
 

@@ -14,14 +14,18 @@
 
 namespace bee_b200 {
 
-// bf16 storage tag: raw bits, arithmetic in fp32, RNE on store.
+// bf16 / f16 storage tags: raw bits, arithmetic in fp32, RNE on store.
 struct bf16_t {
+    uint16_t bits;
+};
+struct f16_t {
     uint16_t bits;
 };
 
 template <typename S> struct Compute { using T = S; };
 template <> struct Compute<uint8_t> { using T = int; };
 template <> struct Compute<bf16_t> { using T = float; };
+template <> struct Compute<f16_t> { using T = float; };
 
 template <typename S> __device__ __forceinline__ typename Compute<S>::T to_c(S s) {
     return static_cast<typename Compute<S>::T>(s);
@@ -29,11 +33,13 @@ template <typename S> __device__ __forceinline__ typename Compute<S>::T to_c(S s
 template <> __device__ __forceinline__ float to_c<bf16_t>(bf16_t s) {
     return __uint_as_float(static_cast<uint32_t>(s.bits) << 16);
 }
+template <> __device__ __forceinline__ float to_c<f16_t>(f16_t s) { return __half2float(__ushort_as_half(s.bits)); }
 template <typename S> __device__ __forceinline__ S from_c(typename Compute<S>::T c) { return static_cast<S>(c); }
 template <> __device__ __forceinline__ bf16_t from_c<bf16_t>(float c) {
     __nv_bfloat16 h = __float2bfloat16_rn(c);
     return bf16_t{*reinterpret_cast<uint16_t*>(&h)};
 }
+template <> __device__ __forceinline__ f16_t from_c<f16_t>(float c) { return f16_t{__half_as_ushort(__float2half_rn(c))}; }
 
 template <int OP, typename C> __device__ __forceinline__ C bin(C a, C b) {
     if constexpr (OP == OP_ADD) return a + b;
@@ -313,6 +319,9 @@ __global__ void __launch_bounds__(kThreads) cast_kernel(const Si* __restrict__ s
         auto c = to_c(src[i]);
         if constexpr (std::is_same_v<So, bool>) dst[i] = (c != decltype(c)(0));
         else if constexpr (std::is_same_v<So, bf16_t>) dst[i] = from_c<bf16_t>(static_cast<float>(c));
+        else if constexpr (std::is_same_v<So, f16_t> && std::is_same_v<Si, double>)
+            dst[i] = f16_t{__half_as_ushort(__double2half(c))};  // one rounding from double
+        else if constexpr (std::is_same_v<So, f16_t>) dst[i] = from_c<f16_t>(static_cast<float>(c));
         else dst[i] = static_cast<So>(c);
     }
 }
@@ -446,6 +455,7 @@ static int cast_from(int dst_dt, const void* src, void* dst, size_t n, cudaStrea
     case DT_F32: cast_kernel<Si, float><<<g, kThreads, 0, st>>>(s, static_cast<float*>(dst), n); break;
     case DT_F64: cast_kernel<Si, double><<<g, kThreads, 0, st>>>(s, static_cast<double*>(dst), n); break;
     case DT_BF16: cast_kernel<Si, bf16_t><<<g, kThreads, 0, st>>>(s, static_cast<bf16_t*>(dst), n); break;
+    case DT_F16: cast_kernel<Si, f16_t><<<g, kThreads, 0, st>>>(s, static_cast<f16_t*>(dst), n); break;
     default: return fail(cudaErrorInvalidValue, "ew_cast: unsupported destination dtype %d", dst_dt);
     }
     return launch_status("ew_cast");
@@ -468,6 +478,7 @@ int bee_b200_ew_binary(int op, int dt, const void* a, const void* b, void* out, 
     case DT_F32: return dispatch_binary_op<float>(op, a, b, out, n, st);
     case DT_F64: return dispatch_binary_op<double>(op, a, b, out, n, st);
     case DT_BF16: return dispatch_binary_op<bf16_t>(op, a, b, out, n, st);
+    case DT_F16: return dispatch_binary_op<f16_t>(op, a, b, out, n, st);
     default: return fail(cudaErrorInvalidValue, "ew_binary: unsupported dtype %d", dt);
     }
 }
@@ -515,6 +526,7 @@ int bee_b200_ew_binary_strided(int op, int dt, int ndim, const int64_t* shape, c
     case DT_F32: return dispatch_binary_strided<float>(op, a, b, out, v, st);
     case DT_F64: return dispatch_binary_strided<double>(op, a, b, out, v, st);
     case DT_BF16: return dispatch_binary_strided<bf16_t>(op, a, b, out, v, st);
+    case DT_F16: return dispatch_binary_strided<f16_t>(op, a, b, out, v, st);
     default: return fail(cudaErrorInvalidValue, "ew_binary_strided: unsupported dtype %d", dt);
     }
 }
@@ -529,6 +541,7 @@ int bee_b200_ew_unary(int op, int dt, const void* src, void* dst, size_t n, bee_
     case DT_F32: return dispatch_unary_op<float>(op, true, src, dst, n, st);
     case DT_F64: return dispatch_unary_op<double>(op, true, src, dst, n, st);
     case DT_BF16: return dispatch_unary_op<bf16_t>(op, true, src, dst, n, st);
+    case DT_F16: return dispatch_unary_op<f16_t>(op, true, src, dst, n, st);
     default: return fail(cudaErrorInvalidValue, "ew_unary: unsupported dtype %d", dt);
     }
 }
@@ -555,6 +568,7 @@ int bee_b200_ew_cast(int src_dt, const void* src, int dst_dt, void* dst, size_t 
     case DT_F32: return cast_from<float>(dst_dt, src, dst, n, st);
     case DT_F64: return cast_from<double>(dst_dt, src, dst, n, st);
     case DT_BF16: return cast_from<bf16_t>(dst_dt, src, dst, n, st);
+    case DT_F16: return cast_from<f16_t>(dst_dt, src, dst, n, st);
     default: return fail(cudaErrorInvalidValue, "ew_cast: unsupported source dtype %d", src_dt);
     }
 }

@@ -48,6 +48,8 @@ struct GemmParams {
     float alpha;
     void* C;
     int c_vec;                 // C, ldc and batch_stride_c allow 16-byte stores
+    int in_f16;                // A and B are f16 (else bf16); sets the MMA's operand format
+    int out_f16;               // 16-bit C is f16 (else bf16)
     // split-K scatter mode: fp32 256x256 partial tiles go to the receive buffer of
     // tile owner (tile % world), slot `rank`, over NVLink peer stores
     float* peer_recv[kMaxPeers];
@@ -108,23 +110,22 @@ __device__ __forceinline__ void store_chunk32(const GemmParams& p, const uint32_
         }
     } else {
         uint16_t* dst = static_cast<uint16_t*>(p.C) + row_off + col0;
+        // 16-bit output: bf16 or f16, both round-to-nearest-even (uniform branch per chunk)
+        auto pack = [&](int j) {
+            const float lo = __uint_as_float(r[j]) * p.alpha, hi = __uint_as_float(r[j + 1]) * p.alpha;
+            return p.out_f16 ? pack_f16x2(lo, hi) : pack_bf16x2(lo, hi);
+        };
         if (col0 + 32 <= p.N && p.c_vec) {
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-                uint4 o;
-                o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * p.alpha, __uint_as_float(r[8 * v + 1]) * p.alpha);
-                o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * p.alpha, __uint_as_float(r[8 * v + 3]) * p.alpha);
-                o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * p.alpha, __uint_as_float(r[8 * v + 5]) * p.alpha);
-                o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * p.alpha, __uint_as_float(r[8 * v + 7]) * p.alpha);
-                reinterpret_cast<uint4*>(dst)[v] = o;
-            }
+            for (int v = 0; v < 4; ++v)
+                reinterpret_cast<uint4*>(dst)[v] = make_uint4(pack(8 * v), pack(8 * v + 2), pack(8 * v + 4), pack(8 * v + 6));
         } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (col0 + j < p.N) {
-                    __nv_bfloat16 h = __float2bfloat16_rn(__uint_as_float(r[j]) * p.alpha);
-                    dst[j] = *reinterpret_cast<uint16_t*>(&h);
-                }
+            for (int j = 0; j < 32; j += 2) {
+                const uint32_t w = pack(j);
+                if (col0 + j < p.N) dst[j] = static_cast<uint16_t>(w & 0xffffu);
+                if (col0 + j + 1 < p.N) dst[j + 1] = static_cast<uint16_t>(w >> 16);
+            }
         }
     }
 }
@@ -226,7 +227,7 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tcgen05_kernel(const __grid_
         __syncwarp();
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
-        constexpr uint32_t idesc = idesc_bf16_f32(128, BN, !B_KMAJOR);
+        const uint32_t idesc = idesc_f16_f32(128, BN, !B_KMAJOR, p.in_f16 != 0);
         int stage = 0;
         uint32_t phase = 0;
         int local = 0;
@@ -439,7 +440,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer (leader CTA only)
         if (leader) {
-            constexpr uint32_t idesc = idesc_bf16_f32(256, 256, !B_KMAJOR);
+            const uint32_t idesc = idesc_f16_f32(256, 256, !B_KMAJOR, p.in_f16 != 0);
             int stage = 0;
             uint32_t phase = 0;
             int local = 0;
@@ -615,16 +616,20 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
 
 template <typename T> struct Acc { using type = T; };
 template <> struct Acc<uint16_t> { using type = float; };  // bf16 bits
+template <> struct Acc<__half> { using type = float; };
 
 template <typename T> __device__ __forceinline__ typename Acc<T>::type ld_as_acc(const T* p) { return *p; }
 template <> __device__ __forceinline__ float ld_as_acc<uint16_t>(const uint16_t* p) {
     return __uint_as_float(static_cast<uint32_t>(*p) << 16);
 }
+template <> __device__ __forceinline__ float ld_as_acc<__half>(const __half* p) { return __half2float(*p); }
 
 template <typename T, typename TO> __device__ __forceinline__ void st_from_acc(TO* p, typename Acc<T>::type v, float alpha) {
     if constexpr (std::is_same_v<TO, uint16_t>) {
         __nv_bfloat16 h = __float2bfloat16_rn(static_cast<float>(v) * alpha);
         *p = *reinterpret_cast<uint16_t*>(&h);
+    } else if constexpr (std::is_same_v<TO, __half>) {
+        *p = __float2half_rn(static_cast<float>(v) * alpha);
     } else if constexpr (std::is_floating_point_v<TO>) {
         *p = static_cast<TO>(v * static_cast<typename Acc<T>::type>(alpha));
     } else {
@@ -721,16 +726,19 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 3-D bf16 tensor map {inner, outer, batch} with 128-byte swizzle.
+// 3-D tensor map of 16-bit elements (bf16, or f16 when `f16`) {inner, outer,
+// batch} with 128-byte swizzle.
 static int make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t batch,
-                    uint64_t row_stride, uint64_t batch_stride, uint32_t box_inner, uint32_t box_outer) {
+                    uint64_t row_stride, uint64_t batch_stride, uint32_t box_inner, uint32_t box_outer,
+                    bool f16 = false) {
     auto enc = encode_fn();
     if (!enc) return fail(cudaErrorNotSupported, "bmm: cuTensorMapEncodeTiled unavailable");
     cuuint64_t dims[3] = {inner, outer, batch};
     cuuint64_t strides[2] = {row_stride * 2, batch_stride * 2};
     cuuint32_t box[3] = {box_inner, box_outer, 1};
     cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+    CUresult r = enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                     const_cast<void*>(ptr), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(cudaErrorInvalidValue, "bmm: tensor map encoding failed (CUresult %d)", int(r));
@@ -776,14 +784,16 @@ static BmmStrides contiguous_strides(size_t M, size_t K, size_t N, int b_trans) 
                       static_cast<long long>(M * K), static_cast<long long>(K * N), static_cast<long long>(M * N)};
 }
 
-// bf16 x bf16 -> (bf16 | fp32) on the tensor cores.  Returns 0, an error, or
-// -1 when the shape or the strides cannot be expressed with TMA (the caller
-// falls back to the SIMT kernel).
+// bf16 x bf16 -> (bf16 | fp32), or f16 x f16 -> (f16 | fp32) when dt_in is
+// F16, on the tensor cores.  Returns 0, an error, or -1 when the shape or the
+// strides cannot be expressed with TMA (the caller falls back to the SIMT kernel).
 // M > 128 and N > 128 use 256x256 tiles on CTA pairs (cta_group::2); smaller
 // problems use 128xBN tiles on single CTAs.  small_tiles: 128x128 tiles on single
 // CTAs whatever the shape (more tiles for outputs that would not fill the GPU).
 static int bmm_bf16_tc(int dt_out, const void* A, const void* B, void* C, size_t batch, size_t M, size_t K, size_t N,
-                       int b_trans, float alpha, const BmmStrides& sd, cudaStream_t st, bool small_tiles = false) {
+                       int b_trans, float alpha, const BmmStrides& sd, cudaStream_t st, bool small_tiles = false,
+                       int dt_in = DT_BF16) {
+    const bool f16 = dt_in == DT_F16;
     // TMA: 16-byte aligned bases, row and batch strides multiples of 16 bytes (8 bf16), positive
     auto ok16 = [](long long v) { return v > 0 && v % 8 == 0 && v < (1ll << 36); };
     if (!ok16(sd.lda) || !ok16(sd.ldb) || !aligned16(A) || !aligned16(B)) return -1;
@@ -794,16 +804,16 @@ static int bmm_bf16_tc(int dt_out, const void* A, const void* B, void* C, size_t
     const int bn = N > 128 && !small_tiles ? 256 : 128;
     const bool pair = N > 128 && M > 128 && !small_tiles;
     CUtensorMap ta, tb;
-    if (make_map(&ta, A, K, M, batch, static_cast<uint64_t>(sd.lda), sa, 64, 128)) return -1;
+    if (make_map(&ta, A, K, M, batch, static_cast<uint64_t>(sd.lda), sa, 64, 128, f16)) return -1;
     if (b_trans) {
         if (make_map(&tb, B, K, N, batch, static_cast<uint64_t>(sd.ldb), sb, 64,
-                     pair ? 128u : static_cast<uint32_t>(bn)))
+                     pair ? 128u : static_cast<uint32_t>(bn), f16))
             return -1;
     } else {
         const uint32_t kbox = pair ? Pair2Cfg::BK : (bn == 256 ? TileCfg<256>::BK : TileCfg<128>::BK);
-        if (make_map(&tb, B, N, K, batch, static_cast<uint64_t>(sd.ldb), sb, 64, kbox)) return -1;
+        if (make_map(&tb, B, N, K, batch, static_cast<uint64_t>(sd.ldb), sb, 64, kbox, f16)) return -1;
     }
-    GemmParams p;
+    GemmParams p{};
     p.M = static_cast<int>(M);
     p.N = static_cast<int>(N);
     p.K = static_cast<int>(K);
@@ -819,6 +829,8 @@ static int bmm_bf16_tc(int dt_out, const void* A, const void* B, void* C, size_t
     p.batch_stride_c = sd.sc;
     p.alpha = alpha;
     p.C = C;
+    p.in_f16 = f16 ? 1 : 0;
+    p.out_f16 = dt_out == DT_F16 ? 1 : 0;
     const bool f32 = dt_out == DT_F32;
     const long long vq = f32 ? 4 : 8;  // elements per 16 bytes
     p.c_vec = aligned16(C) && sd.ldc % vq == 0 && sd.sc % vq == 0 ? 1 : 0;
@@ -1095,6 +1107,14 @@ static int bmm_impl(int dt_in, int dt_out, const void* A, const void* B, void* C
         return dt_out == DT_F32 ? launch_simt<uint16_t, float>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st)
                                 : launch_simt<uint16_t, uint16_t>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st);
     }
+    if (dt_in == DT_F16) {
+        if (dt_out != DT_F16 && dt_out != DT_F32)
+            return fail(cudaErrorInvalidValue, "bmm: f16 input needs an F16 or F32 output, got %d", dt_out);
+        int rc = K == 0 ? -1 : bmm_bf16_tc(dt_out, A, B, C, batch, M, K, N, b_trans, alpha, sd, st, false, DT_F16);
+        if (rc != -1) return rc;
+        return dt_out == DT_F32 ? launch_simt<__half, float>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st)
+                                : launch_simt<__half, __half>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st);
+    }
     if (dt_out != dt_in) return fail(cudaErrorInvalidValue, "bmm: output dtype must equal input dtype for %d", dt_in);
     switch (dt_in) {
     case DT_F32: return launch_simt<float, float>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st);
@@ -1112,7 +1132,7 @@ int bee_b200_bmm(int dt_in, int dt_out, const void* A, const void* B, void* C, s
     if (batch == 0 || M == 0 || N == 0) return ok();
     if (!A || !B || !C) return fail(cudaErrorInvalidValue, "bmm: null pointer");
     cudaStream_t st = as_stream(stream);
-    if (dt_in == DT_BF16 && K == 0 && (dt_out == DT_BF16 || dt_out == DT_F32)) {
+    if ((dt_in == DT_BF16 || dt_in == DT_F16) && K == 0 && (dt_out == dt_in || dt_out == DT_F32)) {
         cudaError_t e = cudaMemsetAsync(C, 0, batch * M * N * (dt_out == DT_F32 ? 4 : 2), st);
         return e == cudaSuccess ? ok() : fail(static_cast<int>(e), "bmm: %s", cudaGetErrorString(e));
     }

@@ -266,11 +266,18 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
            (static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 
-// Instruction descriptor for kind::f16 with bf16 A/B and fp32 D:
-//   bits 4-5 D format (1 = f32), 7-9 A format (1 = bf16), 10-12 B format (1 = bf16),
-//   bit 15 A major (0 = K), bit 16 B major (1 = MN), bits 17-22 N >> 3, bits 24-28 M >> 4.
+// Instruction descriptor for kind::f16 with fp32 D and 16-bit A/B (both bf16
+// or both f16 — one MMA never mixes them):
+//   bits 4-5 D format (1 = f32), 7-9 A format and 10-12 B format (0 = f16,
+//   1 = bf16), bit 15 A major (0 = K), bit 16 B major (1 = MN), bits 17-22
+//   N >> 3, bits 24-28 M >> 4.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n, bool b_mn_major, bool f16_inputs) {
+    return (1u << 4) | ((f16_inputs ? 0u : 1u) << 7) | ((f16_inputs ? 0u : 1u) << 10) |
+           ((b_mn_major ? 1u : 0u) << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t m, uint32_t n, bool b_mn_major) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
+    return idesc_f16_f32(m, n, b_mn_major, false);
 }
 
 }  // namespace sm100

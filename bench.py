@@ -63,6 +63,21 @@ NCU_TRAFFIC = {
 }
 
 
+SWEEP_OPS = ["add_f32", "mul_f32", "cast_f32_bf16", "row_sum_f32", "row_max_f32", "softmax_f32", "sum_i32"]
+
+
+def sweep_config(world: int, peer_exchange: bool = False) -> dict:
+    """The workload both arms report (the reference arm runs the same workload
+    on the host cores)."""
+    return {"workload": "memory-bound op sweep, [8192, 8192] fp32 + int32 per GPU, rows sharded "
+                        "(8192 rows per GPU, global [8192*N, 8192])",
+            "ops": SWEEP_OPS, "bytes_per_step_per_gpu": STEP_BYTES,
+            "l2": "inputs larger than L2 (each tensor 256 MiB > 126 MB), no flush",
+            "parallelism": (f"rows sharded over {world} GPUs; int32 partial sums combined "
+                            + ("inside the reduce kernel over NVLink peer memory" if peer_exchange
+                               else "by an NCCL all-reduce")) if world > 1 else "1 GPU"}
+
+
 def load_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -220,8 +235,19 @@ class Dist:
 
 # ---------------------------------------------------------------- our arm
 
+_INPUTS = {}
+
+
 def make_inputs(rank: int):
-    """Seeded host inputs for one shard (rank r owns rows [8192 r, 8192 (r+1)))."""
+    """Seeded host inputs for one shard (rank r owns rows [8192 r, 8192 (r+1))),
+    generated once per process."""
+    if rank in _INPUTS:
+        return _INPUTS[rank]
+    _INPUTS[rank] = _make_inputs(rank)
+    return _INPUTS[rank]
+
+
+def _make_inputs(rank: int):
     rng = np.random.default_rng(1_000 + rank)
     x = rng.standard_normal((ROWS, COLS), dtype=np.float32)
     y = rng.standard_normal((ROWS, COLS), dtype=np.float32)
@@ -438,13 +464,7 @@ def run_ours(args, d: Dist):
             "value": round(value, 1), "unit": "GB/s", "n_gpus": d.world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded N(0,1) fp32, uniform int32 in [-1000, 1000])",
-            "config": {"workload": "memory-bound op sweep, [8192, 8192] fp32 + int32 per GPU, rows sharded "
-                                   "(8192 rows per GPU, global [8192*N, 8192])",
-                       "ops": [n for n, _ in ops], "bytes_per_step_per_gpu": STEP_BYTES,
-                       "l2": "inputs larger than L2 (each tensor 256 MiB > 126 MB), no flush",
-                       "parallelism": (f"rows sharded over {d.world} GPUs; int32 partial sums combined "
-                                       + ("inside the reduce kernel over NVLink peer memory" if peer is not None
-                                          else "by an NCCL all-reduce")) if d.world > 1 else "1 GPU"},
+            "config": sweep_config(d.world, peer is not None),
             "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(dom_gbs, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(dom_gbs / peaks["hbm_gbs"], 3),
                          "peak_source": peaks["source"], "algorithmic_bytes": OP_BYTES[dominant],
@@ -478,6 +498,7 @@ def run_extras(args, d, dev, stream, peaks):
       [16 x 2048, 4096] bf16 viewed [16, 2048, 32, 128], fused, per GPU (weak);
     * attention_bf16: S = Q.K^T/sqrt(128) (fp32), P = softmax(S) (bf16),
       O = P.V for 32 heads x [2048, 128] per GPU (heads sharded, weak);
+    * gemm_f16_8192: the gemm_bf16_8192 product with f16 inputs and output;
     * gemm_f32_1024: the fp32 parity config, 1024^3.
     """
     import torch
@@ -650,7 +671,7 @@ def run_extras(args, d, dev, stream, peaks):
                                                        "kernels": "bmm (QK^T, fp32 out) -> softmax fp32->bf16 -> bmm (PV)"},
                                      "scaling": "weak (heads sharded)", "status_ok": status_ok()}
             del q, k, v, S, P, o
-        if want("gemm_bf16_8192", "gemm_bf16_8192_splitk"):
+        if want("gemm_bf16_8192", "gemm_bf16_8192_splitk", "gemm_f16_8192"):
             n = 8192
             std = (1.0 / np.sqrt(n)) ** 0.5  # N(0, variance 1/sqrt(8192))
             a = (torch.randn(n, n, device=dev, generator=g) * std).to(torch.bfloat16)
@@ -665,6 +686,17 @@ def run_extras(args, d, dev, stream, peaks):
                                      "frac_of_measured_bf16_sustained": round(tf / d.world / peaks["bf16_tflops_sustained"], 3),
                                      "frac_of_spec_2250": round(tf / d.world / 2250.0, 3),
                                      "scaling": "weak (column shards)", "status_ok": status_ok()}
+            if want("gemm_f16_8192"):
+                # the same product with f16 A and B (f16 out): the tensor cores' f16 operand format
+                a16, b16 = a.to(torch.float16), b.to(torch.float16)
+                c16 = torch.empty(n, n, device=dev, dtype=torch.float16)
+                ms16 = timed(lambda: call("bee_b200_bmm", _capi.F16, _capi.F16, a16.data_ptr(), b16.data_ptr(),
+                                          c16.data_ptr(), 1, n, n, n, 0, 1.0, st), label="gemm_f16_8192")
+                tf16 = d.world * flop / (ms16 / 1e3) / 1e12
+                out["gemm_f16_8192"] = {"ms": round(ms16, 4), "TFLOP/s": round(tf16, 1), "unit": "TFLOP/s",
+                                        "frac_of_measured_bf16_burst": round(tf16 / d.world / peaks["bf16_tflops"], 3),
+                                        "scaling": "weak (column shards)", "status_ok": status_ok()}
+                del a16, b16, c16
 
             # split-K: rank r multiplies A[:, K_r] by B[K_r, :]
             klo, khi = shard_range(n, d.world, d.rank)
@@ -794,13 +826,10 @@ def cpu_sweep(sample_rows: int, reps: int = 1):
     times = {}
     if reference_available():
         ref = Reference()
-        kind, cores = "reference", ref.threads()
-        times["add_f32"] = ref.binary_f32(0, xs, ys, reps)[1]
-        times["mul_f32"] = ref.binary_f32(2, xs, ys, reps)[1]
-        times["row_sum_f32"] = ref.reduce_rows_f32(0, xs, reps)[1]
-        times["row_max_f32"] = ref.reduce_rows_f32(2, xs, reps)[1]
-        times["softmax_f32"] = ref.softmax_f32(xs, reps)[1]
-        times["sum_i32"] = ref.reduce_global_i32(0, xis, reps)[1]
+        kind, cores, isa = "reference", ref.threads(), ref.isa()
+        xs, ys, xis = (np.ascontiguousarray(v) for v in (xs, ys, xis))
+        _INPUTS[("ref", sample_rows)] = (xs, ys, xis)  # kept alive: the reference caches its Tensors by address
+        times.update(ref.sweep(xs, ys, xis)[1])
         # the reference's CPU cast to BF16 writes nothing (CastCpu.hpp:348): time the restatement
         orc = Oracle()
         t = time.perf_counter()
@@ -808,7 +837,7 @@ def cpu_sweep(sample_rows: int, reps: int = 1):
         times["cast_f32_bf16"] = time.perf_counter() - t
     else:
         orc = Oracle()
-        kind, cores = "port", 1
+        kind, cores, isa = "port", 1, "scalar C (oracle port)"
 
         def tm(fn):
             t = time.perf_counter()
@@ -823,7 +852,7 @@ def cpu_sweep(sample_rows: int, reps: int = 1):
         times["sum_i32"] = tm(lambda: orc.reduce_global_i32(0, xis))
     total_t = sum(times.values())
     gbs = STEP_BYTES * scale / total_t / 1e9
-    info = {"kind": kind, "cores": cores,
+    info = {"kind": kind, "cores": cores, "isa": isa,
             "sample": f"[{sample_rows}, {COLS}] rows of the [8192, 8192] shard per op ({n} elements), "
                       f"all 7 ops; bf16 cast timed on the oracle restatement (the reference's CPU cast to BF16 "
                       f"is a no-op)" if kind == "reference" else f"[{sample_rows}, {COLS}] sample, oracle port",
@@ -853,9 +882,7 @@ def run_reference(args, d: Dist):
         "warmup": args.warmup, "ms_per_step": round(wall / max(args.steps, 1) * 1e3, 2), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1) fp32, uniform int32 in [-1000, 1000])",
-        "config": {"workload": "memory-bound op sweep, [8192, 8192] fp32 + int32 per GPU, rows sharded "
-                               "(8192 rows per GPU, global [8192*N, 8192])",
-                   "sample_rows_per_step": sample_rows},
+        "config": sweep_config(d.world, args.exchange == "peer"),
         "cpu_baseline": cb,
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -868,7 +895,9 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["sweep"], default="sweep")
-    ap.add_argument("--ref-rows", type=int, default=2048, help="rows per CPU-baseline sample")
+    ap.add_argument("--ref-rows", type=int, default=ROWS,
+                    help="rows of the [8192, 8192] shard per CPU step (default: the whole shard)")
+    ap.add_argument("--cpu-reps", type=int, default=8, help="CPU-baseline steps timed in the GPU arm (rank 0, N=1)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the GEMM / RMSNorm+RoPE / attention configs")
@@ -904,9 +933,12 @@ def main(argv=None):
     try:
         out = run_ours(args, d)
         if out is not None and not args.no_cpu_baseline and d.world == 1:
-            gbs, info = cpu_sweep(args.ref_rows)
-            cb = dict(info)
-            cb.update({"value": round(gbs, 3), "unit": "GB/s"})
+            cpu_sweep(args.ref_rows)  # warm-up (thread pool, first touch)
+            runs = [cpu_sweep(args.ref_rows) for _ in range(max(args.cpu_reps, 1))]
+            gbs = statistics.median(g for g, _ in runs)
+            cb = dict(runs[-1][1])
+            cb.update({"value": round(gbs, 3), "unit": "GB/s", "steps": len(runs),
+                       "statistic": "median over the steps"})
             out["cpu_baseline"] = cb
         if out is not None:
             print(json.dumps(out), flush=True)

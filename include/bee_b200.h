@@ -80,8 +80,8 @@ BEE_B200_API int bee_b200_device_count(int* count);
 /* ------------------------------------------------------------- elementwise */
 
 /* out[i] = a[i] (op) b[i] over n contiguous elements of dtype dt.
- * dt in {U8, I32, I64, F32, F64, BF16}; BF16 computes in fp32 and rounds to
- * nearest even.  Replaces ops_binary (Bee/CUDA/Ops/OpsBridge.hpp:27) behind
+ * dt in {U8, I32, I64, F32, F64, F16, BF16}; F16 and BF16 compute in fp32 and
+ * round to nearest even.  Replaces ops_binary (Bee/CUDA/Ops/OpsBridge.hpp:27) behind
  * tensor::cuda::ew_binary (Bee/Tensor/Cuda/Backend.hpp:51). */
 BEE_B200_API int bee_b200_ew_binary(int op, int dt, const void* a, const void* b, void* out, size_t n,
                        bee_b200_stream_t stream);
@@ -97,16 +97,17 @@ BEE_B200_API int bee_b200_ew_binary_strided(int op, int dt, int ndim, const int6
                                             void* out, bee_b200_stream_t stream);
 
 
-/* dst[i] = op(src[i]).  Neg/Abs: I32, I64, F32, F64, BF16; Sqrt/Exp/Log: F32,
- * F64, BF16.  Replaces ops_unary (Bee/CUDA/Ops/OpsBridge.hpp:28) behind
+/* dst[i] = op(src[i]).  Neg/Abs: I32, I64, F32, F64, F16, BF16; Sqrt/Exp/Log:
+ * F32, F64, F16, BF16.  Replaces ops_unary (Bee/CUDA/Ops/OpsBridge.hpp:28) behind
  * tensor::cuda::ew_unary (Bee/Tensor/Cuda/Backend.hpp:54). */
 BEE_B200_API int bee_b200_ew_unary(int op, int dt, const void* src, void* dst, size_t n, bee_b200_stream_t stream);
 
-/* dst[i] = cast(src[i]) between Bool, U8, I32, I64, F32, F64 and BF16.
- * F32->BF16 rounds to nearest even (NaN stays NaN); ->Bool is (x != 0);
+/* dst[i] = cast(src[i]) between Bool, U8, I32, I64, F32, F64, F16 and BF16.
+ * ->BF16 and ->F16 round to nearest even (F64->F16 in one rounding; NaN stays
+ * NaN; beyond F16's range is +-inf); ->Bool is (x != 0);
  * float->int truncates toward zero like static_cast.  Replaces ops_cast
  * (Bee/CUDA/Ops/OpsBridge.hpp:29) behind tensor::cuda::ew_cast
- * (Bee/Tensor/Cuda/Backend.hpp:57), which has no BF16 case
+ * (Bee/Tensor/Cuda/Backend.hpp:57), which has no BF16 or F16 case
  * (Bee/CUDA/Ops/Cast.cu:96-104). */
 BEE_B200_API int bee_b200_ew_cast(int src_dt, const void* src, int dst_dt, void* dst, size_t n,
                      bee_b200_stream_t stream);
@@ -223,7 +224,8 @@ BEE_B200_API int bee_b200_rms_norm_rope(int dt, const void* x, const void* w, vo
 /* ------------------------------------------------------------------ matmul */
 
 /* C[M,N] = A[M,K] . B[K,N], row-major contiguous, same dtype.
- * BF16: tcgen05 tensor cores with fp32 accumulation and a bf16 (RNE) result;
+ * BF16 / F16: tcgen05 tensor cores with fp32 accumulation and a bf16 / f16
+ * (RNE) result (F16 outputs beyond its range are +-inf);
  * F32 from 2^28 multiply-adds up (K and N multiples of 8, 16-byte aligned
  * buffers): every value split into three bf16 pieces, six piece products on
  * the same tensor cores with fp32 accumulation (fp32-level error; rows and
@@ -241,7 +243,7 @@ BEE_B200_API int bee_b200_matmul(int dt, const void* A, const void* B, void* C, 
 /* Batched C[b] = alpha * A[b] . op(B[b]) over `batch` contiguous matrices:
  * A [batch, M, K]; B [batch, K, N], or [batch, N, K] when b_trans != 0 (so
  * Q.K^T reads K as stored); C [batch, M, N].  dt_in BF16 with dt_out BF16 or
- * F32 runs on the tensor cores (TMA needs K % 8 == 0, N % 8 == 0 unless
+ * F32, and dt_in F16 with dt_out F16 or F32, run on the tensor cores (TMA needs K % 8 == 0, N % 8 == 0 unless
  * b_trans, 16-byte aligned A and B; other shapes use the SIMT kernel); other
  * dtypes need dt_out == dt_in.  New: the reference matmul is 2-D only
  * (Bee/Tensor/Ops/Matmul.cpp:63-64). */
@@ -253,7 +255,7 @@ BEE_B200_API int bee_b200_bmm(int dt_in, int dt_out, const void* A, const void* 
  * B + b*stride_b + k*ldb + n (b_trans: B[b][n][k] at B + b*stride_b + n*ldb + k);
  * C[b][m][n] at C + b*stride_c + m*ldc + n.  Leading dimensions at least a row;
  * batch strides >= 0 (0 repeats an operand for every batch), output batches
- * must not overlap.  bf16 inputs take the tensor cores when lda, ldb and the
+ * must not overlap.  bf16 and f16 inputs take the tensor cores when lda, ldb and the
  * input batch strides are positive multiples of 8 elements and A, B are 16-byte
  * aligned, else the SIMT kernel (same results up to accumulation order).
  * New: the reference's matmul is 2-D and contiguous only. */

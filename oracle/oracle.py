@@ -56,6 +56,31 @@ def bf16_round(x: np.ndarray) -> np.ndarray:
     return bf16_bits_to_f32(f32_to_bf16_bits(x))
 
 
+# ------------------------------------------------------------------ f16 helpers
+# IEEE binary16 with round-to-nearest-even, the definition the f16 paths are
+# pinned to (the reference stores F16 but computes nothing in it,
+# Bee/Tensor/Core/DType.hpp:10-15).
+
+def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(x, dtype=np.float32).astype(np.float16).view(np.uint16)
+
+
+def f16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(b, dtype=np.uint16).view(np.float16).astype(np.float32)
+
+
+def matmul_exact(a: np.ndarray, b: np.ndarray, b_trans: bool = False, alpha: float = 1.0) -> np.ndarray:
+    """alpha * A.op(B) in float64 for batched [batch, M, K] x [batch, K, N]
+    operands (op(B) = B^T of [batch, N, K] when b_trans): the exact product of
+    16-bit inputs to within float64 rounding, which an fp32-accumulating kernel
+    must match within its tolerance."""
+    a64 = np.asarray(a, np.float64)
+    b64 = np.asarray(b, np.float64)
+    if b_trans:
+        b64 = np.swapaxes(b64, -1, -2)
+    return alpha * (a64 @ b64)
+
+
 class Oracle:
     """Our C restatement of the reference algorithms (see oracle/bee_oracle.c)."""
 
@@ -203,6 +228,7 @@ class Reference:
         self.lib = ctypes.CDLL(str(REF_SO))
         L = self.lib
         L.bref_threads.restype = _i
+        L.bref_isa.restype = ctypes.c_char_p
         for name, args in {
             "bref_matmul_f32": [_vp, _vp, _vp, _i64, _i64, _i64, _i],
             "bref_binary_f32": [_i, _vp, _vp, _vp, _i64, _i64, _i],
@@ -216,6 +242,7 @@ class Reference:
             "bref_view_copy_f32": [_vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i],
             "bref_binary_bcast_f32": [_i, _vp, _vp, _vp, _vp, _i, _vp, _i],
             "bref_mean_int": [_i, _vp, _i64, _i64, _i64, _i, _vp, _i],
+            "bref_sweep": [_vp, _vp, _vp, _i64, _i64, _vp],
         }.items():
             fn = getattr(L, name)
             fn.argtypes = args
@@ -229,6 +256,20 @@ class Reference:
 
     def threads(self) -> int:
         return int(self.lib.bref_threads())
+
+    def sweep(self, x, y, xi):
+        """One timed step of the memory-bound sweep (add, mul, row sum, row max,
+        row softmax, int32 sum) on the reference's CPU path; the arrays must stay
+        alive between calls (their Tensors are cached by address)."""
+        rows, cols = x.shape
+        t = np.zeros(6, np.float64)
+        tot = self._chk(self.lib.bref_sweep(_p(x), _p(y), _p(xi), rows, cols, _p(t)), "sweep")
+        names = ["add_f32", "mul_f32", "row_sum_f32", "row_max_f32", "softmax_f32", "sum_i32"]
+        return tot, dict(zip(names, map(float, t)))
+
+    def isa(self) -> str:
+        """bee::simd::isa_name(bee::simd::current_isa()) on this host."""
+        return self.lib.bref_isa().decode()
 
     def matmul_f32(self, a, b, reps=1):
         a = np.ascontiguousarray(a, np.float32)

@@ -18,6 +18,7 @@
 #include <thread>
 #include <vector>
 
+#include "SIMD/Detect.hpp"
 #include "Tensor/Tensor.hpp"
 
 using namespace bee;
@@ -82,6 +83,10 @@ extern "C" {
 
 int bref_threads(void) { return static_cast<int>(std::thread::hardware_concurrency()); }
 
+// The SIMD level the reference's runtime dispatch picked on this host
+// (Bee/SIMD/Detect.hpp:18-28).
+const char* bref_isa(void) { return bee::simd::isa_name(bee::simd::current_isa()); }
+
 double bref_matmul_f32(const float* a, const float* b, float* c, int64_t m, int64_t k, int64_t n, int reps) {
     Tensor A = make({m, k}, DType::F32, a), B = make({k, n}, DType::F32, b);
     Tensor C;
@@ -93,6 +98,41 @@ double bref_matmul_f32(const float* a, const float* b, float* c, int64_t m, int6
     });
     if (t >= 0) copy_out(C, c);
     return t;
+}
+
+// One step of the memory-bound sweep on the reference's CPU path: add, mul,
+// row sum, row max, row softmax (the composition of public ops above) and the
+// int32 full sum of [rows, cols] inputs.  The input Tensors are built on the
+// first call for these pointers and kept, so a step times only the ops;
+// seconds per op go to times[0..5] in that order; returns their total, or -1.
+double bref_sweep(const float* x, const float* y, const int32_t* xi, int64_t rows, int64_t cols, double* times) {
+    static const void* key[3] = {nullptr, nullptr, nullptr};
+    static int64_t key_rows = -1, key_cols = -1;
+    static Tensor X, Y, XI;
+    if (key[0] != x || key[1] != y || key[2] != xi || key_rows != rows || key_cols != cols) {
+        X = make({rows, cols}, DType::F32, x);
+        Y = make({rows, cols}, DType::F32, y);
+        XI = make({rows * cols}, DType::I32, xi);
+        key[0] = x, key[1] = y, key[2] = xi, key_rows = rows, key_cols = cols;
+    }
+    auto clock = [](auto&& f) {
+        auto t0 = std::chrono::steady_clock::now();
+        const bool ok = f();
+        auto t1 = std::chrono::steady_clock::now();
+        return ok ? std::chrono::duration<double>(t1 - t0).count() : -1.0;
+    };
+    times[0] = clock([&] { return okr(add(X, Y), "add"); });
+    times[1] = clock([&] { return okr(mul(X, Y), "mul"); });
+    times[2] = clock([&] { return okr(sum(X, 1), "row sum"); });
+    times[3] = clock([&] { return okr(max(X, 1), "row max"); });
+    times[4] = clock([&] { return okr(softmax_rows(X), "softmax"); });
+    times[5] = clock([&] { return okr(sum(XI), "int32 sum"); });
+    double total = 0;
+    for (int i = 0; i < 6; ++i) {
+        if (times[i] < 0) return -1.0;
+        total += times[i];
+    }
+    return total;
 }
 
 // op: 0 add, 1 sub, 2 mul, 3 div (same-shape fp32)

@@ -35,7 +35,11 @@ def test_reference_arm_prints_one_contract_line():
     assert d["impl"] == "reference" and d["unit"] == "GB/s" and d["n_gpus"] == 1
     assert d["higher_is_better"] is True and d["value"] > 0
     assert "workload" in d["config"]
+    sys.path.insert(0, str(ROOT))
+    import bench
+    assert d["config"] == bench.sweep_config(1)  # the GPU arm reports the same config at N=1
     cb = d["cpu_baseline"]
+    assert cb["isa"]
     assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
