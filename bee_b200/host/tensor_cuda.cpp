@@ -189,3 +189,13 @@ auto rms_norm_rope(int dt, const void* x, const void* w, void* y, std::size_t ro
 }
 
 }  // namespace bee_b200::tensor_cuda
+
+namespace bee_b200::tensor_cuda {
+
+auto attention(int dt, const void* q, const void* k, const void* v, void* o, std::size_t heads, std::size_t seq,
+               std::size_t head_dim, float scale) -> Result<void> {
+    return finish(bee_b200_attention(dt, q, k, v, o, heads, seq, head_dim, scale, per_thread_stream()),
+                  "cuda::ops::attention");
+}
+
+}  // namespace bee_b200::tensor_cuda

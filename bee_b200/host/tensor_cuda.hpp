@@ -95,4 +95,8 @@ auto deallocate(void* p, std::size_t nbytes, std::size_t alignment) -> void;
                                  std::size_t heads, std::size_t head_dim, float eps, double theta,
                                  std::size_t pos_offset) -> Result<void>;
 
+// fused O = softmax(scale * Q K^T) V per head: q, k, v, o [heads, seq, head_dim] bf16
+[[nodiscard]] auto attention(int dt, const void* q, const void* k, const void* v, void* o, std::size_t heads,
+                             std::size_t seq, std::size_t head_dim, float scale) -> Result<void>;
+
 }  // namespace bee_b200::tensor_cuda

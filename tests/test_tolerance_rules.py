@@ -50,10 +50,15 @@ def test_attention_bound_rejects_a_few_percent():
     p /= p.sum(-1, keepdims=True)
     o = p @ v
     assert_output_close(_bf16(o.astype(np.float32)), o, 1e-2, what="bf16-rounded output")
-    with pytest.raises(AssertionError):
-        assert_output_close(o * 1.03, o, 1e-2, what="3% off")
+    for off in (1.015, 1.03):  # a uniformly wrong output fails the norm-wise bound
+        with pytest.raises(AssertionError):
+            assert_output_close(o * off, o, 1e-2, what=f"{off - 1:.1%} off", elementwise_rtol=2e-2)
     # what a bf16 tensor-core kernel does: P = exp(s - max) rounded to bf16 before
-    # P.V, the row sum l in fp32, the output rounded to bf16 -- inside the bound
+    # P.V, the row sum l in fp32, the output rounded to bf16 -- inside the bound,
+    # but single entries come within ~20% of 1e-2 of rms(O), hence the attention
+    # tests' element-wise bound of 2e-2 beside the norm-wise 1e-2
     pb = _bf16(np.exp(s).astype(np.float32)).astype(np.float64)
     l = np.exp(s).sum(-1, keepdims=True)
-    assert_output_close(_bf16(((pb @ v) / l).astype(np.float32)), o, 1e-2, what="bf16 P")
+    got = _bf16(((pb @ v) / l).astype(np.float32))
+    assert output_err(got, o) > 5e-3
+    assert_output_close(got, o, 1e-2, what="bf16 P", elementwise_rtol=2e-2)
