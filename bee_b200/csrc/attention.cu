@@ -74,26 +74,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
     return d;
 }
 
-// Packed fp32 pairs: one instruction computes both lanes of a .f32x2 register pair.
-__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
-    uint64_t d;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
-    return d;
-}
-__device__ __forceinline__ void unpack_f32x2(uint64_t v, float& lo, float& hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-
 // Maximum of 128 values as a tree of three-input maxima (depth 5 rather than a
 // chain of 127 dependent two-input maxima).
 __device__ __forceinline__ float row_max128(const uint32_t (&s)[128]) {

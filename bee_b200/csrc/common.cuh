@@ -114,4 +114,38 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Packed fp32 pairs (sm_100 .f32x2): one instruction computes both lanes of a
+// 64-bit register pair.
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+__device__ __forceinline__ void unpack_f32x2(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// A bf16x2 word as an fp32 pair (exact).
+__device__ __forceinline__ uint64_t bf16x2_to_f32x2(uint32_t w) { return pack_f32x2(bf16_lo(w), bf16_hi(w)); }
+// An fp32 pair rounded to a bf16x2 word (nearest even).
+__device__ __forceinline__ uint32_t f32x2_to_bf16x2(uint64_t v) {
+    float lo, hi;
+    unpack_f32x2(v, lo, hi);
+    return pack_bf16x2(lo, hi);
+}
+
 }  // namespace bee_b200

@@ -66,12 +66,13 @@ __global__ void __launch_bounds__(256) transpose_tile_kernel(const uint8_t* __re
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const long long tp = (P + TP - 1) / TP, tq = (Q + TQ - 1) / TQ;
     const long long tiles = batch * tp * tq;
-    for (long long t = blockIdx.x; t < tiles; t += gridDim.x) {
+    // the 16-byte loads of tile t (registers), issued a tile ahead so that they
+    // overlap the shared-memory transpose and the stores of the previous tile
+    auto load = [&](long long t, uint4 (&w)[ITERS]) {
         const long long b = t / (tp * tq);
         const long long rem = t - b * tp * tq;
         const long long q0 = (rem / tp) * TQ, p0 = (rem % tp) * TP;
         const T* sbase = s + b * sb;
-        uint4 w[ITERS];
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
             const int slot = it * 8 + warp;  // 4 rows x 8 vectors
@@ -79,6 +80,14 @@ __global__ void __launch_bounds__(256) transpose_tile_kernel(const uint8_t* __re
             const long long q = q0 + qq, p = p0 + pv * VEC;
             if (q < Q && src_vec && p + VEC <= P) w[it] = __ldcs(reinterpret_cast<const uint4*>(sbase + q * ld + p));
         }
+    };
+    uint4 w[ITERS];
+    if (static_cast<long long>(blockIdx.x) < tiles) load(blockIdx.x, w);
+    for (long long t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const long long b = t / (tp * tq);
+        const long long rem = t - b * tp * tq;
+        const long long q0 = (rem / tp) * TQ, p0 = (rem % tp) * TP;
+        const T* sbase = s + b * sb;
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
             const int slot = it * 8 + warp;
@@ -96,6 +105,7 @@ __global__ void __launch_bounds__(256) transpose_tile_kernel(const uint8_t* __re
             }
         }
         __syncthreads();
+        if (t + gridDim.x < tiles) load(t + gridDim.x, w);  // w is free again: its values are in the tile
         T* dbase = d + b * P * Q;
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
