@@ -392,7 +392,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         int stage = 0;
         uint32_t phase = 0;
         long long issued = 0;
-        const uint64_t pol_a = l2_policy_evict_last();
         for (int tile = pair; tile < p.total_tiles; tile += npairs) {
             if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
             int b, mb, nb;
@@ -410,10 +409,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
                     const int m0 = mb * Cfg::BM + static_cast<int>(rank) * 128;
                     const int n0 = nb * Cfg::BN + static_cast<int>(rank) * 128;
                     const int k0 = kb * Cfg::BK;
-                    // A panels are revisited by the next waves of the grouped raster
-                    // (same M-blocks, next columns): keep them in L2
-                    tma_load_3d_pair_hint(sa, &tmA, full_leader, k0, m0, b, pol_a);
-                    tma_load_3d_pair_hint(sa + Cfg::A_HALF, &tmA, full_leader, k0 + 64, m0, b, pol_a);
+                    tma_load_3d_pair(sa, &tmA, full_leader, k0, m0, b);
+                    tma_load_3d_pair(sa + Cfg::A_HALF, &tmA, full_leader, k0 + 64, m0, b);
                     if constexpr (B_KMAJOR) {
                         tma_load_3d_pair(sb, &tmB, full_leader, k0, n0, b);
                         tma_load_3d_pair(sb + Cfg::A_HALF, &tmB, full_leader, k0 + 64, n0, b);

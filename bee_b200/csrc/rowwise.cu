@@ -432,37 +432,16 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) norm_rope_pipe_kernel
         const float* sinj = sin_t + parity * half;
         float ss = 0.f;
         if (NORM) {
-            if constexpr (E == 8) {
-                // bf16: sum of squares in packed fp32 pairs
-                uint64_t ss2 = 0ull;
 #pragma unroll
-                for (int u = 0; u < NP; ++u)
+            for (int u = 0; u < NP; ++u)
 #pragma unroll
-                    for (int q = 0; q < CPU; ++q)
-                        if (live[u]) {
-                            const uint4 v = row[cidx[u][q]];
-                            const uint32_t wds[4] = {v.x, v.y, v.z, v.w};
+                for (int q = 0; q < CPU; ++q)
+                    if (live[u]) {
+                        float t[E];
+                        CK::unpack(row[cidx[u][q]], t);
 #pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                const uint64_t t2 = bf16x2_to_f32x2(wds[k]);
-                                ss2 = fma_f32x2(t2, t2, ss2);
-                            }
-                        }
-                float lo, hi;
-                unpack_f32x2(ss2, lo, hi);
-                ss = lo + hi;
-            } else {
-#pragma unroll
-                for (int u = 0; u < NP; ++u)
-#pragma unroll
-                    for (int q = 0; q < CPU; ++q)
-                        if (live[u]) {
-                            float t[E];
-                            CK::unpack(row[cidx[u][q]], t);
-#pragma unroll
-                            for (int k = 0; k < E; ++k) ss = fmaf(t[k], t[k], ss);
-                        }
-            }
+                        for (int k = 0; k < E; ++k) ss = fmaf(t[k], t[k], ss);
+                    }
         }
         float inv = 1.0f;
         if (NORM) {
@@ -475,34 +454,7 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) norm_rope_pipe_kernel
 #pragma unroll
         for (int u = 0; u < NP; ++u) {
             if (!live[u]) continue;
-            if constexpr (ROPE && E == 8) {
-                // bf16: the rotation in packed fp32 pairs (k, k+1) of both halves;
-                // out_a = a*c - b*s, out_b = b*c + a*s with c, s scaled by 1/rms
-                const uint4 ra = row[cidx[u][0]], rb = row[cidx[u][1]];
-                const uint32_t wa4[4] = {ra.x, ra.y, ra.z, ra.w}, wb4[4] = {rb.x, rb.y, rb.z, rb.w};
-                // weights from L1 (8 KiB shared by the SM's CTAs) rather than 16 registers
-                const uint4 gwa = NORM ? __ldg(reinterpret_cast<const uint4*>(w) + cidx[u][0]) : make_uint4(0, 0, 0, 0);
-                const uint4 gwb = NORM ? __ldg(reinterpret_cast<const uint4*>(w) + cidx[u][1]) : make_uint4(0, 0, 0, 0);
-                const uint32_t ga4[4] = {gwa.x, gwa.y, gwa.z, gwa.w}, gb4[4] = {gwb.x, gwb.y, gwb.z, gwb.w};
-                const uint64_t inv2 = pack_f32x2(inv, inv), ninv2 = pack_f32x2(-inv, -inv);
-                uint32_t oa[4], ob[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    uint64_t A = bf16x2_to_f32x2(wa4[i]), Bv = bf16x2_to_f32x2(wb4[i]);
-                    if (NORM) {
-                        A = mul_f32x2(A, bf16x2_to_f32x2(ga4[i]));
-                        Bv = mul_f32x2(Bv, bf16x2_to_f32x2(gb4[i]));
-                    }
-                    const float2 c2 = *reinterpret_cast<const float2*>(cosj + toff[u] + 2 * i);
-                    const float2 s2 = *reinterpret_cast<const float2*>(sinj + toff[u] + 2 * i);
-                    const uint64_t cpk = pack_f32x2(c2.x, c2.y), spk = pack_f32x2(s2.x, s2.y);
-                    const uint64_t cv = mul_f32x2(cpk, inv2), sv = mul_f32x2(spk, inv2), nsv = mul_f32x2(spk, ninv2);
-                    oa[i] = f32x2_to_bf16x2(fma_f32x2(A, cv, mul_f32x2(Bv, nsv)));
-                    ob[i] = f32x2_to_bf16x2(fma_f32x2(Bv, cv, mul_f32x2(A, sv)));
-                }
-                __stcs(dst + cidx[u][0], make_uint4(oa[0], oa[1], oa[2], oa[3]));
-                __stcs(dst + cidx[u][1], make_uint4(ob[0], ob[1], ob[2], ob[3]));
-            } else if (ROPE) {
+            if (ROPE) {
                 float a[E], b[E];
                 CK::unpack(row[cidx[u][0]], a);
                 CK::unpack(row[cidx[u][1]], b);

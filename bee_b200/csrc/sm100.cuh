@@ -221,24 +221,6 @@ __device__ __forceinline__ void tma_load_3d_pair(void* dst, const void* tmap, ui
         : "memory");
 }
 
-// L2 eviction-priority policy for every access that carries it: evict_last
-// keeps a reused operand resident across waves of tiles.
-__device__ __forceinline__ uint64_t l2_policy_evict_last() {
-    uint64_t pol;
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
-    return pol;
-}
-
-// tma_load_3d_pair with an L2 cache-policy hint (from createpolicy).
-__device__ __forceinline__ void tma_load_3d_pair_hint(void* dst, const void* tmap, uint32_t bar_cluster, int x, int y,
-                                                      int z, uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
-        "[%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z), "l"(policy)
-        : "memory");
-}
-
 template <uint32_t NCOLS> __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
                  "r"(NCOLS)

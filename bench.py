@@ -422,8 +422,8 @@ def run_ours(args, d: Dist):
     e2e = None
     if not args.no_e2e:
         slot[0] = ring.numel() - 1  # a slot of its own, exchanged on the compute stream
-        e2e = run_e2e(args, d, lib, dev, stream, hx, hy, hxi, ops, lambda: allreduce_isum(overlap=False),
-                      [o_add, o_mul, o_bf, o_rsum, o_rmax, o_sm, ring[slot[0]:slot[0] + 1]], [dx, dy, dxi])
+        e2e = run_e2e(args, d, dev, stream, hx, hy, hxi, [dx, dy, dxi],
+                      [o_add, o_mul, o_bf, o_rsum, o_rmax, o_sm, ring[slot[0]:slot[0] + 1]])
 
     clocks = clk.summary()
     probe_stream.synchronize()
@@ -758,59 +758,108 @@ def run_extras(args, d, dev, stream, peaks):
     return out
 
 
-def run_e2e(args, d, lib, dev, stream, hx, hy, hxi, ops, allreduce_isum, outs, dins):
+def run_e2e(args, d, dev, stream, hx, hy, hxi, dins, outs):
     """Same sweep through the C ABI with host buffers: every step copies the
     inputs host->device (pinned), runs the ops and copies every output back.
 
-    The copies go on two copy streams so that PCIe carries both directions at
-    once, as a caller streaming batches would arrange it: the upload of step
-    k+1's inputs (after step k's ops have read theirs) overlaps the download of
-    step k's outputs, and step k+1's ops start once both are done.  The timed
-    region ends when the last step's outputs are in host memory."""
+    Two device buffer sets (inputs and outputs) alternate between steps, as a
+    caller streaming batches would arrange it, and the copies go on two copy
+    streams, so PCIe carries both directions for the whole step: the upload of
+    step k+1's inputs and the download of step k's outputs run together, and
+    step k+1's kernels need only their own upload (the download reading the
+    other buffer set).  A buffer set is reused only after its download and its
+    kernels are done.  The timed region ends when the last step's outputs are
+    in host memory."""
     import torch
+    from bee_b200 import _capi
     from bee_b200._capi import call
     st = stream.cuda_stream
-    h_outs = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+    F32, BF16, I32 = _capi.F32, _capi.BF16, _capi.I32
+    sets = [(list(dins), list(outs)), ([torch.empty_like(t) for t in dins], [torch.empty_like(t) for t in outs])]
+    h_outs = [[torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs] for _ in range(2)]
     h_ins = [hx, hy, hxi]
     h2d = sum(t.numel() * t.element_size() for t in h_ins)
-    d2h = sum(t.numel() * t.element_size() for t in h_outs)
-    up, down = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    ev_up, ev_ops, ev_down = (torch.cuda.Event() for _ in range(3))
+    d2h = sum(t.numel() * t.element_size() for t in h_outs[0])
 
-    def e2e_step():
-        up.wait_event(ev_ops)  # the previous step's ops have read their inputs
-        for h, dd in zip(h_ins, dins):
+    def run_ops(k):
+        (dx, dy, dxi), (o_add, o_mul, o_bf, o_rsum, o_rmax, o_sm, o_isum) = sets[k]
+        call("bee_b200_ew_binary", 0, F32, dx.data_ptr(), dy.data_ptr(), o_add.data_ptr(), N_EL, st)
+        call("bee_b200_ew_binary", 2, F32, dx.data_ptr(), dy.data_ptr(), o_mul.data_ptr(), N_EL, st)
+        call("bee_b200_ew_cast", F32, dx.data_ptr(), BF16, o_bf.data_ptr(), N_EL, st)
+        call("bee_b200_reduce_axis", 0, F32, dx.data_ptr(), o_rsum.data_ptr(), ROWS, COLS, 1, st)
+        call("bee_b200_reduce_axis", 2, F32, dx.data_ptr(), o_rmax.data_ptr(), ROWS, COLS, 1, st)
+        call("bee_b200_softmax_rows", F32, dx.data_ptr(), o_sm.data_ptr(), ROWS, COLS, st)
+        call("bee_b200_reduce_global", 0, I32, dxi.data_ptr(), o_isum.data_ptr(), N_EL, st)
+        if d.pg is not None:
+            import torch.distributed as dist
+            with torch.cuda.stream(stream):
+                dist.all_reduce(o_isum, op=dist.ReduceOp.SUM)
+
+    up, down = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev_up = [torch.cuda.Event() for _ in range(2)]
+    ev_ops = [torch.cuda.Event() for _ in range(2)]
+    ev_down = [torch.cuda.Event() for _ in range(2)]
+    for k in range(2):  # every set starts free
+        ev_ops[k].record(stream)
+        ev_down[k].record(stream)
+
+    def e2e_step(i):
+        k = i & 1
+        ins, outs_k = sets[k]
+        up.wait_event(ev_ops[k])  # this set's previous kernels have read their inputs
+        for h, dd in zip(h_ins, ins):
             call("bee_b200_memcpy_h2d", dd.data_ptr(), h.data_ptr(), h.numel() * h.element_size(), up.cuda_stream)
-        ev_up.record(up)
-        stream.wait_event(ev_up)
-        stream.wait_event(ev_down)  # the previous step's outputs are in host memory
-        for _, fn in ops:
-            fn()
-        allreduce_isum()
-        ev_ops.record(stream)
-        down.wait_event(ev_ops)
-        for h, o in zip(h_outs, outs):
+        ev_up[k].record(up)
+        stream.wait_event(ev_up[k])
+        stream.wait_event(ev_down[k])  # this set's previous outputs are in host memory
+        run_ops(k)
+        ev_ops[k].record(stream)
+        down.wait_event(ev_ops[k])
+        for h, o in zip(h_outs[k], outs_k):
             call("bee_b200_memcpy_d2h", h.data_ptr(), o.data_ptr(), o.numel() * o.element_size(), down.cuda_stream)
-        ev_down.record(down)
+        ev_down[k].record(down)
 
     steps = max(2, min(args.steps, 6))
-    e2e_step()
-    stream.wait_event(ev_down)
+    for i in range(2):  # warm-up, both sets
+        e2e_step(i)
+    for k in range(2):
+        stream.wait_event(ev_down[k])
     d.barrier()
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     up.wait_event(t0)
-    for _ in range(steps):
-        e2e_step()
-    stream.wait_event(ev_down)
+    down.wait_event(t0)
+    for i in range(steps):
+        e2e_step(i)
+    for k in range(2):
+        stream.wait_event(ev_down[k])
     t1.record(stream)
     call("bee_b200_stream_synchronize", st)
     ms = d.max(t0.elapsed_time(t1))
+    # each direction alone (same copies, one stream, nothing else running)
+    def one_way(copy_fn, nbytes):
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(up)
+        for _ in range(2):
+            copy_fn()
+        b.record(up)
+        b.synchronize()
+        return round(2 * nbytes / (a.elapsed_time(b) / 1e3) / 1e9, 1)
+    h2d_alone = one_way(lambda: [call("bee_b200_memcpy_h2d", dd.data_ptr(), h.data_ptr(), h.numel() * h.element_size(),
+                                      up.cuda_stream) for h, dd in zip(h_ins, sets[0][0])], h2d)
+    d2h_alone = one_way(lambda: [call("bee_b200_memcpy_d2h", h.data_ptr(), o.data_ptr(), o.numel() * o.element_size(),
+                                      up.cuda_stream) for h, o in zip(h_outs[0], sets[0][1])], d2h)
+    # the last step's results, read back, must match the device-timed sweep's
+    ok = all(torch.equal(h.to(dev), o) for h, o in zip(h_outs[(steps - 1) & 1], sets[(steps - 1) & 1][1]))
     return {"value": round(d.world * STEP_BYTES * steps / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
-            "ms_per_step": round(ms / steps, 3),
-            "copies": "pinned host buffers; H2D of step k+1 on one copy stream overlaps D2H of step k on another"}
+            "ms_per_step": round(ms / steps, 3), "outputs_match_device": bool(ok),
+            "pcie_gbs": {"h2d_alone": h2d_alone, "d2h_alone": d2h_alone,
+                         "both_in_step": round((h2d + d2h) / (ms / steps / 1e3) / 1e9, 1)},
+            "copies": "pinned host buffers, two device buffer sets alternating between steps; H2D of step k+1 and "
+                      "D2H of step k on two copy streams at once"}
 
 
 # ---------------------------------------------------------------- CPU baseline / reference arm

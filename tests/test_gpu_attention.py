@@ -38,7 +38,8 @@ def _inputs(seed, heads, seq, hd, spread=1.0):
     return f(), f(), f()
 
 
-@pytest.mark.parametrize("heads,seq", [(1, 128), (2, 256), (3, 640)])
+# odd tile counts (3 x 640: the last CTA of a head holds one tile) and longer rows
+@pytest.mark.parametrize("heads,seq", [(1, 128), (2, 256), (3, 640), (1, 512), (2, 1024), (3, 1536)])
 def test_attention_matches_oracle(cuda, oracle, heads, seq):
     torch = cuda
     q, k, v = _inputs(heads * 1000 + seq, heads, seq, 128)
