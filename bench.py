@@ -191,6 +191,16 @@ def smi_id(dev) -> str:
 
 # ---------------------------------------------------------------- distributed plumbing
 
+_T0 = time.perf_counter()
+
+
+def progress(d, msg: str) -> None:
+    """Phase timestamps on stderr (rank 0), so a slow or stuck multi-GPU run shows where it is."""
+    if d.rank == 0:
+        sys.stderr.write(f"[bench +{time.perf_counter() - _T0:.1f}s] {msg}\n")
+        sys.stderr.flush()
+
+
 class Dist:
     def __init__(self, gpus: int):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -261,6 +271,7 @@ def run_ours(args, d: Dist):
     from bee_b200._capi import call
 
     d.init()
+    progress(d, f"process group up ({d.world} ranks)")
     lib = _capi.lib()  # fails loudly if the CUDA library is missing
     dev = torch.device("cuda", d.local)
     stream = torch.cuda.Stream(device=dev)
@@ -268,6 +279,7 @@ def run_ours(args, d: Dist):
     peaks = load_peaks()
 
     x, y, xi = make_inputs(d.rank)
+    progress(d, "inputs generated")
     hx = torch.from_numpy(x).pin_memory()
     hy = torch.from_numpy(y).pin_memory()
     hxi = torch.from_numpy(xi).pin_memory()
@@ -344,6 +356,7 @@ def run_ours(args, d: Dist):
             evs[len(ops)].record(stream)
         allreduce_isum()
 
+    progress(d, "inputs resident, warm-up")
     # warm-up (also checks the int32 sum against the host, bit-exact); the last warm-up
     # step's duration places the clock samples inside the timed region at N > 1
     w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -422,6 +435,7 @@ def run_ours(args, d: Dist):
     e2e = None
     if not args.no_e2e:
         slot[0] = ring.numel() - 1  # a slot of its own, exchanged on the compute stream
+        progress(d, "sweep timed; e2e")
         e2e = run_e2e(args, d, dev, stream, hx, hy, hxi, [dx, dy, dxi],
                       [o_add, o_mul, o_bf, o_rsum, o_rmax, o_sm, ring[slot[0]:slot[0] + 1]])
 
@@ -443,7 +457,9 @@ def run_ours(args, d: Dist):
         # (extras included) is done: NVML in the process slows multi-GPU steps
     if peer is not None:
         peer.close()
+    progress(d, "extras")
     extra = None if args.no_extras else run_extras(args, d, dev, stream, peaks)
+    progress(d, "extras done")
     if d.world > 1 and not args.no_clocks and d.rank == 0:
         after = ClockSampler(smi_id(dev), enabled=True)
         with after:
@@ -557,7 +573,9 @@ def run_extras(args, d, dev, stream, peaks):
         if label is not None and not args.no_clocks:
             probe_stream.synchronize()
             probe_log[label] = round(float(probe_buf.item()), 1)
-        return d.max(e0.elapsed_time(e1)) / n_time
+        ms_call = d.max(e0.elapsed_time(e1)) / n_time
+        progress(d, f"extra {label or 'config'}: {ms_call:.4f} ms per call ({n_warm} warm-up, {n_time} timed)")
+        return ms_call
 
     def status_ok():
         import ctypes
