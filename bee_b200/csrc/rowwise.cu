@@ -102,6 +102,20 @@ template <int THREADS> __device__ __forceinline__ float block_sum(float v, float
     return r;
 }
 
+// Block-wide sum with one barrier: the warp partials of consecutive calls go to
+// alternating halves of `red` ([2][THREADS / 32], `parity` flips per call), so a
+// call's writes never meet the previous call's reads (every thread has passed
+// the previous call's barrier after reading, before the next write).
+template <int THREADS> __device__ __forceinline__ float block_sum_1bar(float v, float (*red)[THREADS / 32], int parity) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[parity][threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = 0.f;
+#pragma unroll
+    for (int w = 0; w < THREADS / 32; ++w) r += red[parity][w];
+    return r;
+}
+
 // ---------------------------------------------------------------- softmax
 
 template <typename Ti, typename To, int THREADS, int NQ>
@@ -324,7 +338,7 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) norm_rope_pipe_kernel
     constexpr int E = CK::E;
     constexpr int CPU = ROPE ? 2 : 1;  // chunks per unit
     extern __shared__ __align__(16) uint8_t pipe_smem[];
-    __shared__ float red[THREADS / 32];
+    __shared__ float red[2][THREADS / 32];
     __shared__ double turns_per_pos[128];
     const uint32_t chunks = cols / E;
     const uint32_t units = chunks / CPU;
@@ -403,6 +417,7 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) norm_rope_pipe_kernel
     int slot = 0;
     uint32_t parity = 1;
     size_t cur_pos = ~size_t(0);
+    int red_parity = 0;
     for (size_t i = i_begin; i < i_end; i += i_step, slot = slot + 1 == S ? 0 : slot + 1) {
         issue();
         cp_async_wait<S - 1>();  // this thread's copies of this row have landed
@@ -445,7 +460,8 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) norm_rope_pipe_kernel
         }
         float inv = 1.0f;
         if (NORM) {
-            ss = block_sum<THREADS>(ss, red);  // also publishes a rebuilt cos / sin table
+            ss = block_sum_1bar<THREADS>(ss, red, red_parity);  // also publishes a rebuilt cos / sin table
+            red_parity ^= 1;
             inv = rsqrtf(ss / static_cast<float>(cols) + eps);
         } else if (new_table) {
             __syncthreads();  // publish the rebuilt cos / sin table (uniform: every thread sees the same position)
