@@ -5,12 +5,17 @@
 // softmax and matmul, each round-tripping through memory).  Here one CTA owns
 // two 128-query tiles (A and B) of one head and streams the keys/values past
 // them in blocks of 128, so S and P never leave the SM:
-//   * warp 0 — TMA: Q_A, Q_B once, then K_j / V_j into two-deep rings (one
-//     64x128 box shape serves all three; K is read as the K-major operand of
-//     Q.K^T, V as the MN-major operand of P.V);
+//   * warp 0 — TMA: Q_A, Q_B and K_0 once, then a two-stage ring whose stage
+//     j & 1 holds V_j and K_{j+1} (one 64x128 box shape serves all three; K is
+//     read as the K-major operand of Q.K^T, V as the MN-major operand of P.V);
 //   * warp 1 — MMA, ping-pong between the tiles: O_A += P_A(j).V_j,
 //     S_A(j+1) = Q_A.K_{j+1}^T, O_B += P_B(j).V_j, S_B(j+1) = Q_B.K_{j+1}^T,
-//     so the tensor core works on one tile while the other tile's softmax runs;
+//     so the tensor core works on one tile while the other tile's softmax runs.
+//     This one thread paces the kernel: each mbarrier wait or tcgen05.commit it
+//     executes costs ~100 cycles even when nothing is pending, so per block it
+//     does one wait for the ring stage, one per tile for P, one commit per tile
+//     for S and one to release the stage, with descriptors precomputed and the
+//     ring slot a compile-time constant (blocks are unrolled in pairs);
 //     warps 2-3 idle; this warpgroup gives most of its registers to the next two
 //     (setmaxnreg);
 //   * warps 4-7 / 8-11 — softmax of tile A / B, one thread per query row: the
@@ -28,6 +33,7 @@
 // Every wait is bounded; a wait that gives up records a code in the status
 // word read by bee_b200_device_status and the CTA abandons its work.
 #include <cuda.h>
+#include <type_traits>
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -92,6 +98,86 @@ __device__ __forceinline__ float row_max128(const uint32_t (&s)[128]) {
     return fmaxf(max3(v[0], v[1], v[2]), fmaxf(v[3], v[4]));
 }
 
+// ---------------------------------------------------------------- MMA issuer
+// The issuing thread paces the kernel: each mbarrier wait or tcgen05.commit on
+// it costs ~100 cycles even when nothing is pending, so everything below keeps
+// them to one wait for the ring stage, one per tile for P, one commit per tile
+// for S and one to release the stage, with the shared-memory descriptors built
+// once and the ring slot a compile-time constant.
+struct MmaRing {
+    uint32_t tmem;
+    uint64_t dq[2], dk[2], dv[2];  // descriptors of Q_A / Q_B, K slots, V slots
+    uint64_t *op_full, *op_empty, *s_full, *p_full;
+    volatile int* abort;
+    int* status;
+    int nkv;
+};
+
+constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128, false);  // B = K rows, K-major
+constexpr uint32_t kIdescO = idesc_bf16_f32(128, 128, true);   // B = V, MN-major
+
+// S_t = Q_t . K^T (K in ring slot KS) into TMEM columns t * 128, then signal the
+// tile's softmax.  Within a tile only the descriptors' start-address field
+// (address >> 4, low 14 bits; every address here is below 2^18, so it never
+// carries out) moves, by a compile-time amount per K step.
+template <int T, int KS>
+__device__ __forceinline__ void issue_s(const MmaRing& r) {
+    // opaque copies: otherwise the compiler hoists every (base + step) of the
+    // unrolled loop out of it and runs out of registers
+    uint64_t qd = r.dq[T], kd = r.dk[KS];
+    asm volatile("" : "+l"(qd), "+l"(kd));
+#pragma unroll
+    for (int k = 0; k < kHead / 16; ++k) {
+        const uint64_t step = static_cast<uint64_t>(((k / 4) * kHalf + (k % 4) * 32) >> 4);
+        mma_f16_ss(r.tmem + static_cast<uint32_t>(T * 128), qd + step, kd + step, kIdescS, k != 0 ? 1u : 0u);
+    }
+    mma_commit(&r.s_full[T]);
+}
+
+// O_t += P_t . V (V in ring slot VS); P_t sits in TMEM columns t * 128 .. + 63 as bf16 pairs.
+template <int T, int VS>
+__device__ __forceinline__ void issue_o(const MmaRing& r, bool acc) {
+    uint64_t vd = r.dv[VS];
+    asm volatile("" : "+l"(vd));
+#pragma unroll
+    for (int k = 0; k < kBlock / 16; ++k)
+        mma_f16_ts(r.tmem + 256u + static_cast<uint32_t>(T * 128), r.tmem + static_cast<uint32_t>(T * 128 + k * 8),
+                   vd + static_cast<uint64_t>((k * 16 * 128) >> 4), kIdescO, (acc || k != 0) ? 1u : 0u);
+}
+
+// Block j of the keys, ring stage ST = j & 1 holding V_j and K_{j+1}.
+template <int NT, int ST>
+__device__ __forceinline__ bool mma_block(const MmaRing& r, int j) {
+    if (!mbar_wait(&r.op_full[ST], static_cast<uint32_t>((j >> 1) & 1), r.abort, r.status, 27)) return false;
+    const bool next = j + 1 < r.nkv;
+    if (!mbar_wait(&r.p_full[0], static_cast<uint32_t>(j & 1), r.abort, r.status, 26)) return false;
+    tc_fence_after();
+    issue_o<0, ST>(r, j != 0);
+    if (next) issue_s<0, ST>(r);
+    if (NT == 2) {
+        if (!mbar_wait(&r.p_full[1], static_cast<uint32_t>(j & 1), r.abort, r.status, 26)) return false;
+        tc_fence_after();
+        issue_o<1, ST>(r, j != 0);
+        if (next) issue_s<1, ST>(r);
+    }
+    mma_commit(&r.op_empty[ST]);
+    return true;
+}
+
+template <int NT>
+__device__ __forceinline__ bool mma_all(const MmaRing& r, bool ok) {
+    if (!ok || r.nkv == 0) return ok;
+    tc_fence_after();
+    issue_s<0, 1>(r);  // K_0 sits in the K slot of stage 1
+    if (NT == 2) issue_s<1, 1>(r);
+    mma_commit(&r.op_empty[1]);
+    for (int j = 0; ok && j < r.nkv; j += 2) {
+        ok = mma_block<NT, 0>(r, j);
+        if (ok && j + 1 < r.nkv) ok = mma_block<NT, 1>(r, j + 1);
+    }
+    return ok;
+}
+
 struct AttnParams {
     int seq;          // queries == keys per head (multiple of 128)
     int nkv;          // seq / 128
@@ -114,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
                                                                          const AttnParams p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t q_full;
-    __shared__ __align__(8) uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+    __shared__ __align__(8) uint64_t op_full[2], op_empty[2];  // ring stage: V_j and K_{j+1}
     __shared__ __align__(8) uint64_t s_full[2], p_full[2];  // [tile]
     __shared__ __align__(8) uint64_t done_bar;
     __shared__ uint32_t tmem_base_sh;
@@ -135,10 +221,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
     if (threadIdx.x == 0) {
         mbar_init(&q_full, 1);
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&k_full[i], 1);
-            mbar_init(&k_empty[i], 1);
-            mbar_init(&v_full[i], 1);
-            mbar_init(&v_empty[i], 1);
+            mbar_init(&op_full[i], 1);
+            mbar_init(&op_empty[i], 1);
             mbar_init(&s_full[i], 1);
             mbar_init(&p_full[i], 4);  // one arrive per softmax warp of the tile
         }
@@ -163,94 +247,56 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
         if (warp == 0) {
             // ------------------------------------------------ TMA producer
             if (lane == 0) {
-                mbar_arrive_expect_tx(&q_full, ntiles * kTile);
+                // Q_A, Q_B and K_0 (into the K slot of stage 1) on q_full
+                mbar_arrive_expect_tx(&q_full, static_cast<uint32_t>((ntiles + (nkv > 0 ? 1 : 0)) * kTile));
                 for (int t = 0; t < ntiles; ++t) {
                     tma_load_3d(sQ + t * kTile, &tmQ, &q_full, 0, q0 + t * kBlock, head);
                     tma_load_3d(sQ + t * kTile + kHalf, &tmQ, &q_full, 64, q0 + t * kBlock, head);
                 }
-                int k_issued = 0, v_issued = 0;
+                if (nkv > 0) {
+                    tma_load_3d(sK + kTile, &tmK, &q_full, 0, 0, head);
+                    tma_load_3d(sK + kTile + kHalf, &tmK, &q_full, 64, 0, head);
+                }
+                // stage s = j & 1 takes V_j and K_{j+1}; stage 1 is first released
+                // by the MMA that read K_0, so its waits run one phase behind stage 0's
+                int filled = 0;
                 for (int j = 0; j < nkv; ++j) {
                     const int s = j & 1;
-                    const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
-                    if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag, status, 21)) break;
-                    mbar_arrive_expect_tx(&k_full[s], kTile);
-                    tma_load_3d(sK + s * kTile, &tmK, &k_full[s], 0, j * kBlock, head);
-                    tma_load_3d(sK + s * kTile + kHalf, &tmK, &k_full[s], 64, j * kBlock, head);
-                    k_issued = j + 1;
-                    if (!mbar_wait(&v_empty[s], ph ^ 1u, abort_flag, status, 22)) break;
-                    mbar_arrive_expect_tx(&v_full[s], kTile);
-                    tma_load_3d(sV + s * kTile, &tmV, &v_full[s], 0, j * kBlock, head);
-                    tma_load_3d(sV + s * kTile + kHalf, &tmV, &v_full[s], 64, j * kBlock, head);
-                    v_issued = j + 1;
+                    const uint32_t par = static_cast<uint32_t>((j >> 1) & 1) ^ (s == 0 ? 1u : 0u);
+                    if (!mbar_wait(&op_empty[s], par, abort_flag, status, 21)) break;
+                    const bool knext = j + 1 < nkv;
+                    mbar_arrive_expect_tx(&op_full[s], static_cast<uint32_t>((knext ? 2 : 1) * kTile));
+                    tma_load_3d(sV + s * kTile, &tmV, &op_full[s], 0, j * kBlock, head);
+                    tma_load_3d(sV + s * kTile + kHalf, &tmV, &op_full[s], 64, j * kBlock, head);
+                    if (knext) {
+                        tma_load_3d(sK + s * kTile, &tmK, &op_full[s], 0, (j + 1) * kBlock, head);
+                        tma_load_3d(sK + s * kTile + kHalf, &tmK, &op_full[s], 64, (j + 1) * kBlock, head);
+                    }
+                    filled = j + 1;
                 }
-                // the last loads of each ring must have landed before the CTA may exit
+                // the last loads must have landed before the CTA may exit
                 // (normally the MMA warp consumed them already)
                 mbar_wait(&q_full, 0, abort_flag, status, 33, 200000000ull);
-                for (int j = k_issued > 2 ? k_issued - 2 : 0; j < k_issued; ++j)
-                    mbar_wait(&k_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, status, 34, 200000000ull);
-                for (int j = v_issued > 2 ? v_issued - 2 : 0; j < v_issued; ++j)
-                    mbar_wait(&v_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, status, 35, 200000000ull);
+                for (int j = filled > 2 ? filled - 2 : 0; j < filled; ++j)
+                    mbar_wait(&op_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, status, 34, 200000000ull);
             }
             __syncwarp();
         } else if (warp == 1) {
             // ------------------------------------------------ MMA issuer
             if (lane == 0) {
-                constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false);  // B = K rows, K-major
-                constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, true);   // B = V, MN-major
+                // Shared-memory descriptors of the operand slots, built once: a thread
+                // that rebuilt both descriptors per MMA took about as long to issue a
+                // 128x128x16 product as the tensor core takes to retire it.
+                const uint64_t dq0 = sdesc_sw128(smem_u32(sQ), 16, 1024), dq1 = sdesc_sw128(smem_u32(sQ + kTile), 16, 1024);
+                const uint64_t dk0 = sdesc_sw128(smem_u32(sK), 16, 1024), dk1 = sdesc_sw128(smem_u32(sK + kTile), 16, 1024);
+                const uint64_t dv0 = sdesc_sw128(smem_u32(sV), kHalf, 1024), dv1 = sdesc_sw128(smem_u32(sV + kTile), kHalf, 1024);
+                MmaRing r{tmem, {dq0, dq1}, {dk0, dk1}, {dv0, dv1}, op_full, op_empty, s_full, p_full, abort_flag, status, nkv};
                 bool ok = mbar_wait(&q_full, 0, abort_flag, status, 23);
-                bool issued = false;
-                // S_t = Q_t . K_j^T into TMEM columns t * 128
-                auto issue_s = [&](int t, int j) {
-                    const uint32_t q_base = smem_u32(sQ + t * kTile);
-                    const uint32_t k_base = smem_u32(sK + (j & 1) * kTile);
-#pragma unroll
-                    for (int k = 0; k < kHead / 16; ++k) {
-                        const uint32_t off = (k / 4) * kHalf + (k % 4) * 32;
-                        mma_f16_ss(tmem + static_cast<uint32_t>(t * 128), sdesc_sw128(q_base + off, 16, 1024),
-                                   sdesc_sw128(k_base + off, 16, 1024), idesc_s, k != 0 ? 1u : 0u);
-                    }
-                    mma_commit(&s_full[t]);
-                    issued = true;
-                };
-                // O_t += P_t . V_j, P_t in TMEM columns t * 128 .. + 63 (bf16 pairs)
-                auto issue_o = [&](int t, int j) {
-                    const uint32_t v_base = smem_u32(sV + (j & 1) * kTile);
-#pragma unroll
-                    for (int k = 0; k < kBlock / 16; ++k)
-                        mma_f16_ts(tmem + 256u + static_cast<uint32_t>(t * 128), tmem + static_cast<uint32_t>(t * 128 + k * 8),
-                                   sdesc_sw128(v_base + k * 16 * 128, kHalf, 1024), idesc_o, (j | k) != 0 ? 1u : 0u);
-                    issued = true;
-                };
-                if (ok && nkv > 0) {
-                    ok = mbar_wait(&k_full[0], 0, abort_flag, status, 24);
-                    if (ok) {
-                        tc_fence_after();
-                        for (int t = 0; t < ntiles; ++t) issue_s(t, 0);
-                        mma_commit(&k_empty[0]);
-                    }
-                }
-                for (int j = 0; ok && j < nkv; ++j) {
-                    const int s = j & 1;
-                    const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
-                    const bool next = j + 1 < nkv;
-                    const int s1 = (j + 1) & 1;
-                    const uint32_t ph1 = static_cast<uint32_t>(((j + 1) >> 1) & 1);
-                    for (int t = 0; ok && t < ntiles; ++t) {
-                        ok = mbar_wait(&p_full[t], static_cast<uint32_t>(j & 1), abort_flag, status, 26);
-                        if (ok && t == 0) ok = mbar_wait(&v_full[s], ph, abort_flag, status, 27);
-                        if (!ok) break;
-                        tc_fence_after();
-                        issue_o(t, j);
-                        if (t == ntiles - 1) mma_commit(&v_empty[s]);
-                        if (next) {
-                            if (t == 0) ok = mbar_wait(&k_full[s1], ph1, abort_flag, status, 24);
-                            if (!ok) break;
-                            tc_fence_after();
-                            issue_s(t, j + 1);
-                            if (t == ntiles - 1) mma_commit(&k_empty[s1]);
-                        }
-                    }
-                }
+                const bool issued = ok && nkv > 0;
+                if (ntiles == 2)
+                    mma_all<2>(r, ok);
+                else
+                    mma_all<1>(r, ok);
                 if (issued) {
                     mma_commit(&done_bar);
                     mbar_wait(&done_bar, 0, abort_flag, status, 28, 200000000ull);
