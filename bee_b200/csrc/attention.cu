@@ -73,6 +73,37 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// 2^x for a packed pair on the FMA pipe, beside the MUFU ex2: Cody-Waite split
+// x = n + f with n = floor(x) (x + 1.5 * 2^23 rounded toward -inf leaves n in the
+// low mantissa bits) and f in [0, 1); 2^f by a cubic fitted here for minimum
+// relative error on [0, 1] (7.5e-5 at most, against 2^-9 for the bf16 rounding of
+// P that follows); n added to the exponent field.  x is clamped at -126 so the
+// exponent field never goes negative (2^-126 and below read as ~0 in bf16 P and
+// in the fp32 row sum).
+__device__ __forceinline__ void ex2_fma_x2(uint64_t x2, float& e0, float& e1) {
+    float x0, x1;
+    unpack_f32x2(x2, x0, x1);
+    const uint64_t xc = pack_f32x2(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+    const uint64_t magic = pack_f32x2(12582912.0f, 12582912.0f);
+    uint64_t t, n, f;
+    asm("add.rm.f32x2 %0, %1, %2;" : "=l"(t) : "l"(xc), "l"(magic));
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(n) : "l"(t), "l"(magic));
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(f) : "l"(xc), "l"(n));
+    uint64_t q = fma_f32x2(f, pack_f32x2(0.07802427560091019f, 0.07802427560091019f),
+                           pack_f32x2(0.22606725990772247f, 0.22606725990772247f));
+    q = fma_f32x2(q, f, pack_f32x2(0.6958336234092712f, 0.6958336234092712f));
+    q = fma_f32x2(q, f, pack_f32x2(0.9999251961708069f, 0.9999251961708069f));
+    float q0, q1, t0, t1;
+    unpack_f32x2(q, q0, q1);
+    unpack_f32x2(t, t0, t1);
+    e0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
+    e1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
+}
+
+// Which pairs of a row's 64 take ex2_fma_x2 instead of the MUFU: bit (i % 16) of
+// the mask for pair i.
+constexpr uint32_t kEx2FmaMask = 0x2222u;
+
 // Three-input maximum (one instruction on sm_100).
 __device__ __forceinline__ float max3(float a, float b, float c) {
     float d;
@@ -182,7 +213,6 @@ struct AttnParams {
     int seq;          // queries == keys per head (multiple of 128)
     int nkv;          // seq / 128
     float scale_log2; // scale * log2(e)
-    uint16_t* O;      // [heads, seq, 128] bf16
 };
 
 constexpr int kThreads = 384;  // warpgroup 0: TMA warp, MMA warp, 2 idle; warpgroups 1-2: softmax
@@ -197,12 +227,14 @@ static_assert(kRegsLaunch * kThreads <= 65536 && kRegsLaunch * 3 * 32 <= 16384, 
 __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                                          const __grid_constant__ CUtensorMap tmK,
                                                                          const __grid_constant__ CUtensorMap tmV,
+                                                                         const __grid_constant__ CUtensorMap tmO,
                                                                          const AttnParams p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t q_full;
     __shared__ __align__(8) uint64_t op_full[2], op_empty[2];  // ring stage: V_j and K_{j+1}
     __shared__ __align__(8) uint64_t s_full[2], p_full[2];  // [tile]
     __shared__ __align__(8) uint64_t done_bar;
+    __shared__ __align__(8) uint64_t o_ready[2];  // [tile]: its 4 warps have staged O
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
 
@@ -227,6 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
             mbar_init(&p_full[i], 4);  // one arrive per softmax warp of the tile
         }
         mbar_init(&done_bar, 1);
+        mbar_init(&o_ready[0], 4);
+        mbar_init(&o_ready[1], 4);
         abort_sh = 0;
         fence_mbar_init();
     }
@@ -234,6 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
         tma_prefetch(&tmQ);
         tma_prefetch(&tmK);
         tma_prefetch(&tmV);
+        tma_prefetch(&tmO);
     }
     if (warp == 1) tmem_alloc<512>(&tmem_base_sh);
     tc_fence_before();
@@ -365,9 +400,16 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int k = h * 64 + 2 * i;
-                    float x0, x1;
-                    unpack_f32x2(fma_f32x2(pack_f32x2(__uint_as_float(sc[k]), __uint_as_float(sc[k + 1])), c2, nm2), x0, x1);
-                    const float e0 = ex2(x0), e1 = ex2(x1);
+                    const uint64_t x2 = fma_f32x2(pack_f32x2(__uint_as_float(sc[k]), __uint_as_float(sc[k + 1])), c2, nm2);
+                    float e0, e1;
+                    if ((kEx2FmaMask >> (i % 16)) & 1u) {
+                        ex2_fma_x2(x2, e0, e1);
+                    } else {
+                        float x0, x1;
+                        unpack_f32x2(x2, x0, x1);
+                        e0 = ex2(x0);
+                        e1 = ex2(x1);
+                    }
                     acc[i & 3] = add_f32x2(acc[i & 3], pack_f32x2(e0, e1));
                     w[i] = pack_bf16x2(e0, e1);
                 }
@@ -384,18 +426,22 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
             unpack_f32x2(acc[3], a6, a7);
             l += ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7));
         }
-        // epilogue: O / l -> bf16, the thread's whole row
+        // epilogue: O / l -> bf16, staged in shared memory (the K slots are free
+        // once every MMA has completed) in the 128-byte-swizzled layout of the
+        // tensor map, then written by two TMA stores per tile: 16-byte stores
+        // from registers, one row per thread, took ~4000 cycles per CTA
         if (ok && nkv > 0) {
             ok = mbar_wait(&done_bar, 0, abort_flag, status, 32);
             if (__all_sync(0xffffffffu, ok)) {
                 tc_fence_after();
                 const float inv = 1.0f / l;
-                uint16_t* orow = p.O + (static_cast<size_t>(head) * p.seq + static_cast<size_t>(q0 + t * kBlock + row)) * kHead;
+                uint8_t* so = sK + t * kTile;  // [2 halves of 64 columns][128 rows][128 bytes]
 #pragma unroll 1
                 for (int cc = 0; cc < 4; ++cc) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(o_col + static_cast<uint32_t>(cc * 32), r);
                     tmem_ld_wait();
+                    uint8_t* half_row = so + (cc >> 1) * kHalf + row * 128;
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
                         uint4 o;
@@ -403,7 +449,19 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
                         o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
                         o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
                         o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
-                        reinterpret_cast<uint4*>(orow + cc * 32)[v] = o;
+                        const int chunk = (cc & 1) * 4 + v;  // 16-byte chunk within the 128-byte row
+                        *reinterpret_cast<uint4*>(half_row + ((chunk ^ (row & 7)) << 4)) = o;
+                    }
+                }
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&o_ready[t]);
+                if (q == 0 && lane == 0) {
+                    if (mbar_wait(&o_ready[t], 0, abort_flag, status, 36)) {
+                        tma_store_3d(&tmO, so, 0, q0 + t * kBlock, head);
+                        tma_store_3d(&tmO, so + kHalf, 64, q0 + t * kBlock, head);
+                        tma_store_commit();
+                        tma_store_wait_read();
                     }
                 }
             }
@@ -469,15 +527,15 @@ extern "C" int bee_b200_attention(int dt, const void* q, const void* k, const vo
         return fail(cudaErrorInvalidValue, "attention: scale must be positive and finite");
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
         return fail(cudaErrorInvalidValue, "attention: buffers must be 16-byte aligned");
-    CUtensorMap tq, tk, tv;
+    CUtensorMap tq, tk, tv, to;
     if (int rc = make_qkv_map(&tq, q, heads, seq)) return rc;
     if (int rc = make_qkv_map(&tk, k, heads, seq)) return rc;
     if (int rc = make_qkv_map(&tv, v, heads, seq)) return rc;
+    if (int rc = make_qkv_map(&to, o, heads, seq)) return rc;
     AttnParams p;
     p.seq = static_cast<int>(seq);
     p.nkv = static_cast<int>(seq / kBlock);
     p.scale_log2 = scale * 1.4426950408889634f;
-    p.O = static_cast<uint16_t*>(o);
     // setmaxnreg.inc waits until the registers it asks for are free, so the
     // split is only safe when the kernel launches with exactly kRegsLaunch
     static std::atomic<int> launch_regs{0};
@@ -495,6 +553,6 @@ extern "C" int bee_b200_attention(int dt, const void* q, const void* k, const vo
     static SmemLimit smem_limit;
     if (int rc = smem_limit.ensure(attention_fwd_kernel, kSmem, "attention")) return rc;
     dim3 grid(static_cast<unsigned>((seq / kBlock + 1) / 2), static_cast<unsigned>(heads));
-    attention_fwd_kernel<<<grid, kThreads, kSmem, as_stream(stream)>>>(tq, tk, tv, p);
+    attention_fwd_kernel<<<grid, kThreads, kSmem, as_stream(stream)>>>(tq, tk, tv, to, p);
     return launch_status("attention");
 }
