@@ -351,10 +351,12 @@ static int run_axis(const void* src, void* dst, size_t outer, size_t axis, size_
     const size_t tw = vec ? 32 * EV : 32;
     const size_t ctiles = (inner + tw - 1) / tw;
     const size_t tiles = outer * ctiles;
-    // as many segments as keep every work item resident at once (tiles * G <=
-    // 8 CTAs per SM): one more item than the GPU holds would run alone in a
-    // second wave at a fraction of the bandwidth
-    size_t G = target / tiles;
+    // as many segments as keep every work item resident at once, about four
+    // CTAs per SM (one more item than the GPU holds would run alone in a second
+    // wave at a fraction of the bandwidth); on [8192, 8192] fp32 four per SM ran
+    // 0.0459 ms against 0.0466 ms at eight (more, shorter segments) and 0.0537 ms
+    // at two
+    size_t G = target / 2 / tiles;
     const size_t max_g = (axis + 63) / 64;  // segments of at least 64 rows (8 per warp)
     if (G > max_g) G = max_g;
     if (G < 1) G = 1;
