@@ -21,14 +21,15 @@
 //   * warps 4-7 / 8-11 — softmax of tile A / B, one thread per query row: the
 //     thread reads its 128 scores from TMEM, keeps a running max m (log2 units)
 //     and sum l, and writes P = 2^(s*c - m) as bf16 back into TMEM over the
-//     first 64 columns of its own scores; P.V then reads P straight from TMEM
+//     first 64 columns of its own scores (three quarters of the exponentials
+//     on the MUFU, one quarter on the FMA pipe); P.V then reads P straight from TMEM
 //     (tcgen05.mma with the A operand in tensor memory).  The running max is
 //     only raised when a block's max exceeds it by more than 8 (a factor 2^8):
 //     until then P <= 256, which bf16 and fp32 hold exactly enough, and O / l
 //     is unchanged; when it is raised the thread rescales its row of O in TMEM
 //     (the previous P.V is complete by then: the MMA that produced the current
 //     scores was issued after it).  At the end each thread divides its O row
-//     by l and stores it.
+//     by l into shared memory, and two TMA stores per tile write O.
 // TMEM (512 columns): S_A 0-127, S_B 128-255, O_A 256-383, O_B 384-511.
 // Every wait is bounded; a wait that gives up records a code in the status
 // word read by bee_b200_device_status and the CTA abandons its work.
