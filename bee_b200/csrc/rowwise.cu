@@ -330,23 +330,20 @@ template <> struct Chunk<uint16_t> {
 // or one publishing the cos/sin table (RoPE alone).  Weights and per-unit
 // offsets stay in registers for the whole kernel; 1/rms is folded into the
 // row's cos/sin values, leaving about three FP instructions per element.
-// A thread keeps its share of the row (and the matching weights) unpacked in
-// registers between the sum-of-squares and the output pass when that share is at
-// most 32 elements: it then runs at 512 threads per SM (up to 128 registers),
-// otherwise at 1024 threads and 64 registers, reloading and unpacking the row
-// from the ring and the weights from packed registers.  The first is 7% faster
-// on 4096-column bf16 rows, where the kernel is bound by instruction issue.
+// A thread keeps its share of the row and the matching weights unpacked in
+// registers between the sum-of-squares pass and the output pass, so each element
+// is unpacked once per row and each weight once per kernel.  Every configuration
+// the dispatcher launches gives a thread at most 32 elements, which fits in 128
+// registers at 512 threads per SM; on 4096-column rows, where the kernel is bound
+// by instruction issue, this ran 6-9% faster in bf16 than reloading the row from
+// the ring and re-expanding packed weights at 1024 threads per SM.
 template <typename T, int NP, bool ROPE>
-constexpr bool pipe_cache_row() {
-    return NP * (ROPE ? 2 : 1) * (16 / static_cast<int>(sizeof(T))) <= 32;
-}
-template <typename T, int THREADS, int NP, bool ROPE>
-constexpr int pipe_min_blocks() {
-    return (pipe_cache_row<T, NP, ROPE>() ? 512 : 1024) / THREADS;
+constexpr int pipe_share() {
+    return NP * (ROPE ? 2 : 1) * (16 / static_cast<int>(sizeof(T)));
 }
 
 template <typename T, int THREADS, int NP, int S, bool NORM, bool ROPE>
-__global__ void __launch_bounds__(THREADS, (pipe_min_blocks<T, THREADS, NP, ROPE>())) norm_rope_pipe_kernel(const T* __restrict__ x, const T* __restrict__ w,
+__global__ void __launch_bounds__(THREADS, 512 / THREADS) norm_rope_pipe_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                                  T* __restrict__ y, size_t rows, uint32_t cols,
                                                                  float eps, RopeArgs rope) {
     using CK = Chunk<T>;
@@ -370,9 +367,8 @@ __global__ void __launch_bounds__(THREADS, (pipe_min_blocks<T, THREADS, NP, ROPE
     uint32_t cidx[NP][CPU];
     uint32_t toff[NP];
     bool live[NP];
-    constexpr bool CACHE = pipe_cache_row<T, NP, ROPE>();
-    uint4 wraw[CACHE ? 1 : NP][CPU];         // weights kept packed (large shares)
-    float wv[CACHE ? NP : 1][CPU][E];        // weights unpacked once (small shares)
+    static_assert(pipe_share<T, NP, ROPE>() <= 32, "a thread's share of the row must fit in registers");
+    float wv[NP][CPU][E];  // weights, unpacked once
 #pragma unroll
     for (int u = 0; u < NP; ++u) {
         const uint32_t unit = tid + u * THREADS;
@@ -389,11 +385,7 @@ __global__ void __launch_bounds__(THREADS, (pipe_min_blocks<T, THREADS, NP, ROPE
         }
 #pragma unroll
         for (int q = 0; q < CPU; ++q) {
-            const uint4 wq = (NORM && live[u]) ? reinterpret_cast<const uint4*>(w)[cidx[u][q]] : make_uint4(0, 0, 0, 0);
-            if constexpr (CACHE)
-                CK::unpack(wq, wv[u][q]);
-            else
-                wraw[u][q] = wq;
+            CK::unpack((NORM && live[u]) ? reinterpret_cast<const uint4*>(w)[cidx[u][q]] : make_uint4(0, 0, 0, 0), wv[u][q]);
         }
     }
     if (ROPE)
@@ -467,30 +459,19 @@ __global__ void __launch_bounds__(THREADS, (pipe_min_blocks<T, THREADS, NP, ROPE
         }
         const float* cosj = cos_t + parity * half;
         const float* sinj = sin_t + parity * half;
-        // small shares: the thread's elements of this row, unpacked once for both passes
-        float xv[CACHE ? NP : 1][CPU][E];
-        if constexpr (CACHE) {
+        // the thread's elements of this row, unpacked once for both passes
+        float xv[NP][CPU][E];
 #pragma unroll
-            for (int u = 0; u < NP; ++u)
+        for (int u = 0; u < NP; ++u)
 #pragma unroll
-                for (int q = 0; q < CPU; ++q) CK::unpack(live[u] ? row[cidx[u][q]] : make_uint4(0, 0, 0, 0), xv[u][q]);
-        }
-        // element k of chunk q of unit u, and its weight
+            for (int q = 0; q < CPU; ++q) CK::unpack(live[u] ? row[cidx[u][q]] : make_uint4(0, 0, 0, 0), xv[u][q]);
         auto elem = [&](int u, int q, float (&t)[E]) {
-            if constexpr (CACHE) {
 #pragma unroll
-                for (int k = 0; k < E; ++k) t[k] = xv[u][q][k];
-            } else {
-                CK::unpack(row[cidx[u][q]], t);
-            }
+            for (int k = 0; k < E; ++k) t[k] = xv[u][q][k];
         };
         auto weight = [&](int u, int q, float (&t)[E]) {
-            if constexpr (CACHE) {
 #pragma unroll
-                for (int k = 0; k < E; ++k) t[k] = wv[u][q][k];
-            } else {
-                CK::unpack(wraw[u][q], t);
-            }
+            for (int k = 0; k < E; ++k) t[k] = wv[u][q][k];
         };
         float ss = 0.f;
         if (NORM) {

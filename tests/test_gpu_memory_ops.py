@@ -377,6 +377,39 @@ def test_rms_norm_rope_llama_config(cuda, oracle):
     assert_scaled(bf16_host(y2)[sel], out, pair, 1e-2, what="rms_norm then rope bf16")
 
 
+@pytest.mark.parametrize("cols,heads", [(8192, 64), (2048, 16)])
+def test_rms_norm_rope_bf16_row_widths(cuda, oracle, cols, heads):
+    """Row widths that take the pipelined kernel at 128 threads (2048 columns, one rotate-half
+    pair of chunks per thread) and at 256 threads (8192 columns, two pairs), fused and RoPE
+    alone, against the oracle on every row."""
+    from bee_b200 import tensor_cuda as tc
+    torch = cuda
+    batch, seq, hd = 2, 48, 128
+    rng = np.random.default_rng(cols)
+    rows = batch * seq
+    x = bf16_round(rng.standard_normal((rows, cols)).astype(np.float32))
+    w = bf16_round((1 + 0.02 * rng.standard_normal(cols)).astype(np.float32))
+    dx, dw = bf16_dev(torch, x), bf16_dev(torch, w)
+    ref = oracle.rms_norm_f32(x, w, 1e-6)
+    want = np.empty_like(ref)
+    for r in range(rows):
+        want[r] = oracle.rope_f32(ref[r:r + 1], 1, heads, hd, 10000.0, r % seq)[0]
+    rr = ref.reshape(rows, heads, hd)
+    pair = np.concatenate([np.abs(rr[..., : hd // 2]) + np.abs(rr[..., hd // 2:])] * 2, -1).reshape(ref.shape)
+    y = torch.empty((rows, cols), dtype=torch.bfloat16, device="cuda")
+    tc.rms_norm_rope(dx, dw, y, seq, heads, hd, 1e-6, 10000.0, 0)
+    assert_scaled(bf16_host(y), want, pair, 1e-2, what=f"rms_norm+rope bf16 x{cols}")
+    # RoPE alone on the same rows (one pass, no sum of squares)
+    y2 = torch.empty_like(y)
+    tc.rope(dx, y2, seq, heads, hd, 10000.0, 0)
+    want2 = np.empty_like(x)
+    for r in range(rows):
+        want2[r] = oracle.rope_f32(x[r:r + 1], 1, heads, hd, 10000.0, r % seq)[0]
+    xr = x.reshape(rows, heads, hd)
+    pair2 = np.concatenate([np.abs(xr[..., : hd // 2]) + np.abs(xr[..., hd // 2:])] * 2, -1).reshape(x.shape)
+    assert_scaled(bf16_host(y2), want2, pair2, 1e-2, what=f"rope bf16 x{cols}")
+
+
 def test_device_selection(cuda):
     import ctypes
     from bee_b200 import _capi
