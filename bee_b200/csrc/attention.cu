@@ -139,7 +139,7 @@ __device__ __forceinline__ float row_max128(const uint32_t (&s)[128]) {
 struct MmaRing {
     uint32_t tmem;
     uint64_t dq[2], dk[2], dv[2];  // descriptors of Q_A / Q_B, K slots, V slots
-    uint64_t *op_full, *op_empty, *s_full, *p_full;
+    uint64_t *op_full, *op_empty, *s_full, *p_full, *o_done;
     volatile int* abort;
     int* status;
     int nkv;
@@ -185,12 +185,18 @@ __device__ __forceinline__ bool mma_block(const MmaRing& r, int j) {
     if (!mbar_wait(&r.p_full[0], static_cast<uint32_t>(j & 1), r.abort, r.status, 26)) return false;
     tc_fence_after();
     issue_o<0, ST>(r, j != 0);
-    if (next) issue_s<0, ST>(r);
+    if (next)
+        issue_s<0, ST>(r);
+    else
+        mma_commit(&r.o_done[0]);  // tile A's epilogue may start while B finishes
     if (NT == 2) {
         if (!mbar_wait(&r.p_full[1], static_cast<uint32_t>(j & 1), r.abort, r.status, 26)) return false;
         tc_fence_after();
         issue_o<1, ST>(r, j != 0);
-        if (next) issue_s<1, ST>(r);
+        if (next)
+            issue_s<1, ST>(r);
+        else
+            mma_commit(&r.o_done[1]);
     }
     mma_commit(&r.op_empty[ST]);
     return true;
@@ -235,6 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
     __shared__ __align__(8) uint64_t op_full[2], op_empty[2];  // ring stage: V_j and K_{j+1}
     __shared__ __align__(8) uint64_t s_full[2], p_full[2];  // [tile]
     __shared__ __align__(8) uint64_t done_bar;
+    __shared__ __align__(8) uint64_t o_done[2];   // [tile]: its last P.V has completed
     __shared__ __align__(8) uint64_t o_ready[2];  // [tile]: its 4 warps have staged O
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
@@ -260,14 +267,24 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
             mbar_init(&p_full[i], 4);  // one arrive per softmax warp of the tile
         }
         mbar_init(&done_bar, 1);
+        mbar_init(&o_done[0], 1);
+        mbar_init(&o_done[1], 1);
         mbar_init(&o_ready[0], 4);
         mbar_init(&o_ready[1], 4);
         abort_sh = 0;
         fence_mbar_init();
-    }
-    if (warp == 0 && lane == 0) {
-        tma_prefetch(&tmQ);
-        tma_prefetch(&tmK);
+        // thread 0 is also the TMA thread: Q_A, Q_B and K_0 (into the K slot of
+        // stage 1) start loading on q_full now, under the TMEM allocation and the
+        // first block barrier
+        mbar_arrive_expect_tx(&q_full, static_cast<uint32_t>((ntiles + (nkv > 0 ? 1 : 0)) * kTile));
+        for (int t = 0; t < ntiles; ++t) {
+            tma_load_3d(sQ + t * kTile, &tmQ, &q_full, 0, q0 + t * kBlock, head);
+            tma_load_3d(sQ + t * kTile + kHalf, &tmQ, &q_full, 64, q0 + t * kBlock, head);
+        }
+        if (nkv > 0) {
+            tma_load_3d(sK + kTile, &tmK, &q_full, 0, 0, head);
+            tma_load_3d(sK + kTile + kHalf, &tmK, &q_full, 64, 0, head);
+        }
         tma_prefetch(&tmV);
         tma_prefetch(&tmO);
     }
@@ -283,16 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
         if (warp == 0) {
             // ------------------------------------------------ TMA producer
             if (lane == 0) {
-                // Q_A, Q_B and K_0 (into the K slot of stage 1) on q_full
-                mbar_arrive_expect_tx(&q_full, static_cast<uint32_t>((ntiles + (nkv > 0 ? 1 : 0)) * kTile));
-                for (int t = 0; t < ntiles; ++t) {
-                    tma_load_3d(sQ + t * kTile, &tmQ, &q_full, 0, q0 + t * kBlock, head);
-                    tma_load_3d(sQ + t * kTile + kHalf, &tmQ, &q_full, 64, q0 + t * kBlock, head);
-                }
-                if (nkv > 0) {
-                    tma_load_3d(sK + kTile, &tmK, &q_full, 0, 0, head);
-                    tma_load_3d(sK + kTile + kHalf, &tmK, &q_full, 64, 0, head);
-                }
+                // (Q_A, Q_B and K_0 were issued with the barrier initialisation)
                 // stage s = j & 1 takes V_j and K_{j+1}; stage 1 is first released
                 // by the MMA that read K_0, so its waits run one phase behind stage 0's
                 int filled = 0;
@@ -326,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
                 const uint64_t dq0 = sdesc_sw128(smem_u32(sQ), 16, 1024), dq1 = sdesc_sw128(smem_u32(sQ + kTile), 16, 1024);
                 const uint64_t dk0 = sdesc_sw128(smem_u32(sK), 16, 1024), dk1 = sdesc_sw128(smem_u32(sK + kTile), 16, 1024);
                 const uint64_t dv0 = sdesc_sw128(smem_u32(sV), kHalf, 1024), dv1 = sdesc_sw128(smem_u32(sV + kTile), kHalf, 1024);
-                MmaRing r{tmem, {dq0, dq1}, {dk0, dk1}, {dv0, dv1}, op_full, op_empty, s_full, p_full, abort_flag, status, nkv};
+                MmaRing r{tmem, {dq0, dq1}, {dk0, dk1}, {dv0, dv1}, op_full, op_empty, s_full, p_full, o_done, abort_flag, status, nkv};
                 bool ok = mbar_wait(&q_full, 0, abort_flag, status, 23);
                 const bool issued = ok && nkv > 0;
                 if (ntiles == 2)
@@ -428,11 +436,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
             l += ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7));
         }
         // epilogue: O / l -> bf16, staged in shared memory (the K slots are free
-        // once every MMA has completed) in the 128-byte-swizzled layout of the
+        // once the tile's last P.V has completed: every MMA that reads K was
+        // issued before it, and the tensor core retires them in order) in the
+        // 128-byte-swizzled layout of the
         // tensor map, then written by two TMA stores per tile: 16-byte stores
         // from registers, one row per thread, took ~4000 cycles per CTA
         if (ok && nkv > 0) {
-            ok = mbar_wait(&done_bar, 0, abort_flag, status, 32);
+            ok = mbar_wait(&o_done[t], 0, abort_flag, status, 32);
             if (__all_sync(0xffffffffu, ok)) {
                 tc_fence_after();
                 const float inv = 1.0f / l;
