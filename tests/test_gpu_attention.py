@@ -87,6 +87,26 @@ def test_attention_config_sampled_rows(cuda):
     assert_scaled(got[:, rows], want, cond, 1e-2, what="attention config rows")
 
 
+@pytest.mark.parametrize("heads,seq", [(2, 8192), (3, 4224)])
+def test_attention_long_sequences_sampled_rows(cuda, heads, seq):
+    """Long rows: 64 and 33 key blocks, so the two-stage K/V ring and the block
+    pairs of the MMA loop go through many phases (and, at 4224 = 33 x 128, end on
+    an odd block with an odd tile count); 48 sampled query rows per head against
+    float64."""
+    torch = cuda
+    hd = 128
+    q, k, v = _inputs(seq + heads, heads, seq, hd)
+    scale = float(1 / np.sqrt(hd))
+    got = _run(torch, q, k, v, scale)
+    rows = np.unique(np.concatenate([np.random.default_rng(seq).choice(seq, 46, replace=False), [0, seq - 1]]))
+    s_ = np.einsum("hid,hjd->hij", q[:, rows].astype(np.float64), k.astype(np.float64)) * scale
+    s_ -= s_.max(-1, keepdims=True)
+    pm = np.exp(s_)
+    pm /= pm.sum(-1, keepdims=True)
+    want = pm @ v.astype(np.float64)
+    assert_output_close(got[:, rows], want, 1e-2, what=f"attention {heads}x{seq} sampled rows", elementwise_rtol=2e-2)
+
+
 def test_attention_rejects_unsupported_shapes(cuda):
     from bee_b200 import _capi
     torch = cuda
