@@ -1097,12 +1097,82 @@ static int matmul_f32_split(const float* A, const float* B, float* C, size_t M, 
 
 using namespace bee_b200;
 
+// Sum of the S K-chunk partials of a split product, in chunk order (so the result
+// does not depend on timing), times alpha, rounded to the output type (n % 4 == 0).
+__global__ void __launch_bounds__(256) sum_ksplit_kernel(const float* __restrict__ part, void* __restrict__ C, int S,
+                                                         size_t n, float alpha, int out_dt) {
+    for (size_t i = (blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x) * 4; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x * 4) {
+        float4 acc = *reinterpret_cast<const float4*>(part + i);
+        for (int s = 1; s < S; ++s) {
+            const float4 v = *reinterpret_cast<const float4*>(part + static_cast<size_t>(s) * n + i);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        acc.x *= alpha;
+        acc.y *= alpha;
+        acc.z *= alpha;
+        acc.w *= alpha;
+        if (out_dt == DT_F32) {
+            *reinterpret_cast<float4*>(static_cast<float*>(C) + i) = acc;
+        } else {
+            const bool h = out_dt == DT_F16;
+            uint2 o;
+            o.x = h ? pack_f16x2(acc.x, acc.y) : pack_bf16x2(acc.x, acc.y);
+            o.y = h ? pack_f16x2(acc.z, acc.w) : pack_bf16x2(acc.z, acc.w);
+            *reinterpret_cast<uint2*>(static_cast<uint16_t*>(C) + i) = o;
+        }
+    }
+}
+
+// One 16-bit product whose output tiles would leave most SMs idle (small M or
+// N, long K): K is cut into S chunks that run as the S entries of a batched
+// product on 128 x 128 tiles (each chunk a view of A and B at an offset, fp32
+// partials in pool scratch), then summed in chunk order.  Returns -1 when the
+// shape does not qualify or the chunk views cannot be described by TMA.
+static int bmm_ksplit(int dt_in, int dt_out, const void* A, const void* B, void* C, size_t M, size_t K, size_t N,
+                      int b_trans, float alpha, const BmmStrides& sd, cudaStream_t st) {
+    const size_t sms = static_cast<size_t>(sm_count());
+    const size_t tiles = ((M + 127) / 128) * ((N + 127) / 128);
+    if (sd.ldc != static_cast<long long>(N) || (M * N) % 4 != 0 || !aligned16(C)) return -1;
+    if (K % 128 != 0 || K < 2048 || tiles * 2 > sms) return -1;
+    // S divides the 128-wide K stages, fills at most the GPU, keeps chunks >= 1024 long
+    const size_t kb = K / 128;
+    size_t S = 1;
+    for (size_t cand = 2; cand <= 8; ++cand)
+        if (kb % cand == 0 && tiles * cand <= sms && K / cand >= 1024) S = cand;
+    if (S < 2) return -1;
+    const size_t Kc = K / S;
+    void* mem = nullptr;
+    cudaError_t e = pool_malloc(&mem, S * M * N * sizeof(float), st);
+    if (e != cudaSuccess) return api_fail(e, "bmm (K split): scratch of %zu bytes: %s", S * M * N * sizeof(float),
+                                          cudaGetErrorString(e));
+    float* part = static_cast<float*>(mem);
+    const BmmStrides ps{sd.lda, sd.ldb, static_cast<long long>(N), static_cast<long long>(Kc),
+                        b_trans ? static_cast<long long>(Kc) : static_cast<long long>(Kc) * sd.ldb,
+                        static_cast<long long>(M * N)};
+    int rc = bmm_bf16_tc(DT_F32, A, B, part, S, M, Kc, N, b_trans, 1.0f, ps, st, true, dt_in);
+    if (rc == 0) {
+        const size_t work = (M * N / 4 + 255) / 256, cap = sms * 8;
+        sum_ksplit_kernel<<<static_cast<unsigned>(work < cap ? work : cap), 256, 0, st>>>(part, C, static_cast<int>(S), M * N,
+                                                                                       alpha, dt_out);
+        rc = launch_status("bmm (K split sum)");
+    }
+    cudaError_t e2 = cudaFreeAsync(mem, st);
+    if (rc == 0 && e2 != cudaSuccess) rc = api_fail(e2, "bmm (K split): %s", cudaGetErrorString(e2));
+    return rc;
+}
+
 static int bmm_impl(int dt_in, int dt_out, const void* A, const void* B, void* C, size_t batch, size_t M, size_t K,
                     size_t N, int b_trans, float alpha, const BmmStrides& sd, cudaStream_t st) {
     if (dt_in == DT_BF16) {
         if (dt_out != DT_BF16 && dt_out != DT_F32)
             return fail(cudaErrorInvalidValue, "bmm: bf16 input needs a BF16 or F32 output, got %d", dt_out);
-        int rc = K == 0 ? -1 : bmm_bf16_tc(dt_out, A, B, C, batch, M, K, N, b_trans, alpha, sd, st);
+        int rc = K == 0 || batch != 1 ? -1 : bmm_ksplit(dt_in, dt_out, A, B, C, M, K, N, b_trans, alpha, sd, st);
+        if (rc != -1) return rc;
+        rc = K == 0 ? -1 : bmm_bf16_tc(dt_out, A, B, C, batch, M, K, N, b_trans, alpha, sd, st);
         if (rc != -1) return rc;
         return dt_out == DT_F32 ? launch_simt<uint16_t, float>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st)
                                 : launch_simt<uint16_t, uint16_t>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st);
@@ -1110,7 +1180,9 @@ static int bmm_impl(int dt_in, int dt_out, const void* A, const void* B, void* C
     if (dt_in == DT_F16) {
         if (dt_out != DT_F16 && dt_out != DT_F32)
             return fail(cudaErrorInvalidValue, "bmm: f16 input needs an F16 or F32 output, got %d", dt_out);
-        int rc = K == 0 ? -1 : bmm_bf16_tc(dt_out, A, B, C, batch, M, K, N, b_trans, alpha, sd, st, false, DT_F16);
+        int rc = K == 0 || batch != 1 ? -1 : bmm_ksplit(dt_in, dt_out, A, B, C, M, K, N, b_trans, alpha, sd, st);
+        if (rc != -1) return rc;
+        rc = K == 0 ? -1 : bmm_bf16_tc(dt_out, A, B, C, batch, M, K, N, b_trans, alpha, sd, st, false, DT_F16);
         if (rc != -1) return rc;
         return dt_out == DT_F32 ? launch_simt<__half, float>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st)
                                 : launch_simt<__half, __half>(A, B, C, batch, M, K, N, b_trans, alpha, sd, st);

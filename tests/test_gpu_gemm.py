@@ -212,6 +212,24 @@ def test_bf16_gemm_b_transposed_f32_out(cuda, oracle, m, k, n):
     assert_dot_close(got, want, af * 0.125, bf, 1e-4, what="bf16 gemm fp32 out")
 
 
+@pytest.mark.parametrize("m,k,n,b_trans,out_f32", [(128, 4096, 4096, False, False), (64, 8192, 2048, False, True),
+                                                    (96, 2048, 1024, True, True), (128, 3072, 8192, True, False),
+                                                    (256, 2048, 256, False, False)])
+def test_bf16_gemm_k_split(cuda, m, k, n, b_trans, out_f32):
+    """Outputs too small to fill the GPU with long K run as K chunks (fp32
+    partials summed in chunk order): against float64 on the output's own scale,
+    fp32 output at 1e-4, bf16 output at 1e-2."""
+    torch = cuda
+    rng = np.random.default_rng(m + k + n)
+    a = rand_bf16(rng, (m, k))
+    b = rand_bf16(rng, (n, k) if b_trans else (k, n))
+    got = run_bmm(torch, a, b, 1, m, k, n, b_trans=b_trans, out_f32=out_f32, alpha=0.5)[0]
+    af = bf16_bits_to_f32(a)
+    bf = bf16_bits_to_f32(b).T if b_trans else bf16_bits_to_f32(b)
+    want = 0.5 * f64_product(af, bf)
+    assert_output_close(got, want, 1e-4 if out_f32 else 1e-2, what=f"bf16 gemm K split {m}x{k}x{n}")
+
+
 def test_bf16_bmm_batched(cuda, oracle):
     torch = cuda
     rng = np.random.default_rng(77)
