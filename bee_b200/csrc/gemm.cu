@@ -83,6 +83,13 @@ __device__ __forceinline__ void grouped_tile(int t, int m_tiles, int n_tiles, in
     nb = r / gsize;
 }
 
+// K order of a persistent CTA's i-th tile: forward for even i, backward for odd
+// i.  The CTAs move through their tiles together, so the tiles of one wave
+// start on the K blocks the previous wave (which shares their A panels under
+// the grouped raster) read last, while those are still in L2.  The MMA side
+// accumulates in iteration order whatever the coordinate.
+__device__ __forceinline__ int k_block(int kb, int i, int num_kb) { return (i & 1) ? num_kb - 1 - kb : kb; }
+
 __device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& b, int& mb, int& nb) {
     b = tile / p.tiles_per_batch;
     grouped_tile(tile - b * p.tiles_per_batch, p.m_tiles, p.n_tiles, mb, nb);
@@ -194,7 +201,7 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tcgen05_kernel(const __grid_
                     uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
                     uint8_t* sb = sa + Cfg::A_BYTES;
                     mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
-                    const int k0 = kb * Cfg::BK;
+                    const int k0 = k_block(kb, tile / static_cast<int>(gridDim.x), p.num_kb) * Cfg::BK;
 #pragma unroll
                     for (int h = 0; h < Cfg::BK / 64; ++h)
                         tma_load_3d(sa + h * Cfg::K_HALF, &tmA, &full_bar[stage], k0 + h * 64, mb * Cfg::BM, b);
@@ -408,7 +415,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
                     if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::STAGE_BYTES);
                     const int m0 = mb * Cfg::BM + static_cast<int>(rank) * 128;
                     const int n0 = nb * Cfg::BN + static_cast<int>(rank) * 128;
-                    const int k0 = kb * Cfg::BK;
+                    const int k0 = k_block(kb, tile / npairs, p.num_kb) * Cfg::BK;
                     tma_load_3d_pair(sa, &tmA, full_leader, k0, m0, b);
                     tma_load_3d_pair(sa + Cfg::A_HALF, &tmA, full_leader, k0 + 64, m0, b);
                     if constexpr (B_KMAJOR) {
