@@ -107,6 +107,35 @@ def test_attention_long_sequences_sampled_rows(cuda, heads, seq):
     assert_output_close(got[:, rows], want, 1e-2, what=f"attention {heads}x{seq} sampled rows", elementwise_rtol=2e-2)
 
 
+@pytest.mark.parametrize("heads,seq", [(20, 2048), (10, 4224), (150, 256), (37, 2048)])
+def test_attention_persistent_schedules(cuda, heads, seq):
+    """More units (a head's pair of query tiles) than SMs.  On a 148-SM B200,
+    20 x 2048 (160 units, a last wave of 12) and 10 x 4224 (170 units of 33 key
+    blocks, single-tile units among them) run as one persistent CTA per SM, each
+    taking an equal share of the (unit, key block) sequence, so most shares end
+    inside a unit and its two pieces are merged; 150 x 256 (units of two key
+    blocks) and 37 x 2048 (two whole waves) keep one CTA per unit.  Three query
+    rows in every 128-row tile (so every piece of every cut unit) against
+    float64, and two calls must agree bit for bit (the merge does not depend on
+    which piece finishes first)."""
+    torch = cuda
+    hd = 128
+    q, k, v = _inputs(heads * 7 + seq, heads, seq, hd)
+    scale = float(1 / np.sqrt(hd))
+    got = _run(torch, q, k, v, scale)
+    again = _run(torch, q, k, v, scale)
+    assert np.array_equal(got, again), "two calls on the same inputs differ"
+    rng = np.random.default_rng(seq + heads)
+    rows = np.sort(np.concatenate([t * 128 + rng.choice(128, 3, replace=False) for t in range(seq // 128)]))
+    s_ = np.einsum("hid,hjd->hij", q[:, rows].astype(np.float64), k.astype(np.float64)) * scale
+    s_ -= s_.max(-1, keepdims=True)
+    pm = np.exp(s_)
+    pm /= pm.sum(-1, keepdims=True)
+    want = pm @ v.astype(np.float64)
+    assert_output_close(got[:, rows], want, 1e-2, what=f"attention {heads}x{seq} persistent", elementwise_rtol=2e-2)
+    assert_scaled(got[:, rows], want, pm @ np.abs(v.astype(np.float64)), 1e-2, what=f"attention {heads}x{seq} persistent")
+
+
 def test_attention_rejects_unsupported_shapes(cuda):
     from bee_b200 import _capi
     torch = cuda
