@@ -426,6 +426,30 @@ def run_ours(args, d: Dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         per_op_ms = {n: float(v) for (n, _), v in zip(ops, t.tolist())}
 
+    # Each op alone (outside the timed region): the same kernel 3 + 10 times back to back,
+    # so no other op's dirty L2 lines are written back during it.  Inside the step, a
+    # reader that follows a writer (row sum after the cast, the int32 sum after the
+    # softmax) also moves the writer's last ~30-40 MB of dirty lines to DRAM.
+    alone_ms = {}
+    slot[0] = ring.numel() - 1
+    for name, fn in ops:
+        if name == "sum_i32":  # the local reduce alone, without the cross-GPU exchange
+            fn = lambda: call("bee_b200_reduce_global", 0, I32, dxi.data_ptr(), ring[slot[0]].data_ptr(), N_EL, st)
+        for _ in range(3):
+            fn()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(10):
+            fn()
+        a1.record(stream)
+        stream.synchronize()
+        alone_ms[name] = a0.elapsed_time(a1) / 10
+    if d.world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([alone_ms[n] for n, _ in ops], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        alone_ms = {n: float(v) for (n, _), v in zip(ops, t.tolist())}
+
     ms_per_step = ms / args.steps
     value = d.world * STEP_BYTES * args.steps / (ms / 1e3) / 1e9
     dominant = max(per_op_ms, key=per_op_ms.get)
@@ -472,8 +496,13 @@ def run_ours(args, d: Dist):
     out = None
     if d.rank == 0:
         ops_json = {n: {"ms": round(per_op_ms[n], 4), "GB/s": round(OP_BYTES[n] / (per_op_ms[n] / 1e3) / 1e9, 1),
-                        "frac_of_hbm": round(OP_BYTES[n] / (per_op_ms[n] / 1e3) / 1e9 / peaks["hbm_gbs"], 3)}
+                        "frac_of_hbm": round(OP_BYTES[n] / (per_op_ms[n] / 1e3) / 1e9 / peaks["hbm_gbs"], 3),
+                        "alone_ms": round(alone_ms[n], 4),
+                        "alone_frac_of_hbm": round(OP_BYTES[n] / (alone_ms[n] / 1e3) / 1e9 / peaks["hbm_gbs"], 3)}
                     for n, _ in ops}
+        ops_note = ("ms / frac_of_hbm: inside the timed step, where a reader that follows a writer also "
+                            "writes the writer's dirty L2 lines back to DRAM; alone_*: the same kernel repeated "
+                            "back to back after the timed region")
         out = {
             "metric": "memory-bound op sweep HBM GB/s (add, mul, fp32->bf16 cast, row sum, row max, row softmax, "
                       "int32 full sum) on [8192, 8192] row shards",
@@ -487,6 +516,7 @@ def run_ours(args, d: Dist):
                          "traffic": NCU_TRAFFIC.get(dominant),
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch"},
             "ops": ops_json,
+            "ops_note": ops_note,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "e2e": e2e,
