@@ -225,7 +225,8 @@ BEE_B200_API int bee_b200_rms_norm_rope(int dt, const void* x, const void* w, vo
 
 /* C[M,N] = A[M,K] . B[K,N], row-major contiguous, same dtype.
  * BF16 / F16: tcgen05 tensor cores with fp32 accumulation and a bf16 / f16
- * (RNE) result (F16 outputs beyond its range are +-inf);
+ * (RNE) result (F16 outputs beyond its range are +-inf; small outputs with a
+ * long K are cut along K as in bee_b200_bmm);
  * F32 from 2^28 multiply-adds up (K and N multiples of 8, 16-byte aligned
  * buffers): every value split into three bf16 pieces, six piece products on
  * the same tensor cores with fp32 accumulation (fp32-level error; rows and
@@ -245,7 +246,12 @@ BEE_B200_API int bee_b200_matmul(int dt, const void* A, const void* B, void* C, 
  * Q.K^T reads K as stored); C [batch, M, N].  dt_in BF16 with dt_out BF16 or
  * F32, and dt_in F16 with dt_out F16 or F32, run on the tensor cores (TMA needs K % 8 == 0, N % 8 == 0 unless
  * b_trans, 16-byte aligned A and B; other shapes use the SIMT kernel); other
- * dtypes need dt_out == dt_in.  New: the reference matmul is 2-D only
+ * dtypes need dt_out == dt_in.  A single 16-bit product (batch 1, and for
+ * bmm_strided ldc == N) whose 128x128 output tiles number at most half the
+ * SMs, with K a multiple of 128 and at least 2048, is cut along K into S <= 8
+ * chunks computed side by side: 4*S*M*N bytes of fp32 partials from the
+ * stream-ordered pool, summed in chunk order (results do not depend on
+ * timing).  New: the reference matmul is 2-D only
  * (Bee/Tensor/Ops/Matmul.cpp:63-64). */
 BEE_B200_API int bee_b200_bmm(int dt_in, int dt_out, const void* A, const void* B, void* C, size_t batch, size_t M,
                               size_t K, size_t N, int b_trans, float alpha, bee_b200_stream_t stream);
@@ -269,7 +275,13 @@ BEE_B200_API int bee_b200_bmm_strided(int dt_in, int dt_out, const void* A, int6
  * bf16, contiguous, 16-byte aligned.  One pass: scores and probabilities stay
  * in tensor memory.  head_dim must be 128, seq a multiple of 128 and scale
  * positive (other shapes: compose bee_b200_bmm, bee_b200_softmax_rows_to and
- * bee_b200_bmm).  New: the reference has no attention. */
+ * bee_b200_bmm).  With more units (a head's pair of query tiles) than SMs and a
+ * last wave that would leave most SMs idle, one persistent CTA per SM runs an
+ * equal share of the work instead; the call then takes about 260 KiB per SM of
+ * scratch from the stream-ordered pool (released on the stream after the
+ * launch) and keeps a 4 KiB block of tickets per stream for the life of the
+ * process (during stream capture it keeps one CTA per unit).  The result does
+ * not depend on timing.  New: the reference has no attention. */
 BEE_B200_API int bee_b200_attention(int dt, const void* q, const void* k, const void* v, void* o, size_t heads,
                                     size_t seq, size_t head_dim, float scale, bee_b200_stream_t stream);
 
