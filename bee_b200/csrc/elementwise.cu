@@ -91,6 +91,7 @@ __global__ void __launch_bounds__(kThreads) binary_kernel(const S* __restrict__ 
     uint4* vo = reinterpret_cast<uint4*>(out);
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    pdl_wait();
     for (; i + (kUnroll - 1) * stride < nvec; i += kUnroll * stride) {
         uint4 x[kUnroll], y[kUnroll];
 #pragma unroll
@@ -101,6 +102,7 @@ __global__ void __launch_bounds__(kThreads) binary_kernel(const S* __restrict__ 
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) st_stream_u4(vo + i + u * stride, vec_bin<S, OP>(x[u], y[u]));
     }
+    pdl_trigger();
     for (; i < nvec; i += stride) st_stream_u4(vo + i, vec_bin<S, OP>(ld_stream_u4(va + i), ld_stream_u4(vb + i)));
     if (blockIdx.x == 0)
         for (size_t j = nvec * E + threadIdx.x; j < n; j += blockDim.x) out[j] = from_c<S>(bin<OP>(to_c(a[j]), to_c(b[j])));
@@ -261,6 +263,7 @@ __global__ void __launch_bounds__(kThreads) cast_f32_bf16_kernel(const float* __
     uint4* vd = reinterpret_cast<uint4*>(dst);
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    pdl_wait();
     for (; i + (kUnroll - 1) * stride < nvec; i += kUnroll * stride) {
         float4 x[kUnroll][2];
 #pragma unroll
@@ -278,6 +281,7 @@ __global__ void __launch_bounds__(kThreads) cast_f32_bf16_kernel(const float* __
             st_stream_u4(vd + i + u * stride, o);
         }
     }
+    pdl_trigger();
     for (; i < nvec; i += stride) {
         float4 p = ld_stream(vs + 2 * i), q = ld_stream(vs + 2 * i + 1);
         uint4 o;
@@ -348,7 +352,8 @@ static void launch_binary(const void* a, const void* b, void* out, size_t n, cud
     const S* pb = static_cast<const S*>(b);
     S* po = static_cast<S*>(out);
     if (aligned16(a) && aligned16(b) && aligned16(out))
-        binary_kernel<S, OP><<<grid_for((n * sizeof(S) / 16 + kUnroll - 1) / kUnroll), kThreads, 0, st>>>(pa, pb, po, n);
+        launch_pdl(binary_kernel<S, OP>, grid_for((n * sizeof(S) / 16 + kUnroll - 1) / kUnroll), kThreads, 0, st, pa, pb,
+                   po, n);
     else
         binary_scalar_kernel<S, OP><<<grid_for(n), kThreads, 0, st>>>(pa, pb, po, n);
 }
@@ -551,8 +556,8 @@ int bee_b200_ew_cast(int src_dt, const void* src, int dst_dt, void* dst, size_t 
     if (!src || !dst) return fail(cudaErrorInvalidValue, "ew_cast: null pointer");
     cudaStream_t st = as_stream(stream);
     if (src_dt == DT_F32 && dst_dt == DT_BF16 && aligned16(src) && aligned16(dst)) {
-        cast_f32_bf16_kernel<<<grid_for((n / 8 + kUnroll - 1) / kUnroll), kThreads, 0, st>>>(
-            static_cast<const float*>(src), static_cast<uint16_t*>(dst), n);
+        launch_pdl(cast_f32_bf16_kernel, grid_for((n / 8 + kUnroll - 1) / kUnroll), kThreads, 0, st,
+                   static_cast<const float*>(src), static_cast<uint16_t*>(dst), n);
         return launch_status("ew_cast");
     }
     if (src_dt == DT_BF16 && dst_dt == DT_F32 && aligned16(src) && aligned16(dst)) {

@@ -31,6 +31,8 @@ __global__ void __launch_bounds__(256) reduce_rows_cta_kernel(const typename P::
                                                               typename P::Out* __restrict__ dst, size_t rows,
                                                               size_t axis) {
     __shared__ typename P::Acc smem[32];
+    pdl_wait();
+    pdl_trigger();  // counts once every CTA (all waves) has started
     for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
         typename P::Acc v = strided_reduce<P, 8>(src + r * axis, 0, axis, threadIdx.x, blockDim.x);
         v = block_reduce<P>(v, smem);
@@ -45,11 +47,13 @@ __global__ void __launch_bounds__(256) reduce_rows_warp_kernel(const typename P:
                                                                size_t axis) {
     const size_t warps = static_cast<size_t>(gridDim.x) * (blockDim.x >> 5);
     const int lane = threadIdx.x & 31;
+    pdl_wait();
     for (size_t r = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
         typename P::Acc v = strided_reduce<P>(src + r * axis, 0, axis, lane, 32);
         v = warp_reduce<P>(v);
         if (lane == 0) dst[r] = P::finish(v, axis);
     }
+    pdl_trigger();
 }
 
 // Cross-CTA combine of a split reduction: `count` CTAs publish partials of one
@@ -272,8 +276,8 @@ static int run_global(const void* src, void* dst, size_t n, cudaStream_t st) {
     void* scratch = nullptr;
     if (bytes <= kStreamScratchBytes && stream_scratch(st, &scratch) == 0) {
         cudaGetLastError();  // a failed probe above must not be reported as a launch error
-        reduce_global_kernel<P><<<grid, kGlobalThreads, 0, st>>>(static_cast<const In*>(src), static_cast<Out*>(dst), n,
-                                                                 static_cast<GlobalScratch*>(scratch));
+        launch_pdl(reduce_global_kernel<P>, grid, kGlobalThreads, 0, st, static_cast<const In*>(src), static_cast<Out*>(dst),
+                   n, static_cast<GlobalScratch*>(scratch));
         return launch_status("reduce_global");
     }
     cudaGetLastError();
@@ -338,11 +342,11 @@ static int run_axis(const void* src, void* dst, size_t outer, size_t axis, size_
         }
         if (axis >= 2048) {
             const size_t grid = outer < (size_t(1) << 30) ? outer : (size_t(1) << 30);
-            reduce_rows_cta_kernel<P><<<static_cast<unsigned>(grid), 256, 0, st>>>(s, d, outer, axis);
+            launch_pdl(reduce_rows_cta_kernel<P>, static_cast<unsigned>(grid), 256, 0, st, s, d, outer, axis);
         } else {
             size_t grid = (outer + 7) / 8;
             if (grid > cap) grid = cap;
-            reduce_rows_warp_kernel<P><<<static_cast<unsigned>(grid), 256, 0, st>>>(s, d, outer, axis);
+            launch_pdl(reduce_rows_warp_kernel<P>, static_cast<unsigned>(grid), 256, 0, st, s, d, outer, axis);
         }
         return launch_status("reduce_axis");
     }

@@ -174,6 +174,7 @@ __global__ void __launch_bounds__(kGlobalThreads) reduce_global_kernel(const typ
     Acc* partials = reinterpret_cast<Acc*>(scratch + 1);
     const unsigned tid = threadIdx.x;
     Acc acc = P::identity();
+    pdl_wait();
     if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
         const uint4* v = reinterpret_cast<const uint4*>(src);
         const size_t nvec = n / E;
@@ -198,6 +199,7 @@ __global__ void __launch_bounds__(kGlobalThreads) reduce_global_kernel(const typ
         for (size_t j = static_cast<size_t>(blockIdx.x) * kGlobalThreads + tid; j < n; j += stride)
             acc = P::add(acc, src[j]);
     }
+    pdl_trigger();
     acc = block_reduce<P>(acc, smem);
     if (tid == 0) {
         partials[blockIdx.x] = acc;

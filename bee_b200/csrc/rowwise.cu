@@ -122,7 +122,9 @@ template <typename Ti, typename To, int THREADS, int NQ>
 __global__ void __launch_bounds__(THREADS) softmax_rows_kernel(const Ti* __restrict__ src, To* __restrict__ dst,
                                                                size_t rows, size_t cols, int vec) {
     __shared__ float red[THREADS / 32];
+    pdl_wait();
     for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        if (r + gridDim.x >= rows) pdl_trigger();  // this CTA's last row
         float v[NQ][4];
         load_row<Ti, THREADS, NQ>(src + r * cols, cols, vec, -INFINITY, v);
         float m = -INFINITY;
@@ -555,10 +557,14 @@ static int launch_softmax(const void* src, void* dst, size_t rows, size_t cols, 
     To* d = static_cast<To*>(dst);
     const int vec = (cols % 4 == 0) && aligned16(src) && aligned16(dst) ? 1 : 0;
     // Register-resident variants: up to 32 fp32 values per thread.
-    if (cols <= 256 * 4) softmax_rows_kernel<Ti, To, 256, 1><<<row_grid(rows, 8), 256, 0, st>>>(s, d, rows, cols, vec);
-    else if (cols <= 256 * 4 * 4) softmax_rows_kernel<Ti, To, 256, 4><<<row_grid(rows, 8), 256, 0, st>>>(s, d, rows, cols, vec);
-    else if (cols <= 256 * 4 * 8) softmax_rows_kernel<Ti, To, 256, 8><<<row_grid(rows, 8), 256, 0, st>>>(s, d, rows, cols, vec);
-    else if (cols <= 1024 * 4 * 8) softmax_rows_kernel<Ti, To, 1024, 8><<<row_grid(rows, 2), 1024, 0, st>>>(s, d, rows, cols, vec);
+    if (cols <= 256 * 4)
+        launch_pdl(softmax_rows_kernel<Ti, To, 256, 1>, row_grid(rows, 8), 256, 0, st, s, d, rows, cols, vec);
+    else if (cols <= 256 * 4 * 4)
+        launch_pdl(softmax_rows_kernel<Ti, To, 256, 4>, row_grid(rows, 8), 256, 0, st, s, d, rows, cols, vec);
+    else if (cols <= 256 * 4 * 8)
+        launch_pdl(softmax_rows_kernel<Ti, To, 256, 8>, row_grid(rows, 8), 256, 0, st, s, d, rows, cols, vec);
+    else if (cols <= 1024 * 4 * 8)
+        launch_pdl(softmax_rows_kernel<Ti, To, 1024, 8>, row_grid(rows, 2), 1024, 0, st, s, d, rows, cols, vec);
     else softmax_rows_long_kernel<Ti, To><<<row_grid(rows, 2), 1024, 0, st>>>(s, d, rows, cols);
     return launch_status("softmax_rows");
 }
