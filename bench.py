@@ -409,7 +409,9 @@ def run_ours(args, d: Dist):
             if k in probe_at and not args.no_clocks and args.clock_source != "nvml":
                 call("bee_b200_clock_probe", 200_000, probe_buf[np_i].data_ptr(), probe_stream.cuda_stream)
                 np_i += 1
-            step(args.warmup + k, per_step_events[k])
+            # nothing between the kernels of a step: an event recorded between two
+            # kernels would stop the next one's early (programmatic) launch
+            step(args.warmup + k)
         if comm is not None:
             stream.wait_stream(comm)  # every step's exchange is inside the timed region
         t1.record(stream)
@@ -418,6 +420,19 @@ def run_ours(args, d: Dist):
     torch.cuda.synchronize()
     ms_local = t0.elapsed_time(t1)
     ms = d.max(ms_local)
+    # Per-op breakdown (and the roofline's kernel duration): the same steps again,
+    # with an event between ops; the events keep each kernel from starting before
+    # the previous one ends, so this pass is slightly slower than the region above.
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record(stream)
+    for k in range(args.steps):
+        step(args.warmup + k, per_step_events[k])
+    if comm is not None:
+        stream.wait_stream(comm)
+    b1.record(stream)
+    stream.synchronize()
+    d.barrier()
+    breakdown_ms_per_step = d.max(b0.elapsed_time(b1)) / args.steps
     per_op_ms = {name: sum(ev[i].elapsed_time(ev[i + 1]) for ev in per_step_events) / args.steps
                  for i, (name, _) in enumerate(ops)}
     if d.world > 1:
@@ -500,9 +515,10 @@ def run_ours(args, d: Dist):
                         "alone_ms": round(alone_ms[n], 4),
                         "alone_frac_of_hbm": round(OP_BYTES[n] / (alone_ms[n] / 1e3) / 1e9 / peaks["hbm_gbs"], 3)}
                     for n, _ in ops}
-        ops_note = ("ms / frac_of_hbm: inside the timed step, where a reader that follows a writer also "
-                            "writes the writer's dirty L2 lines back to DRAM; alone_*: the same kernel repeated "
-                            "back to back after the timed region")
+        ops_note = ("ms / frac_of_hbm: a second pass of the same steps with an event between ops "
+                    f"({round(breakdown_ms_per_step, 4)} ms per step; the events also stop each kernel's early "
+                    "launch), where a reader that follows a writer also writes the writer's dirty L2 lines back "
+                    "to DRAM; alone_*: the same kernel repeated back to back after the timed region")
         out = {
             "metric": "memory-bound op sweep HBM GB/s (add, mul, fp32->bf16 cast, row sum, row max, row softmax, "
                       "int32 full sum) on [8192, 8192] row shards",
