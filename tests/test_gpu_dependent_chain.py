@@ -1,0 +1,70 @@
+"""Dependent ops back to back on one stream.  The streaming kernels (binary,
+fp32->bf16 cast, row and global reduce, row softmax) are launched so that the
+next one may start while the previous one finishes, and each waits for its
+predecessor before touching memory.  A chain in which every op reads the
+previous op's output, and the next round overwrites buffers the previous
+round read, must give bit for bit what the same chain gives with a device
+synchronise after every op."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ADD, SUB, MUL, DIV = 0, 1, 2, 3
+SUM, MAX = 0, 2
+
+
+def _chain(torch, capi, x, y, xi, bufs, rounds, sync):
+    """Per round: a = x + y; b = a * y; c = b - a (reads both); h = bf16(c);
+    r = rowsum(c); m = rowmax(b); s = softmax(c); w = xi + 1; t = int32 sum of w."""
+    a, b, c, h, r, m, s, t, one, w = bufs
+    st = torch.cuda.current_stream().cuda_stream
+    rows, cols = x.shape
+    n = x.numel()
+
+    def op(name, *args):
+        capi.call(name, *args)
+        if sync:
+            torch.cuda.synchronize()
+
+    for _ in range(rounds):
+        op("bee_b200_ew_binary", ADD, capi.F32, x.data_ptr(), y.data_ptr(), a.data_ptr(), n, st)
+        op("bee_b200_ew_binary", MUL, capi.F32, a.data_ptr(), y.data_ptr(), b.data_ptr(), n, st)
+        op("bee_b200_ew_binary", SUB, capi.F32, b.data_ptr(), a.data_ptr(), c.data_ptr(), n, st)
+        op("bee_b200_ew_cast", capi.F32, c.data_ptr(), capi.BF16, h.data_ptr(), n, st)
+        op("bee_b200_reduce_axis", SUM, capi.F32, c.data_ptr(), r.data_ptr(), rows, cols, 1, st)
+        op("bee_b200_reduce_axis", MAX, capi.F32, b.data_ptr(), m.data_ptr(), rows, cols, 1, st)
+        op("bee_b200_softmax_rows", capi.F32, c.data_ptr(), s.data_ptr(), rows, cols, st)
+        op("bee_b200_ew_binary", ADD, capi.I32, xi.data_ptr(), one.data_ptr(), w.data_ptr(), n, st)
+        op("bee_b200_reduce_global", SUM, capi.I32, w.data_ptr(), t.data_ptr(), n, st)
+    torch.cuda.synchronize()
+    return [v.cpu().clone() for v in (a, b, c, h, r, m, s, t, w)]
+
+
+@pytest.mark.parametrize("rows,cols", [(4096, 4096), (333, 8200)])
+def test_dependent_chain_matches_synchronised_chain(cuda, rows, cols):
+    torch = cuda
+    from bee_b200 import _capi
+    g = torch.Generator(device="cuda").manual_seed(rows + cols)
+    x = torch.randn(rows, cols, device="cuda", generator=g)
+    y = torch.randn(rows, cols, device="cuda", generator=g)
+    xi0 = torch.randint(-1000, 1001, (rows, cols), device="cuda", dtype=torch.int32, generator=g)
+    one = torch.ones(rows, cols, device="cuda", dtype=torch.int32)
+
+    def fresh():
+        return (torch.empty_like(x), torch.empty_like(x), torch.empty_like(x),
+                torch.empty(rows, cols, device="cuda", dtype=torch.bfloat16), torch.empty(rows, device="cuda"),
+                torch.empty(rows, device="cuda"), torch.empty_like(x), torch.zeros(1, device="cuda", dtype=torch.int32),
+                one, torch.empty_like(xi0))
+
+    got = _chain(torch, _capi, x, y, xi0, fresh(), 20, sync=False)
+    want = _chain(torch, _capi, x, y, xi0, fresh(), 20, sync=True)
+    names = ["add", "mul", "sub", "cast", "row sum", "row max", "softmax", "int32 sum", "int32 add"]
+    for nm, g_, w_ in zip(names, got, want):
+        assert torch.equal(g_, w_), f"{nm}: the back-to-back chain differs from the synchronised one"
+    # and what the chain computes is right where it is exact
+    xs, ys = x.cpu(), y.cpu()
+    assert torch.equal(got[0], xs + ys) and torch.equal(got[1], (xs + ys) * ys)
+    w = xi0.cpu().numpy().astype(np.int64) + 1
+    assert np.array_equal(got[8].numpy(), w.astype(np.int32))
+    assert int(got[7].item()) == ((int(w.sum()) + 2**31) % 2**32) - 2**31
