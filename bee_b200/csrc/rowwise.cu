@@ -364,6 +364,13 @@ __global__ void __launch_bounds__(THREADS, 512 / THREADS) norm_rope_pipe_kernel(
     const uint32_t hd = static_cast<uint32_t>(rope.head_dim);
     const uint32_t half = hd / 2;
     const uint32_t tid = threadIdx.x;
+    // angle per position of each frequency: kernel arguments only, so it is
+    // computed before the wait for the previous kernel on the stream
+    if (ROPE)
+        for (uint32_t i = tid; i < half; i += THREADS)
+            turns_per_pos[i] = exp(-(2.0 * static_cast<double>(i) / static_cast<double>(hd)) * rope.log_theta) *
+                               0.15915494309189533577;  // 1 / (2 pi)
+    pdl_wait();
 
     // Per-unit constants: chunk indices, table offset, weights.
     uint32_t cidx[NP][CPU];
@@ -390,10 +397,6 @@ __global__ void __launch_bounds__(THREADS, 512 / THREADS) norm_rope_pipe_kernel(
             CK::unpack((NORM && live[u]) ? reinterpret_cast<const uint4*>(w)[cidx[u][q]] : make_uint4(0, 0, 0, 0), wv[u][q]);
         }
     }
-    if (ROPE)
-        for (uint32_t i = tid; i < half; i += THREADS)
-            turns_per_pos[i] = exp(-(2.0 * static_cast<double>(i) / static_cast<double>(hd)) * rope.log_theta) *
-                               0.15915494309189533577;  // 1 / (2 pi)
     if (ROPE) __syncthreads();  // turns_per_pos is read by other threads below
 
     // Row order.  RMSNorm alone: CTA b takes rows b, b + G, ... .  With RoPE the
@@ -435,6 +438,7 @@ __global__ void __launch_bounds__(THREADS, 512 / THREADS) norm_rope_pipe_kernel(
     size_t cur_pos = ~size_t(0);
     int red_parity = 0;
     for (size_t i = i_begin; i < i_end; i += i_step, slot = slot + 1 == S ? 0 : slot + 1) {
+        if (i + i_step >= i_end) pdl_trigger();  // this CTA's last row
         issue();
         cp_async_wait<S - 1>();  // this thread's copies of this row have landed
         const size_t r = row_of(i);
@@ -582,7 +586,7 @@ static int launch_pipe(const T* px, const T* pw, T* py, size_t rows, size_t cols
     int per_sm = static_cast<int>((220 * 1024) / (smem + 1024 + 1024));
     const int by_threads = 2048 / THREADS;
     per_sm = per_sm < 1 ? 1 : (per_sm > by_threads ? by_threads : per_sm);
-    k<<<row_grid(rows, per_sm), THREADS, smem, st>>>(px, pw, py, rows, static_cast<uint32_t>(cols), eps, rope);
+    launch_pdl(k, row_grid(rows, per_sm), THREADS, smem, st, px, pw, py, rows, static_cast<uint32_t>(cols), eps, rope);
     return launch_status(NORM ? (ROPE ? "rms_norm_rope" : "rms_norm_rows") : "rope");
 }
 

@@ -1,5 +1,6 @@
 """Dependent ops back to back on one stream.  The streaming kernels (binary,
-fp32->bf16 cast, row and global reduce, row softmax) are launched so that the
+fp32->bf16 cast, row and global reduce, row softmax, the pipelined RMSNorm /
+RoPE) are launched so that the
 next one may start while the previous one finishes, and each waits for its
 predecessor before touching memory.  A chain in which every op reads the
 previous op's output, and the next round overwrites buffers the previous
@@ -14,10 +15,12 @@ ADD, SUB, MUL, DIV = 0, 1, 2, 3
 SUM, MAX = 0, 2
 
 
-def _chain(torch, capi, x, y, xi, bufs, rounds, sync):
+def _chain(torch, capi, x, y, xi, bufs, rounds, sync, rope):
     """Per round: a = x + y; b = a * y; c = b - a (reads both); h = bf16(c);
-    r = rowsum(c); m = rowmax(b); s = softmax(c); w = xi + 1; t = int32 sum of w."""
-    a, b, c, h, r, m, s, t, one, w = bufs
+    r = rowsum(c); m = rowmax(b); s = softmax(c); z = rms_norm_rope(s, g);
+    w = xi + 1; t = int32 sum of w."""
+    a, b, c, h, r, m, s, t, one, w, g, z = bufs
+    seq, heads, hd = rope
     st = torch.cuda.current_stream().cuda_stream
     rows, cols = x.shape
     n = x.numel()
@@ -35,14 +38,18 @@ def _chain(torch, capi, x, y, xi, bufs, rounds, sync):
         op("bee_b200_reduce_axis", SUM, capi.F32, c.data_ptr(), r.data_ptr(), rows, cols, 1, st)
         op("bee_b200_reduce_axis", MAX, capi.F32, b.data_ptr(), m.data_ptr(), rows, cols, 1, st)
         op("bee_b200_softmax_rows", capi.F32, c.data_ptr(), s.data_ptr(), rows, cols, st)
+        op("bee_b200_rms_norm_rope", capi.F32, s.data_ptr(), g.data_ptr(), z.data_ptr(), rows, seq, heads, hd, 1e-6,
+           10000.0, 0, st)
         op("bee_b200_ew_binary", ADD, capi.I32, xi.data_ptr(), one.data_ptr(), w.data_ptr(), n, st)
         op("bee_b200_reduce_global", SUM, capi.I32, w.data_ptr(), t.data_ptr(), n, st)
     torch.cuda.synchronize()
-    return [v.cpu().clone() for v in (a, b, c, h, r, m, s, t, w)]
+    return [v.cpu().clone() for v in (a, b, c, h, r, m, s, t, w, z)]
 
 
-@pytest.mark.parametrize("rows,cols", [(4096, 4096), (333, 8200)])
-def test_dependent_chain_matches_synchronised_chain(cuda, rows, cols):
+# RMSNorm+RoPE: 4096 = 32 heads x 128 (the pipelined kernel), 8200 = 41 heads x 200
+# (an fp32 row above the pipe's 16 KiB: the plain kernel, launched without overlap)
+@pytest.mark.parametrize("rows,cols,rope", [(4096, 4096, (64, 32, 128)), (333, 8200, (37, 41, 200))])
+def test_dependent_chain_matches_synchronised_chain(cuda, rows, cols, rope):
     torch = cuda
     from bee_b200 import _capi
     g = torch.Generator(device="cuda").manual_seed(rows + cols)
@@ -50,16 +57,17 @@ def test_dependent_chain_matches_synchronised_chain(cuda, rows, cols):
     y = torch.randn(rows, cols, device="cuda", generator=g)
     xi0 = torch.randint(-1000, 1001, (rows, cols), device="cuda", dtype=torch.int32, generator=g)
     one = torch.ones(rows, cols, device="cuda", dtype=torch.int32)
+    gain = 1.0 + 0.02 * torch.randn(cols, device="cuda", generator=g)
 
     def fresh():
         return (torch.empty_like(x), torch.empty_like(x), torch.empty_like(x),
                 torch.empty(rows, cols, device="cuda", dtype=torch.bfloat16), torch.empty(rows, device="cuda"),
                 torch.empty(rows, device="cuda"), torch.empty_like(x), torch.zeros(1, device="cuda", dtype=torch.int32),
-                one, torch.empty_like(xi0))
+                one, torch.empty_like(xi0), gain, torch.empty_like(x))
 
-    got = _chain(torch, _capi, x, y, xi0, fresh(), 20, sync=False)
-    want = _chain(torch, _capi, x, y, xi0, fresh(), 20, sync=True)
-    names = ["add", "mul", "sub", "cast", "row sum", "row max", "softmax", "int32 sum", "int32 add"]
+    got = _chain(torch, _capi, x, y, xi0, fresh(), 20, sync=False, rope=rope)
+    want = _chain(torch, _capi, x, y, xi0, fresh(), 20, sync=True, rope=rope)
+    names = ["add", "mul", "sub", "cast", "row sum", "row max", "softmax", "int32 sum", "int32 add", "rms_norm_rope"]
     for nm, g_, w_ in zip(names, got, want):
         assert torch.equal(g_, w_), f"{nm}: the back-to-back chain differs from the synchronised one"
     # and what the chain computes is right where it is exact
