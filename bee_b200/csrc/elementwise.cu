@@ -174,8 +174,10 @@ __global__ void __launch_bounds__(kThreads) binary_strided_kernel(const S* __res
                                                                   int b_vec, int o_vec) {
     constexpr int E = 16 / sizeof(S);
     const long long per_row = (L + E - 1) / E;
+    pdl_wait();
     if constexpr (ROW_MODE) {
         for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
+            if (row + gridDim.x >= rows) pdl_trigger();  // this CTA's last row
             long long r = row, oa = 0, ob = 0;
             for (int k = d.nd - 1; k >= 0; --k) {
                 const long long x = r % d.shape[k];
@@ -398,13 +400,13 @@ static void launch_binary_strided(const void* a, const void* b, void* out, const
     const long long per_row = (L + E - 1) / E;
     if (per_row >= 256) {
         const long long cap = static_cast<long long>(sm_count()) * 8;
-        binary_strided_kernel<S, OP, true><<<static_cast<unsigned>(rows < cap ? rows : cap), kThreads, 0, st>>>(
-            static_cast<const S*>(a), static_cast<const S*>(b), static_cast<S*>(out), rows, L, d, ia, ib,
-            a_vec ? 1 : 0, b_vec ? 1 : 0, o_vec);
+        launch_pdl(binary_strided_kernel<S, OP, true>, static_cast<unsigned>(rows < cap ? rows : cap), kThreads, 0, st,
+                   static_cast<const S*>(a), static_cast<const S*>(b), static_cast<S*>(out), rows, L, d, ia, ib,
+                   a_vec ? 1 : 0, b_vec ? 1 : 0, o_vec);
     } else {
-        binary_strided_kernel<S, OP, false><<<grid_for(static_cast<size_t>(rows * per_row)), kThreads, 0, st>>>(
-            static_cast<const S*>(a), static_cast<const S*>(b), static_cast<S*>(out), rows, L, d, ia, ib,
-            a_vec ? 1 : 0, b_vec ? 1 : 0, o_vec);
+        launch_pdl(binary_strided_kernel<S, OP, false>, grid_for(static_cast<size_t>(rows * per_row)), kThreads, 0, st,
+                   static_cast<const S*>(a), static_cast<const S*>(b), static_cast<S*>(out), rows, L, d, ia, ib,
+                   a_vec ? 1 : 0, b_vec ? 1 : 0, o_vec);
     }
 }
 

@@ -82,8 +82,10 @@ __global__ void __launch_bounds__(256) transpose_tile_kernel(const uint8_t* __re
         }
     };
     uint4 w[ITERS];
+    pdl_wait();  // nothing global is touched before the previous kernel on the stream has completed
     if (static_cast<long long>(blockIdx.x) < tiles) load(blockIdx.x, w);
     for (long long t = blockIdx.x; t < tiles; t += gridDim.x) {
+        if (t + gridDim.x >= tiles) pdl_trigger();  // this CTA's last tile
         const long long b = t / (tp * tq);
         const long long rem = t - b * tp * tq;
         const long long q0 = (rem / tp) * TQ, p0 = (rem % tp) * TP;
@@ -163,8 +165,10 @@ __global__ void __launch_bounds__(256) transpose_b16_pairs_kernel(const uint16_t
         }
     };
     uint4 w[2][2];
+    pdl_wait();  // nothing global is touched before the previous kernel on the stream has completed
     if (static_cast<long long>(blockIdx.x) < tiles) load(blockIdx.x, w);
     for (long long t = blockIdx.x; t < tiles; t += gridDim.x) {
+        if (t + gridDim.x >= tiles) pdl_trigger();  // this CTA's last tile
         const long long b = t / (tp * tq), rem = t - b * tp * tq;
         const long long q0 = (rem / tp) * TQ, p0 = (rem % tp) * TP;
 #pragma unroll
@@ -303,13 +307,13 @@ int launch_transpose(const void* src, void* dst, long long batch, long long P, l
     const long long tiles = batch * ((P + Sh::TP - 1) / Sh::TP) * ((Q + Sh::TQ - 1) / Sh::TQ);
     if constexpr (ES == 2) {
         if (src_vec && dst_vec && P % Sh::TP == 0 && Q % Sh::TQ == 0) {
-            transpose_b16_pairs_kernel<<<persistent_grid(tiles, 8), 256, 0, st>>>(
-                static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), batch, P, Q, ld, sb);
+            launch_pdl(transpose_b16_pairs_kernel, persistent_grid(tiles, 8), 256, 0, st, static_cast<const uint16_t*>(src),
+                       static_cast<uint16_t*>(dst), batch, P, Q, ld, sb);
             return launch_status("transpose");
         }
     }
-    transpose_tile_kernel<ES><<<persistent_grid(tiles, 8), 256, 0, st>>>(
-        static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), batch, P, Q, ld, sb, src_vec, dst_vec);
+    launch_pdl(transpose_tile_kernel<ES>, persistent_grid(tiles, 8), 256, 0, st, static_cast<const uint8_t*>(src),
+               static_cast<uint8_t*>(dst), batch, P, Q, ld, sb, src_vec, dst_vec);
     return launch_status("transpose");
 }
 

@@ -1,11 +1,13 @@
 """Dependent ops back to back on one stream.  The streaming kernels (binary,
 fp32->bf16 cast, row and global reduce, row softmax, the pipelined RMSNorm /
-RoPE) are launched so that the
+RoPE, the transposes, the broadcasting binary op) are launched so that the
 next one may start while the previous one finishes, and each waits for its
 predecessor before touching memory.  A chain in which every op reads the
 previous op's output, and the next round overwrites buffers the previous
 round read, must give bit for bit what the same chain gives with a device
 synchronise after every op."""
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -18,9 +20,12 @@ SUM, MAX = 0, 2
 def _chain(torch, capi, x, y, xi, bufs, rounds, sync, rope):
     """Per round: a = x + y; b = a * y; c = b - a (reads both); h = bf16(c);
     r = rowsum(c); m = rowmax(b); s = softmax(c); z = rms_norm_rope(s, g);
+    ht = transpose(h) (bf16); u = b - m (m broadcast along each row);
     w = xi + 1; t = int32 sum of w."""
-    a, b, c, h, r, m, s, t, one, w, g, z = bufs
+    a, b, c, h, r, m, s, t, one, w, g, z, ht, u = bufs
     seq, heads, hd = rope
+    I64 = ctypes.c_int64 * 2
+    shape, full, bcast = I64(*x.shape), I64(x.shape[1], 1), I64(1, 0)
     st = torch.cuda.current_stream().cuda_stream
     rows, cols = x.shape
     n = x.numel()
@@ -40,10 +45,13 @@ def _chain(torch, capi, x, y, xi, bufs, rounds, sync, rope):
         op("bee_b200_softmax_rows", capi.F32, c.data_ptr(), s.data_ptr(), rows, cols, st)
         op("bee_b200_rms_norm_rope", capi.F32, s.data_ptr(), g.data_ptr(), z.data_ptr(), rows, seq, heads, hd, 1e-6,
            10000.0, 0, st)
+        op("bee_b200_transpose_2d", capi.BF16, h.data_ptr(), ht.data_ptr(), rows, cols, st)
+        op("bee_b200_ew_binary_strided", SUB, capi.F32, 2, shape, b.data_ptr(), full, m.data_ptr(), bcast,
+           u.data_ptr(), st)
         op("bee_b200_ew_binary", ADD, capi.I32, xi.data_ptr(), one.data_ptr(), w.data_ptr(), n, st)
         op("bee_b200_reduce_global", SUM, capi.I32, w.data_ptr(), t.data_ptr(), n, st)
     torch.cuda.synchronize()
-    return [v.cpu().clone() for v in (a, b, c, h, r, m, s, t, w, z)]
+    return [v.cpu().clone() for v in (a, b, c, h, r, m, s, t, w, z, ht, u)]
 
 
 # RMSNorm+RoPE: 4096 = 32 heads x 128 (the pipelined kernel), 8200 = 41 heads x 200
@@ -63,16 +71,19 @@ def test_dependent_chain_matches_synchronised_chain(cuda, rows, cols, rope):
         return (torch.empty_like(x), torch.empty_like(x), torch.empty_like(x),
                 torch.empty(rows, cols, device="cuda", dtype=torch.bfloat16), torch.empty(rows, device="cuda"),
                 torch.empty(rows, device="cuda"), torch.empty_like(x), torch.zeros(1, device="cuda", dtype=torch.int32),
-                one, torch.empty_like(xi0), gain, torch.empty_like(x))
+                one, torch.empty_like(xi0), gain, torch.empty_like(x),
+                torch.empty(cols, rows, device="cuda", dtype=torch.bfloat16), torch.empty_like(x))
 
     got = _chain(torch, _capi, x, y, xi0, fresh(), 20, sync=False, rope=rope)
     want = _chain(torch, _capi, x, y, xi0, fresh(), 20, sync=True, rope=rope)
-    names = ["add", "mul", "sub", "cast", "row sum", "row max", "softmax", "int32 sum", "int32 add", "rms_norm_rope"]
+    names = ["add", "mul", "sub", "cast", "row sum", "row max", "softmax", "int32 sum", "int32 add", "rms_norm_rope",
+             "transpose", "b - rowmax"]
     for nm, g_, w_ in zip(names, got, want):
         assert torch.equal(g_, w_), f"{nm}: the back-to-back chain differs from the synchronised one"
     # and what the chain computes is right where it is exact
     xs, ys = x.cpu(), y.cpu()
     assert torch.equal(got[0], xs + ys) and torch.equal(got[1], (xs + ys) * ys)
+    assert torch.equal(got[10], got[3].t()) and torch.equal(got[11], got[1] - got[5][:, None])
     w = xi0.cpu().numpy().astype(np.int64) + 1
     assert np.array_equal(got[8].numpy(), w.astype(np.int32))
     assert int(got[7].item()) == ((int(w.sum()) + 2**31) % 2**32) - 2**31
