@@ -330,7 +330,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
         fence_mbar_init();
         // thread 0 is also the TMA thread: Q_A, Q_B and K_0 (into the K slot of
         // stage 1) start loading on q_full now, under the TMEM allocation and the
-        // first block barrier
+        // first block barrier, once the previous kernel on the stream has completed
+        // (the launch may overlap its tail)
+        pdl_wait();
         mbar_arrive_expect_tx(&q_full, static_cast<uint32_t>((ntiles + (nkv > 0 ? 1 : 0)) * kTile));
         for (int t = 0; t < ntiles; ++t) {
             tma_load_3d(sQ + t * kTile, &tmQ, &q_full, 0, q0 + t * kBlock, head);
@@ -348,6 +350,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_fwd_kernel(const __grid
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base_sh;
+    pdl_wait();     // every thread, before its first global access (O)
+    pdl_trigger();  // the next kernel may launch once every CTA, second wave included, has started
 
     if (warp < 4) {
         // warpgroup 0 needs few registers: hand them to the softmax warpgroups
@@ -1076,8 +1080,8 @@ extern "C" int bee_b200_attention(int dt, const void* q, const void* k, const vo
     if (part)
         attention_shares_kernel<<<static_cast<unsigned>(ctas), kThreads, kSmem, st>>>(tq, tk, tv, to, p);
     else
-        attention_fwd_kernel<<<dim3(static_cast<unsigned>(npairs), static_cast<unsigned>(heads)), kThreads, kSmem, st>>>(
-            tq, tk, tv, to, p);
+        launch_pdl(attention_fwd_kernel, dim3(static_cast<unsigned>(npairs), static_cast<unsigned>(heads)), kThreads, kSmem,
+                   st, tq, tk, tv, to, p);
     int rc = launch_status("attention");
     if (part) {
         cudaError_t e = cudaFreeAsync(part, st);

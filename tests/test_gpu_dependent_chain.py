@@ -87,3 +87,37 @@ def test_dependent_chain_matches_synchronised_chain(cuda, rows, cols, rope):
     w = xi0.cpu().numpy().astype(np.int64) + 1
     assert np.array_equal(got[8].numpy(), w.astype(np.int32))
     assert int(got[7].item()) == ((int(w.sum()) + 2**31) % 2**32) - 2**31
+
+
+def test_attention_between_dependent_ops(cuda):
+    """The fused attention also starts launching while the previous kernel on
+    the stream finishes.  Here it reads an add's output and an add reads its
+    output, back to back for five rounds (a bf16 add of zero copies exactly);
+    the result must equal the chain synchronised after every op bit for bit."""
+    torch = cuda
+    from bee_b200 import _capi
+    heads, seq = 6, 1024
+    g = torch.Generator(device="cuda").manual_seed(11)
+    q, k, v = (torch.randn(heads, seq, 128, device="cuda", generator=g).to(torch.bfloat16) for _ in range(3))
+    zero = torch.zeros_like(q)
+    n = q.numel()
+    st = torch.cuda.current_stream().cuda_stream
+
+    def run(sync):
+        qq, o, o2 = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
+        for r in range(5):
+            src = q if r == 0 else o2
+            _capi.call("bee_b200_ew_binary", ADD, _capi.BF16, src.data_ptr(), zero.data_ptr(), qq.data_ptr(), n, st)
+            if sync:
+                torch.cuda.synchronize()
+            _capi.call("bee_b200_attention", _capi.BF16, qq.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), heads,
+                       seq, 128, 0.088, st)
+            if sync:
+                torch.cuda.synchronize()
+            _capi.call("bee_b200_ew_binary", ADD, _capi.BF16, o.data_ptr(), zero.data_ptr(), o2.data_ptr(), n, st)
+            if sync:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        return o2.cpu()
+
+    assert torch.equal(run(False), run(True)), "attention in a back-to-back chain differs from the synchronised chain"
