@@ -182,6 +182,9 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tcgen05_kernel(const __grid_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = tmem_base_sh;
+    // the launch may overlap the previous kernel's tail: no global access before it has completed
+    pdl_wait();
+    pdl_trigger();
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
@@ -759,7 +762,7 @@ static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPar
     static SmemLimit smem_limit;
     if (int rc = smem_limit.ensure(kern, Cfg::SMEM, "bmm")) return rc;
     const int grid = p.total_tiles < sm_count() ? p.total_tiles : sm_count();
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(ta, tb, p);
+    launch_pdl(kern, grid, Cfg::THREADS, Cfg::SMEM, st, ta, tb, p);
     return launch_status("bmm(tcgen05)");
 }
 
@@ -906,6 +909,7 @@ __global__ void __launch_bounds__(256) split3_bf16_kernel(const SplitOperand opA
                                                          size_t M, int* __restrict__ flags) {
     const size_t groups_a = opA.rows * (opA.cols / 8);
     const size_t groups = groups_a + opB.rows * (opB.cols / 8);
+    pdl_wait();
     for (size_t gi0 = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; gi0 < groups;
          gi0 += static_cast<size_t>(gridDim.x) * blockDim.x) {
         const bool is_a = gi0 < groups_a;
@@ -977,6 +981,7 @@ __global__ void __launch_bounds__(256) sum_partials_kernel(const float* __restri
                                                           const float* __restrict__ A, const float* __restrict__ B,
                                                           size_t M, size_t K, size_t N, const int* __restrict__ flags) {
     const size_t n = M * N;
+    pdl_wait();
     const bool any_bad = flags[0] != 0;
     for (size_t i = (blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x) * 4; i < n;
          i += static_cast<size_t>(gridDim.x) * blockDim.x * 4) {
@@ -1004,6 +1009,7 @@ __global__ void __launch_bounds__(256) sum_partials_kernel(const float* __restri
 __global__ void __launch_bounds__(256) split_fixup_kernel(const float* __restrict__ A, const float* __restrict__ B,
                                                          float* __restrict__ C, size_t M, size_t K, size_t N,
                                                          const int* __restrict__ flags) {
+    pdl_wait();
     if (flags[0] == 0) return;
     for (size_t r = blockIdx.x; r < M; r += gridDim.x) {
         const bool row_bad = flags[1 + r] != 0;
@@ -1075,7 +1081,7 @@ static int matmul_f32_split(const float* A, const float* B, float* C, size_t M, 
     };
     if (rc == 0) {
         const SplitOperand opA{A, M, K, a3}, opB{B, K, N, b3};
-        split3_bf16_kernel<<<grid_for(M * (K / 8) + K * (N / 8)), 256, 0, st>>>(opA, opB, g, M, flags);
+        launch_pdl(split3_bf16_kernel, grid_for(M * (K / 8) + K * (N / 8)), 256, 0, st, opA, opB, g, M, flags);
         rc = launch_status("matmul(f32 split)");
     }
     if (rc == 0) {
@@ -1087,7 +1093,7 @@ static int matmul_f32_split(const float* A, const float* B, float* C, size_t M, 
         if (rc == -1) rc = fail(cudaErrorNotSupported, "matmul(f32 split): tensor-core path rejected the split operands");
     }
     if (rc == 0 && S > 1) {
-        sum_partials_kernel<<<grid_for(M * N / 4), 256, 0, st>>>(part, C, S, A, B, M, K, N, flags);
+        launch_pdl(sum_partials_kernel, grid_for(M * N / 4), 256, 0, st, part, C, S, A, B, M, K, N, flags);
         rc = launch_status("matmul(f32 split sum)");
     }
     if (rc == 0 && S == 1) {
@@ -1108,6 +1114,7 @@ using namespace bee_b200;
 // does not depend on timing), times alpha, rounded to the output type (n % 4 == 0).
 __global__ void __launch_bounds__(256) sum_ksplit_kernel(const float* __restrict__ part, void* __restrict__ C, int S,
                                                          size_t n, float alpha, int out_dt) {
+    pdl_wait();
     for (size_t i = (blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x) * 4; i < n;
          i += static_cast<size_t>(gridDim.x) * blockDim.x * 4) {
         float4 acc = *reinterpret_cast<const float4*>(part + i);
@@ -1163,8 +1170,8 @@ static int bmm_ksplit(int dt_in, int dt_out, const void* A, const void* B, void*
     int rc = bmm_bf16_tc(DT_F32, A, B, part, S, M, Kc, N, b_trans, 1.0f, ps, st, true, dt_in);
     if (rc == 0) {
         const size_t work = (M * N / 4 + 255) / 256, cap = sms * 8;
-        sum_ksplit_kernel<<<static_cast<unsigned>(work < cap ? work : cap), 256, 0, st>>>(part, C, static_cast<int>(S), M * N,
-                                                                                       alpha, dt_out);
+        launch_pdl(sum_ksplit_kernel, static_cast<unsigned>(work < cap ? work : cap), 256, 0, st, part, C,
+                   static_cast<int>(S), M * N, alpha, dt_out);
         rc = launch_status("bmm (K split sum)");
     }
     cudaError_t e2 = cudaFreeAsync(mem, st);

@@ -121,3 +121,43 @@ def test_attention_between_dependent_ops(cuda):
         return o2.cpu()
 
     assert torch.equal(run(False), run(True)), "attention in a back-to-back chain differs from the synchronised chain"
+
+
+def test_products_between_dependent_ops(cuda):
+    """The single-CTA tensor-core GEMM and the kernels around it (fp32 matmul:
+    split into bf16 pieces, products, partial sum; a 16-bit product with a
+    small output and a long K: products of K chunks, then their sum) also
+    launch early.  C1 = A . B (fp32), D = C1 + C1, C2 = D . B, and a bf16
+    128 x 4096 x 4096 product of a cast of C2's rows, back to back for three
+    rounds, must equal the chain synchronised after every op bit for bit."""
+    torch = cuda
+    from bee_b200 import _capi
+    g = torch.Generator(device="cuda").manual_seed(21)
+    n = 1024
+    A = torch.rand(n, n, device="cuda", generator=g) * 2 - 1
+    B = torch.rand(n, n, device="cuda", generator=g) * 2 - 1
+    W = (torch.randn(4096, 4096, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    st = torch.cuda.current_stream().cuda_stream
+
+    def run(sync):
+        C1, D, C2 = (torch.empty(n, n, device="cuda") for _ in range(3))
+        X = torch.empty(128, 4096, device="cuda", dtype=torch.bfloat16)
+        Y = torch.empty(128, 4096, device="cuda", dtype=torch.bfloat16)
+
+        def op(name, *args):
+            _capi.call(name, *args)
+            if sync:
+                torch.cuda.synchronize()
+
+        for _ in range(3):
+            op("bee_b200_matmul", _capi.F32, A.data_ptr(), B.data_ptr(), C1.data_ptr(), n, n, n, st)
+            op("bee_b200_ew_binary", ADD, _capi.F32, C1.data_ptr(), C1.data_ptr(), D.data_ptr(), n * n, st)
+            op("bee_b200_matmul", _capi.F32, D.data_ptr(), B.data_ptr(), C2.data_ptr(), n, n, n, st)
+            op("bee_b200_ew_cast", _capi.F32, C2.data_ptr(), _capi.BF16, X.data_ptr(), 128 * 4096, st)
+            op("bee_b200_bmm", _capi.BF16, _capi.BF16, X.data_ptr(), W.data_ptr(), Y.data_ptr(), 1, 128, 4096, 4096, 0,
+               1.0, st)
+        torch.cuda.synchronize()
+        return C1.cpu(), C2.cpu(), Y.cpu()
+
+    for nm, a_, b_ in zip(["C1", "C2", "Y"], run(False), run(True)):
+        assert torch.equal(a_, b_), f"{nm}: the back-to-back chain differs from the synchronised one"
