@@ -10,7 +10,12 @@
  * bee_b200_last_error() on the calling thread.  All compute calls are
  * asynchronous on the given stream; a caller that wants the reference's
  * synchronous semantics synchronises the stream afterwards (the C++ bridge in
- * bee_b200/host does exactly that).
+ * bee_b200/host does exactly that).  Most kernels launch with programmatic
+ * stream serialisation: they may start while the previous kernel on the stream
+ * finishes but touch no memory until it has completed, and they let the next
+ * such launch start early; a caller's own kernel launched with that attribute
+ * right after one of them must wait (griddepcontrol.wait) before reading its
+ * outputs.  Ordinary launches, copies and events see plain stream order.
  *
  * Integer codes are the reference's:
  *   dtype   = bee::DType            (Bee/Tensor/Core/DType.hpp:17-32)
