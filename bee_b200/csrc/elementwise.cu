@@ -112,6 +112,7 @@ __global__ void __launch_bounds__(kThreads) binary_kernel(const S* __restrict__ 
 template <typename S, int OP>
 __global__ void __launch_bounds__(kThreads) binary_scalar_kernel(const S* __restrict__ a, const S* __restrict__ b,
                                                                  S* __restrict__ out, size_t n) {
+    pdl_wait();
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
         out[i] = from_c<S>(bin<OP>(to_c(a[i]), to_c(b[i])));
@@ -235,6 +236,7 @@ __global__ void __launch_bounds__(kThreads) binary_strided_kernel(const S* __res
 template <typename S, int OP>
 __global__ void __launch_bounds__(kThreads) unary_kernel(const S* __restrict__ a, S* __restrict__ out, size_t n,
                                                          int vectorised) {
+    pdl_wait();
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (!vectorised) {
@@ -303,6 +305,7 @@ __global__ void __launch_bounds__(kThreads) cast_f32_bf16_kernel(const float* __
 // bf16 -> fp32 (exact): 16 bytes in, 32 bytes out per vector step.
 __global__ void __launch_bounds__(kThreads) cast_bf16_f32_kernel(const uint16_t* __restrict__ src,
                                                                   float* __restrict__ dst, size_t n) {
+    pdl_wait();
     const size_t nvec = n / 8;
     const uint4* vs = reinterpret_cast<const uint4*>(src);
     float4* vd = reinterpret_cast<float4*>(dst);
@@ -320,6 +323,7 @@ __global__ void __launch_bounds__(kThreads) cast_bf16_f32_kernel(const uint16_t*
 // Generic element-by-element cast (static_cast semantics, ->Bool is x != 0).
 template <typename Si, typename So>
 __global__ void __launch_bounds__(kThreads) cast_kernel(const Si* __restrict__ src, So* __restrict__ dst, size_t n) {
+    pdl_wait();
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
         auto c = to_c(src[i]);
@@ -334,6 +338,7 @@ __global__ void __launch_bounds__(kThreads) cast_kernel(const Si* __restrict__ s
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads) scale_kernel(T* __restrict__ buf, T factor, size_t n) {
+    pdl_wait();
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) buf[i] *= factor;
 }
@@ -357,7 +362,7 @@ static void launch_binary(const void* a, const void* b, void* out, size_t n, cud
         launch_pdl(binary_kernel<S, OP>, grid_for((n * sizeof(S) / 16 + kUnroll - 1) / kUnroll), kThreads, 0, st, pa, pb,
                    po, n);
     else
-        binary_scalar_kernel<S, OP><<<grid_for(n), kThreads, 0, st>>>(pa, pb, po, n);
+        launch_pdl(binary_scalar_kernel<S, OP>, grid_for(n), kThreads, 0, st, pa, pb, po, n);
 }
 
 template <typename S>
@@ -427,7 +432,7 @@ template <typename S, int OP>
 static void launch_unary(const void* a, void* out, size_t n, cudaStream_t st) {
     int vec = aligned16(a) && aligned16(out);
     size_t work = vec ? (n * sizeof(S) / 16 + kUnroll - 1) / kUnroll : n;
-    unary_kernel<S, OP><<<grid_for(work), kThreads, 0, st>>>(static_cast<const S*>(a), static_cast<S*>(out), n, vec);
+    launch_pdl(unary_kernel<S, OP>, grid_for(work), kThreads, 0, st, static_cast<const S*>(a), static_cast<S*>(out), n, vec);
 }
 
 template <typename S>
@@ -455,14 +460,14 @@ static int cast_from(int dst_dt, const void* src, void* dst, size_t n, cudaStrea
     const Si* s = static_cast<const Si*>(src);
     unsigned g = grid_for(n);
     switch (dst_dt) {
-    case DT_BOOL: cast_kernel<Si, bool><<<g, kThreads, 0, st>>>(s, static_cast<bool*>(dst), n); break;
-    case DT_U8: cast_kernel<Si, uint8_t><<<g, kThreads, 0, st>>>(s, static_cast<uint8_t*>(dst), n); break;
-    case DT_I32: cast_kernel<Si, int32_t><<<g, kThreads, 0, st>>>(s, static_cast<int32_t*>(dst), n); break;
-    case DT_I64: cast_kernel<Si, int64_t><<<g, kThreads, 0, st>>>(s, static_cast<int64_t*>(dst), n); break;
-    case DT_F32: cast_kernel<Si, float><<<g, kThreads, 0, st>>>(s, static_cast<float*>(dst), n); break;
-    case DT_F64: cast_kernel<Si, double><<<g, kThreads, 0, st>>>(s, static_cast<double*>(dst), n); break;
-    case DT_BF16: cast_kernel<Si, bf16_t><<<g, kThreads, 0, st>>>(s, static_cast<bf16_t*>(dst), n); break;
-    case DT_F16: cast_kernel<Si, f16_t><<<g, kThreads, 0, st>>>(s, static_cast<f16_t*>(dst), n); break;
+    case DT_BOOL: launch_pdl(cast_kernel<Si, bool>, g, kThreads, 0, st, s, static_cast<bool*>(dst), n); break;
+    case DT_U8: launch_pdl(cast_kernel<Si, uint8_t>, g, kThreads, 0, st, s, static_cast<uint8_t*>(dst), n); break;
+    case DT_I32: launch_pdl(cast_kernel<Si, int32_t>, g, kThreads, 0, st, s, static_cast<int32_t*>(dst), n); break;
+    case DT_I64: launch_pdl(cast_kernel<Si, int64_t>, g, kThreads, 0, st, s, static_cast<int64_t*>(dst), n); break;
+    case DT_F32: launch_pdl(cast_kernel<Si, float>, g, kThreads, 0, st, s, static_cast<float*>(dst), n); break;
+    case DT_F64: launch_pdl(cast_kernel<Si, double>, g, kThreads, 0, st, s, static_cast<double*>(dst), n); break;
+    case DT_BF16: launch_pdl(cast_kernel<Si, bf16_t>, g, kThreads, 0, st, s, static_cast<bf16_t*>(dst), n); break;
+    case DT_F16: launch_pdl(cast_kernel<Si, f16_t>, g, kThreads, 0, st, s, static_cast<f16_t*>(dst), n); break;
     default: return fail(cudaErrorInvalidValue, "ew_cast: unsupported destination dtype %d", dst_dt);
     }
     return launch_status("ew_cast");
@@ -563,8 +568,8 @@ int bee_b200_ew_cast(int src_dt, const void* src, int dst_dt, void* dst, size_t 
         return launch_status("ew_cast");
     }
     if (src_dt == DT_BF16 && dst_dt == DT_F32 && aligned16(src) && aligned16(dst)) {
-        cast_bf16_f32_kernel<<<grid_for(n / 8), kThreads, 0, st>>>(static_cast<const uint16_t*>(src),
-                                                                    static_cast<float*>(dst), n);
+        launch_pdl(cast_bf16_f32_kernel, grid_for(n / 8), kThreads, 0, st, static_cast<const uint16_t*>(src),
+                   static_cast<float*>(dst), n);
         return launch_status("ew_cast");
     }
     switch (src_dt) {
@@ -584,8 +589,8 @@ int bee_b200_scale_fp(int dt, void* buf, double factor, size_t n, bee_b200_strea
     if (n == 0) return ok();
     if (!buf) return fail(cudaErrorInvalidValue, "scale_fp: null pointer");
     cudaStream_t st = as_stream(stream);
-    if (dt == DT_F32) scale_kernel<float><<<grid_for(n), kThreads, 0, st>>>(static_cast<float*>(buf), float(factor), n);
-    else if (dt == DT_F64) scale_kernel<double><<<grid_for(n), kThreads, 0, st>>>(static_cast<double*>(buf), factor, n);
+    if (dt == DT_F32) launch_pdl(scale_kernel<float>, grid_for(n), kThreads, 0, st, static_cast<float*>(buf), float(factor), n);
+    else if (dt == DT_F64) launch_pdl(scale_kernel<double>, grid_for(n), kThreads, 0, st, static_cast<double*>(buf), factor, n);
     else return fail(cudaErrorInvalidValue, "scale_fp: dtype %d is not F32/F64", dt);
     return launch_status("scale_fp");
 }

@@ -227,6 +227,7 @@ __device__ __forceinline__ long long row_offset(long long r, const ViewDims& v) 
 template <int ES, bool ROW_MODE>
 __global__ void __launch_bounds__(256) rows_copy_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
                                                         long long rows, long long L, ViewDims v, int vec_ok) {
+    pdl_wait();
     using T = typename Word<ES>::T;
     constexpr int VEC = 16 / ES;
     const T* s = reinterpret_cast<const T*>(src);
@@ -273,6 +274,7 @@ __global__ void __launch_bounds__(256) rows_copy_kernel(const uint8_t* __restric
 template <int ES>
 __global__ void __launch_bounds__(256) gather_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
                                                      long long n, long long L, long long inner_stride, ViewDims v) {
+    pdl_wait();
     using T = typename Word<ES>::T;
     const T* s = reinterpret_cast<const T*>(src);
     T* d = reinterpret_cast<T*>(dst);
@@ -333,11 +335,11 @@ int launch_rows(const void* src, void* dst, long long rows, long long L, const V
     for (int i = 0; i < v.nd; ++i) vec_ok = vec_ok && (v.stride[i] * ES) % 16 == 0;
     const long long per_row = (L + 16 / ES - 1) / (16 / ES);
     if (per_row >= 256) {  // rows of 4 KiB or more: a CTA per row
-        rows_copy_kernel<ES, true><<<persistent_grid(rows, 8), 256, 0, st>>>(
-            static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, L, v, vec_ok ? 1 : 0);
+        launch_pdl(rows_copy_kernel<ES, true>, persistent_grid(rows, 8), 256, 0, st, static_cast<const uint8_t*>(src),
+                   static_cast<uint8_t*>(dst), rows, L, v, vec_ok ? 1 : 0);
     } else {
-        rows_copy_kernel<ES, false><<<persistent_grid((rows * per_row + 255) / 256, 8), 256, 0, st>>>(
-            static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, L, v, vec_ok ? 1 : 0);
+        launch_pdl(rows_copy_kernel<ES, false>, persistent_grid((rows * per_row + 255) / 256, 8), 256, 0, st,
+                   static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, L, v, vec_ok ? 1 : 0);
     }
     return launch_status("strided_copy(rows)");
 }
@@ -345,8 +347,8 @@ int launch_rows(const void* src, void* dst, long long rows, long long L, const V
 template <int ES>
 int launch_gather(const void* src, void* dst, long long n, long long L, long long inner_stride, const ViewDims& v,
                   cudaStream_t st) {
-    gather_kernel<ES><<<persistent_grid((n + 255) / 256, 8), 256, 0, st>>>(
-        static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), n, L, inner_stride, v);
+    launch_pdl(gather_kernel<ES>, persistent_grid((n + 255) / 256, 8), 256, 0, st, static_cast<const uint8_t*>(src),
+               static_cast<uint8_t*>(dst), n, L, inner_stride, v);
     return launch_status("strided_copy(gather)");
 }
 
